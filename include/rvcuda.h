@@ -1,0 +1,137 @@
+/* rvcuda.h - C ABI of the B200 (sm_100a) MoE-layer backend, librvcuda.so.
+ *
+ * Drop-in for the expert path of Rosevine's HIP executor. It keeps the conventions of the
+ * reference ABI runtime/hip/rvhip.h:1-14: every function returns 0 or a CUDA error code
+ * (cudaError_t values; RVC_ERR_* below for backend-specific failures), rvc_error_string()
+ * returns a static string, no exception crosses the ABI, scalar arguments are validated
+ * here and buffer extents are the caller's contract (the host wrapper range-checks every
+ * view against its allocation, as runtime/src/hip.rs:258-263 does).
+ *
+ * Differences, all additive (the reference's ADR plans stream-taking entry points,
+ * docs/adr/0002-expert-residency-and-scheduling.md:353-358):
+ *  - compute entry points take a trailing `void *stream` (a cudaStream_t; NULL = the
+ *    legacy default stream, which orders work like the reference's null stream);
+ *  - compute entry points take a caller-allocated device workspace (rvc_alloc) sized by
+ *    rvc_moe_workspace_bytes(); nothing allocates during a call.
+ *
+ * Layouts:
+ *  - Q4_0 expert tensors as bound by runtime/src/model.rs:36-40 (GGUF): gate_up
+ *    [n_experts][2*ff rows][n_embd/32 blocks of 18 B] (gate rows then up rows), down
+ *    [n_experts][n_embd rows][ff/32 blocks]. rvc_pack_experts turns them into the packed
+ *    device planes every MoE entry point reads.
+ *  - Router weight [n_experts][n_embd] (ggml dims [n_embd, n_experts],
+ *    runtime/src/contract.rs:66), f32 (the reference model) or bf16 (the benchmark).
+ *  - Activations row-major [n_tok][n_embd], f32 or bf16; outputs f32.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of activations and router weights. */
+#define RVC_F32 0
+#define RVC_BF16 1
+
+/* Backend error codes (outside the cudaError_t range). */
+#define RVC_ERR_DEVICE_TIMEOUT 10001 /* a bounded device wait ran out (status word) */
+#define RVC_ERR_DEVICE_INDEX 10002   /* a device-side index check failed (status word) */
+#define RVC_ERR_UNSUPPORTED 10003    /* shape outside what the kernels support */
+#define RVC_ERR_WORKSPACE 10004      /* workspace too small for this call */
+
+/* ---------------------------------------------------------------- runtime
+ * 1:1 with runtime/hip/rvhip.h:22-38 (rvh_init ... rvh_event_elapsed). */
+int rvc_init(int device);                                    /* rvhip.h:22 */
+int rvc_mem_info(size_t *free_bytes, size_t *total_bytes);   /* rvhip.h:23 */
+int rvc_alloc(size_t bytes, void **out);                     /* rvhip.h:24 */
+int rvc_free(void *ptr);                                     /* rvhip.h:25 */
+int rvc_upload(void *dst, const void *src, size_t bytes);    /* rvhip.h:26 */
+int rvc_download(void *dst, const void *src, size_t bytes);  /* rvhip.h:27 */
+int rvc_copy(void *dst, const void *src, size_t bytes);      /* rvhip.h:28, device to device */
+int rvc_sync(void);                                          /* rvhip.h:29 */
+const char *rvc_error_string(int code);                      /* rvhip.h:30 */
+int rvc_event_create(void **out);                            /* rvhip.h:34 */
+int rvc_event_destroy(void *ev);                             /* rvhip.h:35 */
+int rvc_event_record(void *ev);                              /* rvhip.h:36 */
+int rvc_event_sync(void *ev);                                /* rvhip.h:37 */
+int rvc_event_elapsed(void *start, void *end, float *ms);    /* rvhip.h:38 */
+/* Stream-ordered variants (additive): async copies and events on `stream`. */
+int rvc_upload_async(void *dst, const void *src, size_t bytes, void *stream);
+int rvc_download_async(void *dst, const void *src, size_t bytes, void *stream);
+int rvc_event_record_on(void *ev, void *stream);
+int rvc_stream_sync(void *stream);
+
+/* ------------------------------------------------------------- MoE layer */
+
+/* Weights of one MoE layer, as runtime/src/model.rs:11-41 binds them (gate_inp,
+ * down_exps_scale, gate_up_exps, down_exps), with the experts already packed.
+ * Shapes of the target (runtime/src/contract.rs:12-22): n_embd 2816, ff 704,
+ * n_experts 128, used 8. Supported: n_embd % 256 == 0, ff % 32 == 0,
+ * n_experts <= 256, used <= 16. */
+typedef struct rvc_moe_weights {
+    int n_embd;
+    int ff;
+    int n_experts;
+    int used;
+    int router_dtype;         /* RVC_F32 or RVC_BF16 */
+    const void *router;       /* device [n_experts][n_embd] */
+    const void *packed;       /* device, from rvc_pack_experts */
+    const float *down_scale;  /* device [n_experts], or NULL for all ones */
+} rvc_moe_weights;
+
+/* Bytes of the packed expert planes (equal to the GGUF bytes of both tensors). */
+size_t rvc_packed_bytes(int n_experts, int n_embd, int ff);
+
+/* One-time repack at upload, replacing the raw uploads of runtime/src/hip_exec.rs:429-433.
+ * gate_up / down: device copies of the GGUF tensors. packed: rvc_packed_bytes() bytes. */
+int rvc_pack_experts(const void *gate_up_q4, const void *down_q4, int n_experts, int n_embd, int ff, void *packed,
+                     void *stream);
+
+/* Device workspace for calls of up to max_tok tokens. */
+size_t rvc_moe_workspace_bytes(int max_tok, int n_embd, int ff, int n_experts, int used);
+
+/* Router: logits = router . x (+ bias), softmax, top-`used`, renormalised weights, and the
+ * dispatch plan. Replaces rvh_rms_norm+rvh_f32_mm (hip_exec.rs:786-787, rvhip.h:43,50), the
+ * logits download (:789) and the host select_experts / MoePlan::new (runtime/src/exec.rs:
+ * 507-558). The caller applies the router-input norm, as the reference does before f32_mm.
+ * bias: optional f32 logit bias, bias[t*bias_stride + e] (stride 0 = one row for all tokens).
+ * Outputs (device, each may be NULL): ids/wts [n_tok][used] in slot order; hist
+ * [n_experts] pairs per expert; perm [n_tok*used] the pair order of MoePlan (pair = t*used+j);
+ * logits [n_tok][n_experts]. */
+int rvc_moe_router(const rvc_moe_weights *w, const void *x, int x_dtype, const float *bias, int bias_stride,
+                   int n_tok, int32_t *ids, float *wts, int32_t *hist, int32_t *perm, float *logits, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* Routed experts for given ids/weights: Q8_0 activations, gate/up with GELU-tanh, Q8_0 h,
+ * down, and the slot-order weighted combine into out [n_tok][n_embd] f32 (before
+ * post_ffw_norm_2). Replaces hip_exec.rs:820-843 (gather_rows, per-expert q4_mm,
+ * geglu_split, q4_mm, moe_combine; rvhip.h:44,71,77-80) and computes what experts_cpu
+ * (runtime/src/exec.rs:572-640) computes with Activation::Q8_0. */
+int rvc_moe_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids,
+                    const float *wts, int n_tok, float *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The whole MoE layer: rvc_moe_router on x_router, then rvc_moe_experts on x_expert (the
+ * reference's layer() MoE branch, hip_exec.rs:780-843, between its norms). ids/wts may be
+ * NULL. x_router and x_expert may be the same buffer. */
+int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
+                    const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
+                    void *workspace, size_t workspace_bytes, void *stream);
+
+/* Zero the workspace's status word (call once after allocating a workspace). */
+int rvc_workspace_reset(void *workspace, void *stream);
+
+/* Synchronise `stream`, then read and clear the workspace's device status word:
+ * returns 0, RVC_ERR_DEVICE_TIMEOUT or RVC_ERR_DEVICE_INDEX. */
+int rvc_status(void *workspace, void *stream);
+
+/* Test hook: the exact int32 Q4_0 x Q8_0 block sums the expert kernels form, for
+ * `n_rows` rows of one expert of the packed weights against Q8_0 activation rows.
+ * which: 0 = gate_up (original row numbering), 1 = down. xq8: device [n_in][nblk*34]
+ * (reference Q8_0 blocks). out: device int32 [n_in][n_rows][nblk]. */
+int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,
+                         const void *xq8, int n_in, int32_t *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif

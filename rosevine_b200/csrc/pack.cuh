@@ -1,0 +1,41 @@
+// pack.cuh - one-time repack of the reference's Q4_0 expert tensors into device planes.
+//
+// Input: the GGUF layout bound by runtime/src/model.rs:36-40 - per expert, gate_up is 2*ff rows
+// (gate rows 0..ff-1, then up rows) of n_embd/32 18-byte blocks; down is n_embd rows of ff/32
+// blocks. The HIP executor uploads these bytes unchanged (runtime/src/hip_exec.rs:429-433);
+// this backend splits each block into a 16-byte nibble plane and an f16 scale plane (so every
+// copy is 16-byte aligned for TMA and every row of nibbles is one contiguous run), and
+// interleaves gate and up rows per 32 columns:
+//   packed gate_up row R = q*64 + s*32 + i  holds  original row s*ff + q*32 + i.
+// Nibble bytes and scale bits are copied unchanged, so every dot product sees the same
+// integers and scales as the reference.
+#pragma once
+#include "common.cuh"
+
+namespace rvc {
+
+__global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int rows, int nblk, bool interleave_gu,
+                          int ff, uint8_t *__restrict__ nib, uint16_t *__restrict__ scl) {
+    const size_t total = (size_t)n_experts * rows * nblk;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t b = i % nblk;
+        const size_t row = (i / nblk) % rows;
+        const size_t e = i / ((size_t)nblk * rows);
+        size_t prow = row;
+        if (interleave_gu) {
+            const size_t s = row / ff, col = row % ff;
+            prow = (col / 32) * 64 + s * 32 + (col % 32);
+        }
+        const uint8_t *blk = src + i * Q4_BLOCK;
+        const size_t dst = (e * rows + prow) * nblk + b;
+        // 18-byte blocks are only 2-byte aligned: read as 9 halfwords
+        const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+        *reinterpret_cast<uint4 *>(nib + dst * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        scl[dst] = h[0];
+    }
+}
+
+}  // namespace rvc
