@@ -106,16 +106,26 @@ int ws_max_tok(size_t bytes, const rvc_moe_weights *w) {
 
 constexpr int DECODE_MAX_PAIRS = 512;  // k_down_combine_decode keeps [pairs][16] f32 in smem
 
-// Opt a kernel into the full 227 KB of dynamic shared memory, once per (kernel slot, device).
+// Opt a kernel into the dynamic shared memory it needs beyond the default 48 KB: the opt-in
+// limit is the device's per-block maximum minus the kernel's static shared memory. Done once
+// per (kernel slot, device); returns a CUDA error code.
 template <typename K>
-void set_smem_attr(K kernel, int slot) {
+int set_smem_attr(K kernel, int slot) {
     static bool done[16][64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !done[slot][dev]) {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (dev >= 0 && dev < 64) done[slot][dev] = true;
-    }
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev >= 0 && dev < 64 && done[slot][dev]) return 0;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return (int)e;
+    int optin = 0;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+    if (e != cudaSuccess) return (int)e;
+    if (dev >= 0 && dev < 64) done[slot][dev] = true;
+    return 0;
 }
 
 int launch_router_logits(const rvc_moe_weights *w, const void *x, int x_dtype, const float *bias, int bias_stride,
@@ -249,7 +259,7 @@ int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, con
     Q8View xv{at<int8_t>(ws, L.xq), at<float>(ws, L.xd), at<int32_t>(ws, L.xs)};
     {
         const size_t smem = (size_t)GU_UNIT_ROWS * nb * 18;
-        set_smem_attr(k_gate_up_decode, 0);
+        if ((rc = set_smem_attr(k_gate_up_decode, 0))) return rc;
         dim3 grid(w->ff / 32, std::min(w->n_experts, pairs));
         k_gate_up_decode<<<grid, 256, smem, st>>>(pk, w->n_embd, w->ff, xv, plan, w->used, at<int8_t>(ws, L.hq),
                                                   at<float>(ws, L.hd), at<int32_t>(ws, L.hs), status);
@@ -259,7 +269,7 @@ int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, con
         const int nbh = w->ff / QK;
         const size_t stage = ((size_t)DN_ROWS * nbh * 18 + 127) & ~size_t(127);
         const size_t smem = DN_STAGES * stage + (size_t)pairs * DN_ROWS * 4;
-        set_smem_attr(k_down_combine_decode, 1);
+        if ((rc = set_smem_attr(k_down_combine_decode, 1))) return rc;
         Q8View hv{at<int8_t>(ws, L.hq), at<float>(ws, L.hd), at<int32_t>(ws, L.hs)};
         k_down_combine_decode<<<w->n_embd / DN_ROWS, 256, smem, st>>>(pk, w->n_embd, w->ff, hv, plan, ids, wts,
                                                                       w->down_scale, n_tok, w->used, out, status);

@@ -44,7 +44,7 @@ class MoeLayer:
         else:
             raise TypeError("router weights must be bf16 bits (uint16) or float32")
         dev = self.device
-        self.router = torch.from_numpy(np.ascontiguousarray(w_router).view(np.uint8)).to(dev)
+        self.router_w = torch.from_numpy(np.ascontiguousarray(w_router).view(np.uint8)).to(dev)
         self.down_scale = None if down_scale is None else torch.from_numpy(
             np.ascontiguousarray(down_scale, dtype=np.float32)).to(dev)
         self.packed = torch.empty(rc.packed_bytes(self.n_experts, n_embd, ff), dtype=torch.uint8, device=dev)
@@ -56,7 +56,7 @@ class MoeLayer:
         self.ws = torch.empty(rc.workspace_bytes(max_tok, n_embd, ff, self.n_experts, used), dtype=torch.uint8,
                               device=dev)
         rc.workspace_reset(self.ws, _stream_handle(None))
-        self.w = rc.weights_struct(n_embd, ff, self.n_experts, used, self.router_dtype, self.router, self.packed,
+        self.w = rc.weights_struct(n_embd, ff, self.n_experts, used, self.router_dtype, self.router_w, self.packed,
                                    self.down_scale)
 
     @staticmethod
