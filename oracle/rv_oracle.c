@@ -110,12 +110,19 @@ void rvo_quantize_q8_0(const float *x, int k, uint8_t *out) {
     }
 }
 
+/* f32 exp and tanh as Rust's f32::exp / f32::tanh reach them: the platform libm. The checker
+ * takes the correctly rounded f32 result (the double-precision function rounded once), which
+ * is what glibc >= 2.41 returns for tanhf (CORE-MATH) and what glibc's expf returns except
+ * within its documented 0.502-ulp error, so parity does not depend on the host's glibc. */
+float rvo_expf(float x) { return (float)exp((double)x); }
+float rvo_tanhf(float x) { return (float)tanh((double)x); }
+
 /* tanh-approximation GELU, evaluated left to right as ops.rs:145-149. */
 float rvo_gelu(float x) {
     const float A = 0.044715f;
     const float S = 0.7978846f; /* 0.797_884_6 */
     float inner = (S * x) * (1.0f + (A * x) * x);
-    return (0.5f * x) * (1.0f + tanhf(inner));
+    return (0.5f * x) * (1.0f + rvo_tanhf(inner));
 }
 
 /* Softmax with f32 exp and an f64 sum, scaled by (1/sum) rounded to f32 (ops.rs:170-179). */
@@ -124,7 +131,7 @@ void rvo_softmax(float *x, int n) {
     for (int i = 0; i < n; ++i) mx = fmaxf(mx, x[i]); /* f32::max ignores NaN like fmaxf */
     double sum = 0.0;
     for (int i = 0; i < n; ++i) {
-        x[i] = expf(x[i] - mx);
+        x[i] = rvo_expf(x[i] - mx);
         sum += (double)x[i];
     }
     float inv = (float)(1.0 / sum);

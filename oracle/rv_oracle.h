@@ -8,8 +8,8 @@
  * Every function restates the reference algorithm it names (paths relative to
  * the Rosevine project root). Arithmetic order follows the reference so that
  * results are bit-identical to the Rust code on the same glibc: f32 operations
- * are never contracted (built with -ffp-contract=off), expf/tanhf are glibc's,
- * exactly as Rust's f32::exp / f32::tanh resolve on x86_64 Linux.
+ * are never contracted (built with -ffp-contract=off); f32 exp/tanh are the correctly
+ * rounded results of the libm functions Rust's f32::exp / f32::tanh call (rv_oracle.c).
  *
  * Parity pins: tests/test_oracle_golden.py checks this code against the
  * reference's own known-answer tests (ops.rs, expert_kernel.rs, exec.rs tests)
@@ -42,6 +42,9 @@ uint16_t rvo_f32_to_f16(float f);
 float rvo_bf16_to_f32(uint16_t b);
 /* ops.rs:95-105: x has k (multiple of 32) values; out gets k/32 * 34 bytes. */
 void rvo_quantize_q8_0(const float *x, int k, uint8_t *out);
+/* f32 exp / tanh, correctly rounded (see rv_oracle.c) */
+float rvo_expf(float x);
+float rvo_tanhf(float x);
 /* ops.rs:145-149 */
 float rvo_gelu(float x);
 /* ops.rs:170-179 (in place) */

@@ -5,7 +5,8 @@
 // what the CPU-experts Q8_0 path computes (runtime/src/exec.rs:572-640 with
 // Activation::Q8_0, runtime/src/expert_pool.rs:311-320 and
 // runtime/src/expert_kernel.rs:147-161):
-//   gate/up:  y = sum_b sumi_b * (dw_b * dx_b), sumi_b the exact int32 block dot;
+//   gate/up:  y = sum_b sumi_b * (dw_b * dx_b), sumi_b the exact int32 block dot, summed in
+//             block order with separately rounded f32 operations (the scalar reference order);
 //   h = gelu_tanh(gate) * up, re-quantised to Q8_0 per 32 columns;
 //   down:     the same block dot over h;
 //   combine:  out[t] = sum_j (y_j * down_scale[e_j]) * w_j in slot order (bit-exact order).
@@ -80,6 +81,10 @@ __global__ void __launch_bounds__(256) k_gate_up_decode(PackedView pk, int n_emb
     }
     if (!mbar_wait(&bar, 0, status)) return;
 
+    // Each row's dot follows the reference's scalar order exactly (expert_kernel.rs:147-161):
+    // acc = 0; for b in 0..nb: acc = acc + (float)sumi_b * (dw_b * dx_b), each operation
+    // rounded separately. The 8 lanes of a row group each form one block term per chunk of 8
+    // blocks; the terms are then added in block order through shuffles.
     const int grp = lane >> 3, l8 = lane & 7;
     for (int c0 = 0; c0 < n_e; c0 += GU_TOK) {
         const int nt = min(GU_TOK, n_e - c0);
@@ -92,32 +97,37 @@ __global__ void __launch_bounds__(256) k_gate_up_decode(PackedView pk, int n_emb
             float acc[GU_TOK];
 #pragma unroll
             for (int i = 0; i < GU_TOK; ++i) acc[i] = 0.0f;
-            for (int b = l8; b < nb; b += 8) {
+            for (int cb = 0; cb < nb; cb += 8) {
+                const int b = cb + l8;
                 const uint4 nib = *reinterpret_cast<const uint4 *>(snib + ((size_t)r * nb + b) * 16);
                 const float dw = f16_bits_to_f32(sscl[r * nb + b]);
+                float term[GU_TOK];
 #pragma unroll
                 for (int i = 0; i < GU_TOK; ++i) {
+                    term[i] = 0.0f;
                     if (i < nt) {
                         const size_t xb = (size_t)tok[i] * nb + b;
                         const int4 qa = __ldg(reinterpret_cast<const int4 *>(x.q + xb * QK));
                         const int4 qb = __ldg(reinterpret_cast<const int4 *>(x.q + xb * QK + 16));
                         const int sumi = q4q8_sumi(nib, qa, qb, __ldg(x.s + xb));
-                        acc[i] = fmaf((float)sumi, __fmul_rn(dw, __ldg(x.d + xb)), acc[i]);
+                        term[i] = __fmul_rn((float)sumi, __fmul_rn(dw, __ldg(x.d + xb)));
                     }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                    for (int i = 0; i < GU_TOK; ++i)
+                        acc[i] = __fadd_rn(acc[i], __shfl_sync(0xffffffffu, term[i], (lane & ~7) | j));
                 }
             }
 #pragma unroll
             for (int i = 0; i < GU_TOK; ++i) {
-                float v = acc[i];
-                v += __shfl_xor_sync(0xffffffffu, v, 4);
-                v += __shfl_xor_sync(0xffffffffu, v, 2);
-                v += __shfl_xor_sync(0xffffffffu, v, 1);
                 if (l8 == 0 && i < nt) {
                     const int col = warp * 4 + grp;
                     if (pass == 0)
-                        sg[i][col] = v;
+                        sg[i][col] = acc[i];
                     else
-                        su[i][col] = v;
+                        su[i][col] = acc[i];
                 }
             }
         }
@@ -196,17 +206,18 @@ __global__ void __launch_bounds__(256) k_down_combine_decode(PackedView pk, int 
             }
             for (int j = 0; j < n_e; ++j) {
                 const size_t k = (size_t)(p0 + j);
-                float v = 0.0f;
+                float term = 0.0f;
                 if (lane < nbh) {
                     const size_t hb = k * nbh + lane;
                     const int4 qa = __ldg(reinterpret_cast<const int4 *>(h.q + hb * QK));
                     const int4 qb = __ldg(reinterpret_cast<const int4 *>(h.q + hb * QK + 16));
                     const int sumi = q4q8_sumi(nib, qa, qb, __ldg(h.s + hb));
-                    v = (float)sumi * __fmul_rn(dw, __ldg(h.d + hb));
+                    term = __fmul_rn((float)sumi, __fmul_rn(dw, __ldg(h.d + hb)));
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) ysm[k * DN_ROWS + rr] = v;
+                // block terms added in block order, as the scalar reference (expert_kernel.rs:147-161)
+                float acc = 0.0f;
+                for (int b = 0; b < nbh; ++b) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, b));
+                if (lane == 0) ysm[k * DN_ROWS + rr] = acc;
             }
         }
         __syncthreads();

@@ -234,7 +234,7 @@ namespace {
 int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids, const float *wts,
                 int n_tok, float *out, void *ws, const Workspace &L, bool quantised, cudaStream_t st) {
     const int pairs = n_tok * w->used;
-    if (pairs > DECODE_MAX_PAIRS) return RVC_ERR_UNSUPPORTED;
+    if (pairs > DECODE_MAX_PAIRS || w->ff / QK > 32) return RVC_ERR_UNSUPPORTED;
     const int nb = w->n_embd / QK;
     int rc;
     if (!quantised) {

@@ -21,7 +21,16 @@ def oracle():
 
 @pytest.fixture(scope="session")
 def pool(oracle):
-    p = oracle.Pool(threads=min(8, os.cpu_count() or 1))
+    # the reference's generic (scalar) Q8_0 order: the GPU path reproduces it bit for bit
+    p = oracle.Pool(threads=min(8, os.cpu_count() or 1), kernel=oracle.KERNEL_SCALAR)
+    yield p
+    p.close()
+
+
+@pytest.fixture(scope="session")
+def pool_avx2(oracle):
+    # the reference's AVX2 int8 routine (expert_kernel.rs:163-191): same integers, other f32 order
+    p = oracle.Pool(threads=min(8, os.cpu_count() or 1), kernel=oracle.KERNEL_AVX2)
     yield p
     p.close()
 

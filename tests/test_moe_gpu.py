@@ -1,12 +1,16 @@
 """GPU parity of the decode MoE path against the CPU oracle, through the C ABI.
 
-Bars (from the task's north star): expert ids and int32 block dot products bit-exact; the
-router logits are also bit-exact (same sequential f32 order as runtime/src/ops.rs:321-326);
-fp32 layer outputs within max-rel 1e-3 per row, where a row's relative error is
-max_i |gpu_i - cpu_i| / max_i |cpu_i| (the denominator guarded by the row's largest
-magnitude, as scripts/correctness_oracle.py:96-115 guards its relative errors). Rows with
-exact router ties would be excluded and counted; seeded inputs here have none, which the
-tests assert.
+Bars (from the task's north star): expert ids and int32 block dot products bit-exact, fp32
+layer outputs within max-rel 1e-3 per row (a row's relative error is
+max_i |gpu_i - cpu_i| / max_i |cpu_i|, the denominator guarded by the row's largest magnitude,
+as scripts/correctness_oracle.py:96-115 guards its relative errors). Rows with exact router
+ties would be excluded and counted; seeded inputs here have none, which the tests assert.
+
+The decode path does better than the tolerance: it reproduces the reference's generic (scalar)
+Q8_0 order (runtime/src/expert_kernel.rs:147-161) and its router order (ops.rs:321-326), so
+logits, weights, ids and the layer output are bit-identical to the oracle's scalar kernel. The
+reference's own AVX2 routine (expert_kernel.rs:163-191) sums in another f32 order; against it
+the bar is the 1e-3 tolerance, which is also how far the reference's two routines are apart.
 """
 import numpy as np
 import pytest
@@ -63,8 +67,7 @@ def test_router_bit_exact(layer, weights, oracle, n_tok, cfg):
     assert exact_ties(probs) == 0
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     gw = wts.cpu().numpy()
-    ulps = np.abs(gw.view(np.int32).astype(np.int64) - want_w.view(np.int32).astype(np.int64))
-    assert ulps.max() <= 2, f"weights differ by {ulps.max()} ulp"
+    assert np.array_equal(gw.view(np.uint32), want_w.view(np.uint32)), "weights must be bit-exact"
     order, pos_of, counts = oracle.moe_plan(want_ids, 128)
     assert np.array_equal(hist.cpu().numpy(), counts)
     assert np.array_equal(perm.cpu().numpy(), order)
@@ -109,17 +112,21 @@ def test_int32_block_dots_bit_exact(layer, weights, oracle, which, expert, extre
 
 
 @pytest.mark.parametrize("n_tok", [1, 2, 4, 8, 16, 32, 64])
-def test_decode_layer_matches_oracle(layer, weights, oracle, pool, n_tok):
+def test_decode_layer_matches_oracle(layer, weights, oracle, pool, pool_avx2, n_tok):
     from rosevine_b200 import synth
     x = synth.tokens(n_tok, 200 + n_tok)
     ids = torch.empty((n_tok, 8), dtype=torch.int32, device="cuda")
     wts = torch.empty((n_tok, 8), dtype=torch.float32, device="cuda")
     out = layer.forward(xdev(x), ids=ids, wts=wts)
     layer.status()
+    got = out.cpu().numpy()
     want, want_ids, want_w, _ = oracle.moe_layer(pool, x, x, weights["w_router"], weights["gate_up"], weights["down"])
     assert np.array_equal(ids.cpu().numpy(), want_ids)
-    err = row_rel_err(out.cpu().numpy(), want)
-    assert err.max() <= ROW_TOL, f"max row rel err {err.max():.3e}"
+    assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"not bit-exact: max row rel err {row_rel_err(got, want).max():.3e}"
+    want_avx2, _, _, _ = oracle.moe_layer(pool_avx2, x, x, weights["w_router"], weights["gate_up"], weights["down"])
+    assert row_rel_err(got, want_avx2).max() <= ROW_TOL
 
 
 def test_decode_f32_inputs_f32_router_and_down_scale(weights, oracle, pool):
@@ -136,8 +143,9 @@ def test_decode_f32_inputs_f32_router_and_down_scale(weights, oracle, pool):
     out = lyr.forward(torch.from_numpy(xr).cuda(), x_expert=torch.from_numpy(x).cuda())
     lyr.status()
     want, _, _, _ = oracle.moe_layer(pool, xr, x, wr, weights["gate_up"], weights["down"], down_scale=ds)
-    err = row_rel_err(out.cpu().numpy(), want)
-    assert err.max() <= ROW_TOL, f"max row rel err {err.max():.3e}"
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"not bit-exact: max row rel err {row_rel_err(got, want).max():.3e}"
 
 
 def test_experts_entry_with_caller_ids(layer, weights, oracle, pool):
@@ -150,7 +158,7 @@ def test_experts_entry_with_caller_ids(layer, weights, oracle, pool):
     out = layer.experts(xdev(x), torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda())
     layer.status()
     want = oracle.experts_q8(pool, x, weights["gate_up"], weights["down"], None, ids, w)
-    assert row_rel_err(out.cpu().numpy(), want).max() <= ROW_TOL
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
 def test_repeat_calls_are_deterministic(layer):
