@@ -125,6 +125,22 @@ int rvc_workspace_reset(void *workspace, void *stream);
  * returns 0, RVC_ERR_DEVICE_TIMEOUT or RVC_ERR_DEVICE_INDEX. */
 int rvc_status(void *workspace, void *stream);
 
+/* rvc_moe_forward without a caller workspace (no counterpart in the reference; added for
+ * hosts that cannot allocate device memory per call - their VRAM is pre-carved by their own
+ * allocator, or a decode step must never risk a failing or synchronising allocation).
+ * Scratch comes from a fixed array of RVC_NOALLOC_SCRATCH_BYTES inside librvcuda.so, which
+ * every GPU that loads the library holds until the process exits; that is room for 64
+ * tokens at the target's shapes. Calls needing more return RVC_ERR_WORKSPACE. Nothing is
+ * allocated. The first call on a device looks up the array's device address (make that
+ * first call before any stream capture). All calls share the one array: calls that may
+ * overlap on the GPU (other streams, other threads) race and must be serialised by the
+ * caller. Device status (bounded-wait timeouts) is cleared at the start of every call and
+ * is not reported by this entry point. */
+#define RVC_NOALLOC_SCRATCH_BYTES (1u << 20)
+int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
+                            const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
+                            void *stream);
+
 /* Test hook: the exact int32 Q4_0 x Q8_0 block sums the expert kernels form, for
  * `n_rows` rows of one expert of the packed weights against Q8_0 activation rows.
  * which: 0 = gate_up (original row numbering), 1 = down. xq8: device [n_in][nblk*34]

@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "experts_decode.cuh"
@@ -481,3 +482,50 @@ int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------ fixed-scratch layer (no allocation)
+// Some hosts cannot hand this library a workspace: their device memory is carved up once at
+// start-up by their own allocator, or they must never risk an allocation failing (or
+// synchronising the device) in the middle of a decode step. rvc_moe_forward_noalloc serves
+// them from this file-scope array instead, sized RVC_NOALLOC_SCRATCH_BYTES per GPU and held
+// by every GPU that loads the library until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[RVC_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device memory: the device
+// address has to be looked up, once per device, with that device current.
+int noalloc_scratch(void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+}  // namespace
+
+extern "C" int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, const void *x_expert,
+                                       int x_dtype, const float *bias, int bias_stride, int n_tok, float *out,
+                                       int32_t *ids, float *wts, void *stream) {
+    if (!dims_ok(w) || n_tok <= 0) return (int)cudaErrorInvalidValue;
+    if (Workspace(n_tok, w->n_embd, w->ff, w->n_experts, w->used).total > (size_t)RVC_NOALLOC_SCRATCH_BYTES)
+        return RVC_ERR_WORKSPACE;
+    void *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // The array keeps the previous call's contents; only the status word must start at zero.
+    rc = (int)cudaMemsetAsync(scratch, 0, 256, S(stream));
+    if (rc) return rc;
+    return rvc_moe_forward(w, x_router, x_expert, x_dtype, bias, bias_stride, n_tok, out, ids, wts, scratch,
+                           RVC_NOALLOC_SCRATCH_BYTES, stream);
+}

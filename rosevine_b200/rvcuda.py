@@ -30,7 +30,7 @@ EXPORTS = [
     "rvc_error_string", "rvc_event_create", "rvc_event_destroy", "rvc_event_record", "rvc_event_sync",
     "rvc_event_elapsed", "rvc_upload_async", "rvc_download_async", "rvc_event_record_on", "rvc_stream_sync",
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
-    "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums",
+    "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
 ]
 
 
@@ -94,6 +94,7 @@ def lib() -> ctypes.CDLL:
             "rvc_workspace_reset": ([P, P], I),
             "rvc_status": ([P, P], I),
             "rvc_debug_block_sums": ([W, I, I, P, I, P, I, P, P], I),
+            "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -256,6 +257,21 @@ def moe_forward(w: MoeWeights, x_router, x_expert, x_dtype: int, n_tok: int, out
                                 _ptr(bias, bias_rows * 4), bias_stride, n_tok, _ptr(out, n_tok * w.n_embd * 4),
                                 _ptr(ids, n_tok * w.used * 4), _ptr(wts, n_tok * w.used * 4), ws.ptr, ws.nbytes,
                                 stream))
+
+
+NOALLOC_SCRATCH_BYTES = 1 << 20
+
+
+def moe_forward_noalloc(w: MoeWeights, x_router, x_expert, x_dtype: int, n_tok: int, out, bias=None,
+                        bias_stride: int = 0, ids=None, wts=None, stream: int | None = None) -> None:
+    """rvc_moe_forward on the library's fixed device scratch: for callers that cannot provide
+    (allocate) a workspace. Up to 64 tokens at the target's shapes; calls must not overlap."""
+    xb = n_tok * w.n_embd * _xbytes(x_dtype)
+    bias_rows = (n_tok - 1) * bias_stride + w.n_experts if bias is not None else 0
+    check(lib().rvc_moe_forward_noalloc(ctypes.byref(w), _ptr(x_router, xb), _ptr(x_expert, xb), x_dtype,
+                                        _ptr(bias, bias_rows * 4), bias_stride, n_tok,
+                                        _ptr(out, n_tok * w.n_embd * 4), _ptr(ids, n_tok * w.used * 4),
+                                        _ptr(wts, n_tok * w.used * 4), stream))
 
 
 def workspace_reset(workspace, stream: int | None = None) -> None:
