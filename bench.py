@@ -169,7 +169,34 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     ho = {b: torch.empty((b, 2816), dtype=torch.float32).pin_memory() for b in SWEEP}
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in SWEEP]
 
-    def step_device(timed: bool):
+    # One CUDA graph per B holding the layer call (the C ABI call captured as-is: K0 on the
+    # library's side lane, K1, gate/up, down+combine). Warm-up outside capture first.
+    graphs, graphs_exp = {}, {}
+    for b in SWEEP:
+        layer.forward(xs[b], out=outs[b], ids=ids[b], wts=wts[b], stream=sh)
+        layer.experts(xs[b], ids[b], wts[b], out=outs[b], stream=sh)
+    torch.cuda.synchronize()
+    for b in SWEEP:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer.forward(xs[b], out=outs[b], ids=ids[b], wts=wts[b])
+        graphs[b] = g
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            layer.experts(xs[b], ids[b], wts[b], out=outs[b])
+        graphs_exp[b] = g2
+    torch.cuda.synchronize()
+
+    def step_graph(timed: bool, which=graphs):
+        for i, b in enumerate(SWEEP):
+            flush.zero_()
+            if timed:
+                ev[i][0].record(stream)
+            which[b].replay()
+            if timed:
+                ev[i][1].record(stream)
+
+    def step_stream(timed: bool):
         for i, b in enumerate(SWEEP):
             flush.zero_()
             if timed:
@@ -209,26 +236,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank])
                           if os.environ.get("CUDA_VISIBLE_DEVICES") else local_rank)
     clocks.start()
-    per_b = timed_loop(step_device, args.steps, args.warmup)
+    per_b = timed_loop(step_graph, args.steps, args.warmup)
     clk = clocks.stop()
     layer.status(stream=sh)
+    per_b_stream = timed_loop(step_stream, args.steps, args.warmup)
     per_b_e2e = timed_loop(step_e2e, max(1, args.steps), max(1, args.warmup))
-    layer.status(stream=sh)
-
-    # expert phase alone, for the roofline (same ids as the timed forward)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    phase = {}
-    for b in SWEEP:
-        tsum = 0.0
-        for it in range(args.warmup + args.steps):
-            flush.zero_()
-            e0.record(stream)
-            layer.experts(xs[b], ids[b], wts[b], out=outs[b], stream=sh)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            if it >= args.warmup:
-                tsum += e0.elapsed_time(e1)
-        phase[b] = tsum / args.steps
+    phase = timed_loop(lambda t: step_graph(t, graphs_exp), args.steps, args.warmup)
     layer.status(stream=sh)
 
     distinct = {b: distinct_experts(ids[b].cpu().numpy()) for b in SWEEP}
@@ -248,11 +261,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         decode.append({"B": b, "us_per_layer": per_b[b] * 1e3, "distinct_experts": distinct[b],
                        "algorithmic_bytes": byt, "hbm_gbs": byt / (per_b[b] * 1e-3) / 1e9,
                        "frac_of_hbm": byt / (per_b[b] * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                       "us_per_layer_no_graph": per_b_stream[b] * 1e3,
                        "expert_phase_us": phase[b] * 1e3, "e2e_us": per_b_e2e[b] * 1e3})
-    # roofline of the expert phase over the sweep (bytes and time summed over B)
+    # roofline of the whole decode layer over the sweep (algorithmic bytes and device time
+    # summed over B), and of the expert GEMV phase alone
+    lay_bytes = sum(algorithmic_bytes(b, distinct[b]) for b in SWEEP)
+    achieved = lay_bytes / (step_ms * 1e-3) / 1e9
     ph_bytes = sum(distinct[b] * EXPERT_BYTES for b in SWEEP)
-    ph_ms = sum(phase.values())
-    achieved = ph_bytes / (ph_ms * 1e-3) / 1e9
+    ph_gbs = ph_bytes / (sum(phase.values()) * 1e-3) / 1e9
     h2d = sum(b * 2816 * 2 for b in SWEEP)
     d2h = sum(b * 2816 * 4 for b in SWEEP)
     res = {
@@ -265,14 +281,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "tokens_per_step": tokens, "l2": "flushed (256 MB write) before every timed layer call",
                    "parallelism": "replicas" if world > 1 else "single GPU"},
         "decode": {"b1_us_per_token": per_b[1] * 1e3, "b1_hbm_gbs": decode[0]["hbm_gbs"], "per_b": decode},
-        "roofline": {"bound": "hbm", "kernel": "expert phase (rvc_moe_experts: quant, plan, gate/up GEMV, "
-                                                "down GEMV + combine), summed over the sweep",
+        "roofline": {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_router_chains || k_route_fast, "
+                                                "k_gate_up_decode, k_down_combine_decode), bytes and time summed "
+                                                "over the sweep",
                      "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                     "expert_phase_gbs": ph_gbs, "expert_phase_frac": ph_gbs / peaks["hbm_gbs"],
                      "traffic": None},
         "e2e": {"value": world * tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 5 * len(SWEEP) * args.steps,
+        "gpu_launches": 4 * len(SWEEP) * args.steps,
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu:

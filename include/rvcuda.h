@@ -136,7 +136,7 @@ int rvc_status(void *workspace, void *stream);
  * overlap on the GPU (other streams, other threads) race and must be serialised by the
  * caller. Device status (bounded-wait timeouts) is cleared at the start of every call and
  * is not reported by this entry point. */
-#define RVC_NOALLOC_SCRATCH_BYTES (1u << 20)
+#define RVC_NOALLOC_SCRATCH_BYTES (8u << 20)
 int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
                             const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
                             void *stream);

@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "librvcuda.so")
 SOURCES = ["csrc/rvcuda.cu"]
-HEADERS = ["csrc/common.cuh", "csrc/router.cuh", "csrc/experts_decode.cuh", "csrc/pack.cuh"]
+HEADERS = ["csrc/common.cuh", "csrc/router.cuh", "csrc/router_fast.cuh", "csrc/experts_decode.cuh", "csrc/pack.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]
@@ -23,13 +23,16 @@ def stale() -> bool:
     return any(os.path.getmtime(os.path.join(HERE, d)) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not stale():
+def build(force: bool = False, verbose: bool = False, profile_out: str | None = None) -> str:
+    """Build librvcuda.so; with profile_out, build a profiling variant (phase timestamps,
+    -DRVC_PROFILE) at that path instead."""
+    out = profile_out or LIB
+    if not force and not profile_out and not stale():
         return LIB
-    cmd = [NVCC, *FLAGS, *([] if not verbose else ["-Xptxas", "-v"]), "-o", LIB,
-           *[os.path.join(HERE, s) for s in SOURCES]]
+    cmd = [NVCC, *FLAGS, *([] if not verbose else ["-Xptxas", "-v"]), *(["-DRVC_PROFILE"] if profile_out else []),
+           "-o", out, *[os.path.join(HERE, s) for s in SOURCES]]
     subprocess.run(cmd, check=True, cwd=HERE)
-    return LIB
+    return out
 
 
 if __name__ == "__main__":

@@ -17,8 +17,29 @@ constexpr int Q8_BLOCK = 34;    // f16 d + 32 int8
 // Device status codes (bit flags, OR-ed into the status word).
 constexpr int STATUS_TIMEOUT = 1;   // a bounded wait ran out
 constexpr int STATUS_BAD_INDEX = 2; // an index read from device memory was out of range
+constexpr int STATUS_ROUTE_MISMATCH = 4;  // verified fast ids differ from the exact-order ids
 
 constexpr long long kSpinLimit = 1ll << 22;  // millions of polls: far above any real wait, still bounded
+
+// Phase timestamps for profiling builds (-DRVC_PROFILE): thread 0 of each CTA records the
+// global timer (ns) at marked points of a kernel; rvc_profile_dump (profiling builds only)
+// copies them out. Ordinary builds compile the marks away.
+#ifdef RVC_PROFILE
+__device__ unsigned long long g_prof[8][1024][8];
+#define RVC_MARK(K, P)                                                                             \
+    do {                                                                                           \
+        const unsigned b_ = blockIdx.x + blockIdx.y * gridDim.x;                                   \
+        if (threadIdx.x == 0 && b_ < 1024) {                                                       \
+            unsigned long long t_;                                                                 \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                 \
+            ::rvc::g_prof[K][b_][P] = t_;                                                          \
+        }                                                                                          \
+    } while (0)
+#else
+#define RVC_MARK(K, P) \
+    do {               \
+    } while (0)
+#endif
 
 __device__ __forceinline__ void set_status(int *status, int code) {
     if (status) atomicOr(status, code);
@@ -108,6 +129,32 @@ __device__ __forceinline__ int q4q8_sumi(const uint4 nib, const int4 qa, const i
     s = dp4a_us((nib.z >> 4) & 0x0F0F0F0Fu, qb.z, s);
     s = dp4a_us((nib.w >> 4) & 0x0F0F0F0Fu, qb.w, s);
     return s - 8 * qsum;
+}
+
+// ----------------------------------------------------------- Q8_0 row records
+// A quantised activation row (x of a token, h of a pair) as one contiguous record, so that a
+// row can be staged into shared memory with a single bulk copy:
+//   [nblk x 32 int8 quants][nblk x f32 scale (the f16 scale widened)][nblk x int32 sum of quants]
+// nblk*40 bytes, a multiple of 16 when nblk is even.
+__host__ __device__ constexpr int q8rec_bytes(int nblk) { return nblk * 40; }
+
+struct Q8Rec {
+    const uint8_t *p;  // start of the record
+    int nblk;
+    __device__ __forceinline__ int4 qa(int b) const { return *reinterpret_cast<const int4 *>(p + b * 32); }
+    __device__ __forceinline__ int4 qb(int b) const { return *reinterpret_cast<const int4 *>(p + b * 32 + 16); }
+    __device__ __forceinline__ float d(int b) const { return reinterpret_cast<const float *>(p + nblk * 32)[b]; }
+    __device__ __forceinline__ int s(int b) const { return reinterpret_cast<const int *>(p + nblk * 36)[b]; }
+};
+
+// Store block b of a record from the warp that quantised it (quant_q8_lane below).
+__device__ __forceinline__ void q8rec_store(uint8_t *rec, int nblk, int b, int lane, int8_t q, uint16_t dbits,
+                                            int qsum) {
+    rec[b * 32 + lane] = (uint8_t)q;
+    if (lane == 0) {
+        reinterpret_cast<float *>(rec + nblk * 32)[b] = __half2float(__ushort_as_half(dbits));
+        reinterpret_cast<int *>(rec + nblk * 36)[b] = qsum;
+    }
 }
 
 // tanh-approximation GELU with the reference's constants and evaluation order

@@ -4,7 +4,7 @@
 // runtime/src/hip_exec.rs:787), the blocking logits download (:789), and the host-side
 // select_experts / MoePlan (runtime/src/exec.rs:507-558).
 //
-// Parity: the logits are computed in the reference's exact order (matvec_f32,
+// Parity: logits are computed in the reference's exact order by router_fast.cuh (matvec_f32,
 // runtime/src/ops.rs:321-326: a sequential f32 sum of separately rounded products, folded
 // from -0.0), so they are bit-identical. Softmax follows ops.rs:170-179 (f32 exp of
 // (l - max), f64 sum, f32 scale by (1/sum)); top-8 follows ops.rs:182-187 (descending,
@@ -45,47 +45,6 @@ __device__ __forceinline__ void ld8<uint16_t>(const uint16_t *p, size_t i, float
     }
 }
 
-// ---------------------------------------------------------------- exact logits
-// One thread per expert row, TOK tokens per CTA. Each (token, expert) logit is one
-// sequential chain s = (s + w*x) with separately rounded multiply and add; the TOK
-// independent chains per thread give instruction-level parallelism.
-template <int TOK, typename XT, typename WT>
-__global__ void __launch_bounds__(128) k_router_logits_exact(const XT *__restrict__ x, const WT *__restrict__ w,
-                                                             const float *__restrict__ bias, int bias_stride,
-                                                             int n_tok, int n_experts, int n_embd,
-                                                             float *__restrict__ logits) {
-    const int e = blockIdx.y * blockDim.x + threadIdx.x;
-    const int t0 = blockIdx.x * TOK;
-    if (e >= n_experts) return;
-    float s[TOK];
-#pragma unroll
-    for (int i = 0; i < TOK; ++i) s[i] = -0.0f;
-    const int nt = min(TOK, n_tok - t0);
-    const WT *wr = w + (size_t)e * n_embd;
-    for (int k = 0; k < n_embd; k += 8) {
-        float wv[8];
-        ld8<WT>(wr, k, wv);
-        float xv[TOK][8];
-#pragma unroll
-        for (int i = 0; i < TOK; ++i) {
-            if (i < nt) ld8<XT>(x + (size_t)(t0 + i) * n_embd, k, xv[i]);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int i = 0; i < TOK; ++i) s[i] = __fadd_rn(s[i], __fmul_rn(wv[j], xv[i][j]));
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < TOK; ++i) {
-        if (i < nt) {
-            float v = s[i];
-            if (bias) v = __fadd_rn(v, __ldg(bias + (size_t)(t0 + i) * bias_stride + e));
-            logits[(size_t)(t0 + i) * n_experts + e] = v;
-        }
-    }
-}
-
 // IEEE totalOrder key (as f32::total_cmp): larger key = larger value.
 __device__ __forceinline__ int32_t total_key(float f) {
     int32_t b = __float_as_int(f);
@@ -96,27 +55,21 @@ constexpr float ROUTER_SUM_MIN = 1.0f / 16384.0f;  // exec.rs:124-125
 constexpr int MAX_EXPERTS = 256;
 constexpr int MAX_USED = 16;
 
-// ----------------------------------------------------------- select + quantise
-// One warp per token: softmax over n_experts (<= 256) logits, top `used`, renormalised
-// weights; then Q8_0 quantisation of the token's expert input (n_embd/32 blocks).
-// Q8 planes: xq[t][nb][32] int8, xd[t][nb] f32 (the f16 scale widened), xs[t][nb] sum of q.
-template <typename XT>
-__global__ void __launch_bounds__(256) k_select_quant(const float *__restrict__ logits, const XT *__restrict__ x_expert,
-                                                      int n_tok, int n_experts, int used, int n_embd,
-                                                      int32_t *__restrict__ ids, float *__restrict__ wts,
-                                                      float *__restrict__ probs_out, int8_t *__restrict__ xq,
-                                                      float *__restrict__ xd, int32_t *__restrict__ xs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (t >= n_tok) return;
+// ------------------------------------------------------------- selection
+// One warp: softmax over n_experts (<= 256) logits, top `used`, renormalised weights, for
+// one token (ops.rs:170-187, exec.rs:507-517). Logits are read with ld.global.cg so a CTA may
+// select on logits other CTAs wrote before a release/acquire handoff. ids/wts get `used`
+// entries in slot order; probs (may be NULL) all n_experts probabilities.
+__device__ __forceinline__ void warp_select(const float *lg, int n_experts, int used, int32_t *ids, float *wts,
+                                            float *probs) {
+    const int lane = threadIdx.x & 31;
     constexpr int PER = MAX_EXPERTS / 32;
-    const float *lg = logits + (size_t)t * n_experts;
     float v[PER];
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const int e = lane + 32 * i;
-        v[i] = e < n_experts ? lg[e] : -INFINITY;
+        v[i] = e < n_experts ? __ldcg(lg + e) : -INFINITY;
         mx = fmaxf(mx, v[i]);
     }
 #pragma unroll
@@ -139,14 +92,11 @@ __global__ void __launch_bounds__(256) k_select_quant(const float *__restrict__ 
         const int e = lane + 32 * i;
         v[i] = __fmul_rn(v[i], inv);
         key[i] = e < n_experts ? total_key(v[i]) : INT32_MIN;
-        if (probs_out && e < n_experts) probs_out[(size_t)t * n_experts + e] = v[i];
+        if (probs && e < n_experts) probs[e] = v[i];
     }
-    // top-`used`: repeated warp argmax over (key desc, index asc)
-    float sel_p = 0.0f;
-    int sel_e = 0;
-    float psum = -0.0f;
-    float ptop[MAX_USED];
-    int etop[MAX_USED];
+    // top-`used`: repeated warp argmax over (key desc, index asc); lane j keeps winner j
+    float psum = -0.0f, my_p = 0.0f;
+    int my_e = 0;
     for (int j = 0; j < used; ++j) {
         int32_t bk = INT32_MIN;
         int be = 0x7fffffff;
@@ -163,40 +113,29 @@ __global__ void __launch_bounds__(256) k_select_quant(const float *__restrict__ 
             float op = __shfl_xor_sync(0xffffffffu, bp, o);
             if (ok > bk || (ok == bk && oe < be)) bk = ok, be = oe, bp = op;
         }
-        // remove the winner
 #pragma unroll
         for (int i = 0; i < PER; ++i)
-            if (lane + 32 * i == be) key[i] = INT32_MIN, v[i] = -INFINITY;
-        if (j < MAX_USED) ptop[j] = bp, etop[j] = be;
+            if (lane + 32 * i == be) key[i] = INT32_MIN;
+        if (lane == j) my_p = bp, my_e = be;
         psum = __fadd_rn(psum, bp);  // f32 sum in top order (exec.rs:512)
-        (void)sel_p, (void)sel_e;
     }
     psum = fmaxf(psum, ROUTER_SUM_MIN);
     if (lane < used) {
-        float p = 0.0f;
-        int e = 0;
-#pragma unroll
-        for (int j = 0; j < MAX_USED; ++j)
-            if (j == lane) p = ptop[j], e = etop[j];
-        ids[(size_t)t * used + lane] = e;
-        wts[(size_t)t * used + lane] = __fdiv_rn(p, psum);
+        ids[lane] = my_e;
+        wts[lane] = __fdiv_rn(my_p, psum);
     }
-    // Q8_0 of the expert input (ops.rs:95-105), one block of 32 per warp iteration.
-    if (xq) {
-        const int nb = n_embd / QK;
-        const XT *xr = x_expert + (size_t)t * n_embd;
-        for (int b = 0; b < nb; ++b) {
-            float val = ld_val<XT>(xr, (size_t)b * QK + lane);
-            uint16_t dbits;
-            int qsum;
-            int8_t q = quant_q8_lane(val, &dbits, &qsum);
-            xq[((size_t)t * nb + b) * QK + lane] = q;
-            if (lane == 0) {
-                xd[(size_t)t * nb + b] = f16_bits_to_f32(dbits);
-                xs[(size_t)t * nb + b] = qsum;
-            }
-        }
-    }
+}
+
+// ----------------------------------------------------------------- select
+// One warp per token: warp_select over the token's logits.
+__global__ void __launch_bounds__(256) k_select(const float *__restrict__ logits, int n_tok, int n_experts, int used,
+                                                int32_t *__restrict__ ids, float *__restrict__ wts,
+                                                float *__restrict__ probs_out) {
+    const int warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= n_tok) return;
+    warp_select(logits + (size_t)t * n_experts, n_experts, used, ids + (size_t)t * used, wts + (size_t)t * used,
+                probs_out ? probs_out + (size_t)t * n_experts : nullptr);
 }
 
 // ------------------------------------------------------------------- plan

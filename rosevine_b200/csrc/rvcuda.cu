@@ -16,6 +16,7 @@
 #include "experts_decode.cuh"
 #include "pack.cuh"
 #include "router.cuh"
+#include "router_fast.cuh"
 
 using namespace rvc;
 
@@ -58,7 +59,11 @@ PackedView packed_view(const rvc_moe_weights *w) {
 
 // Workspace carve-up for calls of up to max_tok tokens.
 struct Workspace {
-    size_t status, logits, ids, wts, xq, xd, xs, counts, offsets, order, pos_of, active, n_active, hq, hd, hs, total;
+    // header (first 256 B, cleared by rvc_workspace_reset): int status at 0, the K0 and K1
+    // last-CTA counters at 4 and 8 (each kernel returns its counter to zero), and at 12 the
+    // running count of tokens the fast router sent to its exact fallback.
+    size_t status, logits, lbound, lexact0, lexact1, ids, ids_exact, wts, xrec, counts, offsets, order, pos_of,
+        active, n_active, hrec, ybuf, total;
     Workspace(int max_tok, int n_embd, int ff, int ne, int used) {
         const size_t nb = n_embd / QK, nbh = ff / QK, pairs = (size_t)max_tok * used;
         size_t o = 0;
@@ -69,20 +74,21 @@ struct Workspace {
         };
         status = take(256);
         logits = take((size_t)max_tok * ne * 4);
+        lbound = take((size_t)max_tok * ne * 4);
+        lexact0 = take((size_t)max_tok * ne * 4);
+        lexact1 = take((size_t)max_tok * ne * 4);
         ids = take(pairs * 4);
+        ids_exact = take(pairs * 4);
         wts = take(pairs * 4);
-        xq = take((size_t)max_tok * nb * QK);
-        xd = take((size_t)max_tok * nb * 4);
-        xs = take((size_t)max_tok * nb * 4);
+        xrec = take((size_t)max_tok * q8rec_bytes((int)nb));
         counts = take((size_t)ne * 4);
         offsets = take((size_t)(ne + 1) * 4);
         order = take(pairs * 4);
         pos_of = take(pairs * 4);
         active = take((size_t)ne * 4);
         n_active = take(4);
-        hq = take(pairs * nbh * QK);
-        hd = take(pairs * nbh * 4);
-        hs = take(pairs * nbh * 4);
+        hrec = take(pairs * q8rec_bytes((int)nbh));
+        ybuf = pairs > (size_t)DN_MAX_PAIRS ? take(pairs * n_embd * 4) : o;  // y of the expert-major path
         total = o;
     }
 };
@@ -105,14 +111,14 @@ int ws_max_tok(size_t bytes, const rvc_moe_weights *w) {
     return lo;
 }
 
-constexpr int DECODE_MAX_PAIRS = 512;  // k_down_combine_decode keeps [pairs][16] f32 in smem
+constexpr int DECODE_MAX_PAIRS = 512;  // pairs per call on the decode kernels
 
 // Opt a kernel into the dynamic shared memory it needs beyond the default 48 KB: the opt-in
 // limit is the device's per-block maximum minus the kernel's static shared memory. Done once
 // per (kernel slot, device); returns a CUDA error code.
 template <typename K>
 int set_smem_attr(K kernel, int slot) {
-    static bool done[16][64] = {};
+    static bool done[40][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
@@ -129,36 +135,102 @@ int set_smem_attr(K kernel, int slot) {
     return 0;
 }
 
-int launch_router_logits(const rvc_moe_weights *w, const void *x, int x_dtype, const float *bias, int bias_stride,
-                         int n_tok, float *logits, cudaStream_t st) {
-    constexpr int TOK = 8;
-    dim3 grid((n_tok + TOK - 1) / TOK, (w->n_experts + 127) / 128);
-    const bool xb = x_dtype == RVC_BF16, wb = w->router_dtype == RVC_BF16;
-    if (xb && wb)
-        k_router_logits_exact<TOK, uint16_t, uint16_t><<<grid, 128, 0, st>>>(
-            (const uint16_t *)x, (const uint16_t *)w->router, bias, bias_stride, n_tok, w->n_experts, w->n_embd,
-            logits);
-    else if (xb)
-        k_router_logits_exact<TOK, uint16_t, float><<<grid, 128, 0, st>>>(
-            (const uint16_t *)x, (const float *)w->router, bias, bias_stride, n_tok, w->n_experts, w->n_embd, logits);
-    else if (wb)
-        k_router_logits_exact<TOK, float, uint16_t><<<grid, 128, 0, st>>>(
-            (const float *)x, (const uint16_t *)w->router, bias, bias_stride, n_tok, w->n_experts, w->n_embd, logits);
-    else
-        k_router_logits_exact<TOK, float, float><<<grid, 128, 0, st>>>(
-            (const float *)x, (const float *)w->router, bias, bias_stride, n_tok, w->n_experts, w->n_embd, logits);
+int g_num_sms[64] = {};
+int num_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!g_num_sms[dev]) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    return g_num_sms[dev] > 0 ? g_num_sms[dev] : 148;
+}
+
+// Tokens per K0 tile: up to 16 (8 for f32 activations, to fit the staged rows in shared memory).
+template <typename XT>
+int chains_tpc(int n_tok) {
+    return std::min(n_tok, sizeof(XT) == 4 ? 8 : 16);
+}
+
+// K0: exact-order router chains -> lexact; with done_cnt set, the last CTA also selects ids/wts.
+template <typename XT, typename WT>
+int launch_chains_t(RouteArgs a, cudaStream_t st) {
+    const int tpc = chains_tpc<XT>(a.n_tok);
+    const size_t smem = (size_t)C0_EPC * c0_row_bytes<WT>(a.n_embd) + (size_t)tpc * c0_row_bytes<XT>(a.n_embd);
+    int rc = set_smem_attr(k_router_chains<XT, WT>, 2 + 2 * (int)sizeof(XT) / 2 + (int)sizeof(WT) / 4);
+    if (rc) return rc;
+    dim3 grid((a.n_experts + C0_EPC - 1) / C0_EPC, (a.n_tok + tpc - 1) / tpc);
+    const int threads = std::max(32, (C0_EPC * tpc + 31) / 32 * 32);
+    k_router_chains<XT, WT><<<grid, threads, smem, st>>>(a, tpc);
     return launched();
 }
 
-int launch_select_quant(const rvc_moe_weights *w, const float *logits, const void *x_expert, int x_dtype, int n_tok,
-                        int32_t *ids, float *wts, int8_t *xq, float *xd, int32_t *xs, cudaStream_t st) {
-    dim3 grid((n_tok + 7) / 8);
-    if (x_dtype == RVC_BF16)
-        k_select_quant<uint16_t><<<grid, 256, 0, st>>>(logits, (const uint16_t *)x_expert, n_tok, w->n_experts,
-                                                         w->used, w->n_embd, ids, wts, nullptr, xq, xd, xs);
-    else
-        k_select_quant<float><<<grid, 256, 0, st>>>(logits, (const float *)x_expert, n_tok, w->n_experts, w->used,
-                                                      w->n_embd, ids, wts, nullptr, xq, xd, xs);
+int launch_chains(const RouteArgs &a, int x_dtype, int w_dtype, cudaStream_t st) {
+    const bool xb = x_dtype == RVC_BF16, wb = w_dtype == RVC_BF16;
+    if (xb && wb) return launch_chains_t<uint16_t, uint16_t>(a, st);
+    if (xb) return launch_chains_t<uint16_t, float>(a, st);
+    if (wb) return launch_chains_t<float, uint16_t>(a, st);
+    return launch_chains_t<float, float>(a, st);
+}
+
+// K1: verified fast router + Q8_0 of x + plan (n_tok <= RF_MAX_TOK), templated on n_embd / 256.
+template <typename XT, typename WT, int NB8>
+int launch_route_fast_n(RouteArgs a, cudaStream_t st) {
+    const size_t smem = (size_t)a.n_embd * sizeof(float);  // fallback: one x row (below 48 KB)
+    k_route_fast<XT, WT, NB8><<<std::min(a.n_experts, num_sms()), RF_THREADS, smem, st>>>(a);
+    return launched();
+}
+
+template <typename XT, typename WT>
+int launch_route_fast_t(RouteArgs a, cudaStream_t st) {
+    switch (a.n_embd / 256) {
+        case 1: return launch_route_fast_n<XT, WT, 1>(a, st);
+        case 2: return launch_route_fast_n<XT, WT, 2>(a, st);
+        case 4: return launch_route_fast_n<XT, WT, 4>(a, st);
+        case 8: return launch_route_fast_n<XT, WT, 8>(a, st);
+        case 11: return launch_route_fast_n<XT, WT, 11>(a, st);
+        case 16: return launch_route_fast_n<XT, WT, 16>(a, st);
+        default: return RVC_ERR_UNSUPPORTED;
+    }
+}
+
+int launch_route_fast(const RouteArgs &a, int x_dtype, int w_dtype, cudaStream_t st) {
+    const bool xb = x_dtype == RVC_BF16, wb = w_dtype == RVC_BF16;
+    if (xb && wb) return launch_route_fast_t<uint16_t, uint16_t>(a, st);
+    if (xb) return launch_route_fast_t<uint16_t, float>(a, st);
+    if (wb) return launch_route_fast_t<float, uint16_t>(a, st);
+    return launch_route_fast_t<float, float>(a, st);
+}
+
+// Per-device side stream and fork/join events for K0, which runs beside K1 and the gate/up
+// GEMV. The mutex keeps one caller's record/wait pairs together.
+struct SideLane {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+SideLane g_side[64];
+
+int side_lane(SideLane **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    SideLane &L = g_side[dev];
+    if (!L.stream) {
+        std::lock_guard<std::mutex> lock(L.mu);
+        if (!L.stream) {
+            cudaStream_t s;
+            if ((e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return (int)e;
+            if ((e = cudaEventCreateWithFlags(&L.fork, cudaEventDisableTiming)) != cudaSuccess) return (int)e;
+            if ((e = cudaEventCreateWithFlags(&L.join, cudaEventDisableTiming)) != cudaSuccess) return (int)e;
+            L.stream = s;
+        }
+    }
+    *out = &L;
+    return 0;
+}
+
+int launch_select(const rvc_moe_weights *w, const float *logits, int n_tok, int32_t *ids, float *wts,
+                  cudaStream_t st) {
+    k_select<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, n_tok, w->n_experts, w->used, ids, wts, nullptr);
     return launched();
 }
 
@@ -168,8 +240,7 @@ int launch_select_quant(const rvc_moe_weights *w, const float *logits, const voi
 namespace rvc {
 template <typename XT>
 __global__ void __launch_bounds__(256) k_quant_rows(const XT *__restrict__ x, int n_tok, int n_embd,
-                                                    int8_t *__restrict__ xq, float *__restrict__ xd,
-                                                    int32_t *__restrict__ xs) {
+                                                    uint8_t *__restrict__ xrec) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = n_embd / QK;
     const long long total = (long long)n_tok * nb;
@@ -179,11 +250,7 @@ __global__ void __launch_bounds__(256) k_quant_rows(const XT *__restrict__ x, in
         uint16_t dbits;
         int qsum;
         const int8_t q = quant_q8_lane(v, &dbits, &qsum);
-        xq[(size_t)i * QK + lane] = q;
-        if (lane == 0) {
-            xd[i] = f16_bits_to_f32(dbits);
-            xs[i] = qsum;
-        }
+        q8rec_store(xrec + (size_t)t * q8rec_bytes(nb), nb, (int)b, lane, q, dbits, qsum);
     }
 }
 
@@ -232,48 +299,80 @@ __global__ void k_debug_block_sums(PackedView pk, int which, int expert, int n_e
 
 namespace {
 
-int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids, const float *wts,
-                int n_tok, float *out, void *ws, const Workspace &L, bool quantised, cudaStream_t st) {
+// Expert GEMVs for n_tok <= 64 tokens: (Q8_0 of x,) plan, gate/up, down + combine.
+// quantised: x already in the workspace's Q8 planes; planned: the plan is already built.
+// ids_check: exact-order ids the combine verifies against (may be NULL). join: an event the
+// stream waits for before the down/combine kernel (the exact weights), or NULL.
+int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids,
+                const int32_t *ids_check, const float *wts, int n_tok, float *out, void *ws, const Workspace &L,
+                bool quantised, bool planned, cudaEvent_t join, cudaStream_t st) {
     const int pairs = n_tok * w->used;
-    if (pairs > DECODE_MAX_PAIRS || w->ff / QK > 32) return RVC_ERR_UNSUPPORTED;
-    const int nb = w->n_embd / QK;
+    const int nb = w->n_embd / QK, nbh = w->ff / QK;
+    if (pairs > DECODE_MAX_PAIRS || nbh % 2) return RVC_ERR_UNSUPPORTED;
     int rc;
+    uint8_t *xrec = at<uint8_t>(ws, L.xrec), *hrec = at<uint8_t>(ws, L.hrec);
     if (!quantised) {
         const int blocks = std::min(1184, (int)(((long long)n_tok * nb + 7) / 8));
         if (x_dtype == RVC_BF16)
-            k_quant_rows<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)x_expert, n_tok, w->n_embd,
-                                                           at<int8_t>(ws, L.xq), at<float>(ws, L.xd),
-                                                           at<int32_t>(ws, L.xs));
+            k_quant_rows<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)x_expert, n_tok, w->n_embd, xrec);
         else
-            k_quant_rows<float><<<blocks, 256, 0, st>>>((const float *)x_expert, n_tok, w->n_embd, at<int8_t>(ws, L.xq),
-                                                        at<float>(ws, L.xd), at<int32_t>(ws, L.xs));
+            k_quant_rows<float><<<blocks, 256, 0, st>>>((const float *)x_expert, n_tok, w->n_embd, xrec);
         if ((rc = launched())) return rc;
     }
     int *status = at<int>(ws, L.status);
-    k_plan<<<1, PLAN_THREADS, 0, st>>>(ids, pairs, w->n_experts, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
-                                       at<int32_t>(ws, L.order), at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
-                                       at<int32_t>(ws, L.n_active), status);
-    if ((rc = launched())) return rc;
+    if (!planned) {
+        k_plan<<<1, PLAN_THREADS, 0, st>>>(ids, pairs, w->n_experts, at<int32_t>(ws, L.counts),
+                                           at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.order),
+                                           at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
+                                           at<int32_t>(ws, L.n_active), status);
+        if ((rc = launched())) return rc;
+    }
     PlanView plan{at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.order),
                   at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active), at<int32_t>(ws, L.n_active)};
     PackedView pk = packed_view(w);
-    Q8View xv{at<int8_t>(ws, L.xq), at<float>(ws, L.xd), at<int32_t>(ws, L.xs)};
+    const int max_active = std::min(w->n_experts, pairs);
     {
-        const size_t smem = (size_t)GU_UNIT_ROWS * nb * 18;
-        if ((rc = set_smem_attr(k_gate_up_decode, 0))) return rc;
-        dim3 grid(w->ff / 32, std::min(w->n_experts, pairs));
-        k_gate_up_decode<<<grid, 256, smem, st>>>(pk, w->n_embd, w->ff, xv, plan, w->used, at<int8_t>(ws, L.hq),
-                                                  at<float>(ws, L.hd), at<int32_t>(ws, L.hs), status);
+        const size_t smem = gu_smem_bytes(nb);
+        dim3 grid(w->ff / 32, max_active);
+        switch (nb / 8) {
+#define RVC_GU_CASE(NB8)                                                                                  \
+    case NB8:                                                                                             \
+        if ((rc = set_smem_attr(k_gate_up_decode<NB8>, 16 + NB8))) return rc;                            \
+        k_gate_up_decode<NB8><<<grid, 256, smem, st>>>(pk, w->ff, xrec, plan, w->used, hrec, status); \
+        break;
+            RVC_GU_CASE(1)
+            RVC_GU_CASE(2)
+            RVC_GU_CASE(4)
+            RVC_GU_CASE(8)
+            RVC_GU_CASE(11)
+            RVC_GU_CASE(16)
+#undef RVC_GU_CASE
+            default:
+                return RVC_ERR_UNSUPPORTED;
+        }
         if ((rc = launched())) return rc;
     }
-    {
-        const int nbh = w->ff / QK;
-        const size_t stage = ((size_t)DN_ROWS * nbh * 18 + 127) & ~size_t(127);
-        const size_t smem = DN_STAGES * stage + (size_t)pairs * DN_ROWS * 4;
+    if (pairs <= DN_MAX_PAIRS) {
+        // every h record fits in shared memory: down + slot-order combine in one kernel
+        const int nbuf = max_active > DN_BATCH ? 2 : 1;
+        const size_t smem = dn_smem_bytes(nbh, nbuf, pairs);
         if ((rc = set_smem_attr(k_down_combine_decode, 1))) return rc;
-        Q8View hv{at<int8_t>(ws, L.hq), at<float>(ws, L.hd), at<int32_t>(ws, L.hs)};
-        k_down_combine_decode<<<w->n_embd / DN_ROWS, 256, smem, st>>>(pk, w->n_embd, w->ff, hv, plan, ids, wts,
-                                                                      w->down_scale, n_tok, w->used, out, status);
+        if (join && (rc = (int)cudaStreamWaitEvent(st, join, 0))) return rc;
+        k_down_combine_decode<<<w->n_embd / DN_ROWS, 256, smem, st>>>(pk, w->n_embd, w->ff, hrec, plan, ids,
+                                                                      ids_check, wts, w->down_scale, n_tok, w->used,
+                                                                      nbuf, out, status);
+        if ((rc = launched())) return rc;
+    } else {
+        // expert-major down into y, then the slot-order combine
+        float *y = at<float>(ws, L.ybuf);
+        if ((rc = set_smem_attr(k_down_expert, 2))) return rc;
+        k_down_expert<<<dim3(w->n_embd / DE_ROWS, max_active), 256, de_smem_bytes(nbh), st>>>(pk, w->n_embd, w->ff,
+                                                                                            hrec, plan, y, status);
+        if ((rc = launched())) return rc;
+        if (join && (rc = (int)cudaStreamWaitEvent(st, join, 0))) return rc;
+        k_combine<<<dim3((w->n_embd + 255) / 256, n_tok), 256, 0, st>>>(y, plan.pos_of, ids, ids_check, wts,
+                                                                         w->down_scale, w->used, w->n_embd, out,
+                                                                         status);
         if ((rc = launched())) return rc;
     }
     return 0;
@@ -402,9 +501,13 @@ int rvc_moe_router(const rvc_moe_weights *w, const void *x, int x_dtype, const f
     float *lg = logits ? logits : at<float>(workspace, L.logits);
     int32_t *id = ids ? ids : at<int32_t>(workspace, L.ids);
     float *wt = wts ? wts : at<float>(workspace, L.wts);
-    int rc = launch_router_logits(w, x, x_dtype, bias, bias_stride, n_tok, lg, st);
+    RouteArgs a{};
+    a.x = x, a.w = w->router, a.bias = bias, a.bias_stride = bias_stride;
+    a.n_tok = n_tok, a.n_experts = w->n_experts, a.n_embd = w->n_embd, a.used = w->used;
+    a.lexact = lg, a.status = at<int>(workspace, L.status);
+    int rc = launch_chains(a, x_dtype, w->router_dtype, st);  // exact-order logits
     if (rc) return rc;
-    rc = launch_select_quant(w, lg, x, x_dtype, n_tok, id, wt, nullptr, nullptr, nullptr, st);
+    rc = launch_select(w, lg, n_tok, id, wt, st);
     if (rc) return rc;
     if (hist || perm) {
         const int pairs = n_tok * w->used;
@@ -424,7 +527,8 @@ int rvc_moe_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype,
         return (int)cudaErrorInvalidValue;
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
     Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
-    return run_experts(w, x_expert, x_dtype, ids, wts, n_tok, out, workspace, L, false, S(stream));
+    return run_experts(w, x_expert, x_dtype, ids, nullptr, wts, n_tok, out, workspace, L, false, false, nullptr,
+                       S(stream));
 }
 
 int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
@@ -435,18 +539,43 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
         (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
-    if (n_tok * w->used > DECODE_MAX_PAIRS) return RVC_ERR_UNSUPPORTED;
+    if (n_tok * w->used > DECODE_MAX_PAIRS || n_tok > RF_MAX_TOK) return RVC_ERR_UNSUPPORTED;
     Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
     cudaStream_t st = S(stream);
-    float *lg = at<float>(workspace, L.logits);
     int32_t *id = ids ? ids : at<int32_t>(workspace, L.ids);
     float *wt = wts ? wts : at<float>(workspace, L.wts);
-    int rc = launch_router_logits(w, x_router, x_dtype, bias, bias_stride, n_tok, lg, st);
+    int *status = at<int>(workspace, L.status);
+    uint8_t *hdr = static_cast<uint8_t *>(workspace);
+    SideLane *lane = nullptr;
+    int rc = side_lane(&lane);
     if (rc) return rc;
-    rc = launch_select_quant(w, lg, x_expert, x_dtype, n_tok, id, wt, at<int8_t>(workspace, L.xq),
-                             at<float>(workspace, L.xd), at<int32_t>(workspace, L.xs), st);
-    if (rc) return rc;
-    return run_experts(w, x_expert, x_dtype, id, wt, n_tok, out, workspace, L, true, st);
+    std::lock_guard<std::mutex> lock(lane->mu);
+    // K0 on the side lane: exact-order logits, selection and the combine weights
+    if ((rc = (int)cudaEventRecord(lane->fork, st))) return rc;
+    if ((rc = (int)cudaStreamWaitEvent(lane->stream, lane->fork, 0))) return rc;
+    RouteArgs a0{};
+    a0.x = x_router, a0.w = w->router, a0.bias = bias, a0.bias_stride = bias_stride;
+    a0.n_tok = n_tok, a0.n_experts = w->n_experts, a0.n_embd = w->n_embd, a0.used = w->used;
+    a0.lexact = at<float>(workspace, L.lexact0);
+    a0.done_cnt = reinterpret_cast<unsigned *>(hdr + 4);
+    a0.ids = at<int32_t>(workspace, L.ids_exact), a0.wts = wt, a0.status = status;
+    if ((rc = launch_chains(a0, x_dtype, w->router_dtype, lane->stream))) return rc;
+    if ((rc = (int)cudaEventRecord(lane->join, lane->stream))) return rc;
+    // K1 on the caller's stream: verified ids, Q8_0 of x and the plan
+    RouteArgs a1 = a0;
+    a1.x = x_router;
+    a1.lfast = at<float>(workspace, L.logits), a1.lbound = at<float>(workspace, L.lbound);
+    a1.lexact = at<float>(workspace, L.lexact1);
+    a1.done_cnt = reinterpret_cast<unsigned *>(hdr + 8);
+    a1.fallback_cnt = reinterpret_cast<unsigned *>(hdr + 12);
+    a1.ids = id, a1.wts = nullptr;
+    a1.plan = PlanOut{at<int32_t>(workspace, L.counts), at<int32_t>(workspace, L.offsets),
+                      at<int32_t>(workspace, L.order), at<int32_t>(workspace, L.pos_of),
+                      at<int32_t>(workspace, L.active), at<int32_t>(workspace, L.n_active)};
+    if (x_router == x_expert) a1.xrec = at<uint8_t>(workspace, L.xrec);
+    if ((rc = launch_route_fast(a1, x_dtype, w->router_dtype, st))) return rc;
+    return run_experts(w, x_expert, x_dtype, id, at<int32_t>(workspace, L.ids_exact), wt, n_tok, out, workspace, L,
+                       x_router == x_expert, true, lane->join, st);
 }
 
 int rvc_workspace_reset(void *workspace, void *stream) {
@@ -529,3 +658,14 @@ extern "C" int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_r
     return rvc_moe_forward(w, x_router, x_expert, x_dtype, bias, bias_stride, n_tok, out, ids, wts, scratch,
                            RVC_NOALLOC_SCRATCH_BYTES, stream);
 }
+
+#ifdef RVC_PROFILE
+// Profiling builds only: copy (and clear) the phase timestamps recorded by RVC_MARK.
+extern "C" int rvc_profile_dump(void *host, size_t bytes) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(host, rvc::g_prof, bytes);
+    static unsigned long long zero[8][1024][8];
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(rvc::g_prof, zero, sizeof zero);
+    return (int)e;
+}
+#endif

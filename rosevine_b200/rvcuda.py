@@ -259,7 +259,7 @@ def moe_forward(w: MoeWeights, x_router, x_expert, x_dtype: int, n_tok: int, out
                                 stream))
 
 
-NOALLOC_SCRATCH_BYTES = 1 << 20
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 def moe_forward_noalloc(w: MoeWeights, x_router, x_expert, x_dtype: int, n_tok: int, out, bias=None,
