@@ -55,24 +55,45 @@ def measured_peaks() -> dict:
 
 
 # ------------------------------------------------------------------- clocks
+def gpu_smi_id(local_rank: int) -> str:
+    """nvidia-smi --id for the CUDA device local_rank: its UUID (independent of
+    CUDA_VISIBLE_DEVICES renumbering), else its index."""
+    import torch
+    u = getattr(torch.cuda.get_device_properties(local_rank), "uuid", None)
+    if u is not None:
+        u = str(u)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return vis.split(",")[local_rank] if vis else str(local_rank)
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
+    def __init__(self, gpu_id: str):
+        self.idx = gpu_id  # "GPU-<uuid>" of the device under test (or an nvidia-smi index)
         self.proc = None
         self.path = os.path.join("/tmp", f"rvc_clocks_{os.getpid()}.csv")
 
     def start(self):
+        """Start sampling every 20 ms and wait (up to 5 s) until the first sample is written,
+        so that the timed region that follows is covered from its start."""
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.01)
+        self.t_start = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -233,8 +254,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.barrier()
         return {b: per_b[b] / steps for b in SWEEP}  # ms per call
 
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank])
-                          if os.environ.get("CUDA_VISIBLE_DEVICES") else local_rank)
+    clocks = ClockSampler(gpu_smi_id(local_rank))
     clocks.start()
     per_b = timed_loop(step_graph, args.steps, args.warmup)
     clk = clocks.stop()
@@ -281,16 +301,15 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "tokens_per_step": tokens, "l2": "flushed (256 MB write) before every timed layer call",
                    "parallelism": "replicas" if world > 1 else "single GPU"},
         "decode": {"b1_us_per_token": per_b[1] * 1e3, "b1_hbm_gbs": decode[0]["hbm_gbs"], "per_b": decode},
-        "roofline": {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_router_chains || k_route_fast, "
-                                                "k_gate_up_decode, k_down_combine_decode), bytes and time summed "
-                                                "over the sweep",
+        "roofline": {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_fd_route, k_fd_gate, k_fd_down), "
+                                                "algorithmic bytes and device time summed over the sweep",
                      "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                      "expert_phase_gbs": ph_gbs, "expert_phase_frac": ph_gbs / peaks["hbm_gbs"],
                      "traffic": None},
         "e2e": {"value": world * tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 4 * len(SWEEP) * args.steps,
+        "gpu_launches": 3 * len(SWEEP) * args.steps,  # k_fd_route, k_fd_gate, k_fd_down per layer call
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu:
@@ -335,7 +354,7 @@ def run_reference(args, rank: int) -> dict | None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)

@@ -6,13 +6,24 @@
 // this backend splits each block into a 16-byte nibble plane and an f16 scale plane (so every
 // copy is 16-byte aligned for TMA and every row of nibbles is one contiguous run), and
 // interleaves gate and up rows per 32 columns:
-//   packed gate_up row R = q*64 + s*32 + i  holds  original row s*ff + q*32 + i.
+//   packed gate_up row R = q*64 + s*32 + i  holds  original row s*ff + q*32 + i,
+// and within a gate_up row the 16-byte nibble block b sits at position b ^ (R & 7) (so that
+// 32 threads reading block b of 32 consecutive rows hit distinct shared-memory banks; rows
+// hold a multiple of 8 blocks). Scales are not swizzled.
 // Nibble bytes and scale bits are copied unchanged, so every dot product sees the same
 // integers and scales as the reference.
 #pragma once
 #include "common.cuh"
 
 namespace rvc {
+
+// Packed expert planes (byte offsets inside the packed buffer are computed on the host).
+struct PackedView {
+    const uint8_t *gu_nib;   // [E][2*ff packed rows][nb][16]
+    const uint16_t *gu_scl;  // [E][2*ff][nb]
+    const uint8_t *dn_nib;   // [E][n_embd][nbh][16]
+    const uint16_t *dn_scl;  // [E][n_embd][nbh]
+};
 
 __global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int rows, int nblk, bool interleave_gu,
                           int ff, uint8_t *__restrict__ nib, uint16_t *__restrict__ scl) {
@@ -28,12 +39,14 @@ __global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int ro
         }
         const uint8_t *blk = src + i * Q4_BLOCK;
         const size_t dst = (e * rows + prow) * nblk + b;
+        // gate/up nibble blocks are XOR-swizzled within a row: block b at position b ^ (prow & 7)
+        const size_t dnib = interleave_gu ? (e * rows + prow) * nblk + (b ^ (prow & 7)) : dst;
         // 18-byte blocks are only 2-byte aligned: read as 9 halfwords
         const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
-        *reinterpret_cast<uint4 *>(nib + dst * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(nib + dnib * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         scl[dst] = h[0];
     }
 }

@@ -79,7 +79,7 @@ __device__ __forceinline__ void warp_select(const float *lg, int n_experts, int 
     for (int i = 0; i < PER; ++i) {
         const int e = lane + 32 * i;
         if (e < n_experts) {
-            v[i] = (float)exp((double)__fsub_rn(v[i], mx));
+            v[i] = fd_exp_f32(__fsub_rn(v[i], mx));
             sum += (double)v[i];
         }
     }

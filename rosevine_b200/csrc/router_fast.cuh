@@ -1,33 +1,25 @@
-// router_fast.cuh - decode-latency routing: exact-order chains (K0) and a verified fast router (K1).
+// router_fast.cuh - the reference's exact router order, and the bound that lets a fast router skip it.
 //
 // The reference router is a sequential f32 dot per (token, expert) (matvec_f32,
-// runtime/src/ops.rs:321-326), so its logits carry that order's rounding. Two kernels
-// reproduce its selection (exec.rs:507-517) without putting a 2816-step dependent chain in
-// front of the expert GEMVs:
+// runtime/src/ops.rs:321-326), so its logits carry that order's rounding.
 //
-// K0 k_router_chains: the exact chains themselves, one per thread, with whole rows of the
-//    router and of x staged into shared memory by a few large 1-D TMA bulk copies. Logits are
-//    bit-identical to the reference; the last CTA selects (softmax, top-k, renormalised
-//    weights) - these are the weights the combine uses. It runs on a side branch, concurrently
-//    with K1 and the gate/up GEMV.
-// K1 k_route_fast: every (token, expert) dot in parallel in f64 (the products of bf16/f32
-//    operands are exact in f64), plus a rigorous bound on how far the sequential f32 result
-//    can be from it: |s_seq - S| <= u * (sum_i |S_i| + sum_i |p_i|) * (1 + 1e-2), S_i the
-//    exact prefix sums (Higham, Accuracy and Stability of Numerical Algorithms, 2nd ed.,
-//    eq. 4.4 with products rounded once), plus the rounding of the bias add and of the f32
-//    store. A token whose top-(used+1) are separated by more than their bounds has the same
-//    ids in the reference; any other token gets its logits from exact chains inside K1 (about
-//    3% of tokens at the benchmark's distributions). K1 also quantises x to Q8_0 and builds
-//    the dispatch plan, so the expert kernels can start as soon as it ends.
+// k_router_chains: the exact chains themselves, one per thread, with whole rows of the router
+//    and of x staged into shared memory by a few large 1-D TMA bulk copies. Logits are
+//    bit-identical to the reference (rvc_moe_router returns them); with a done counter the
+//    last CTA also selects (softmax, top-k, renormalised weights: block_select).
+// The decode kernel (decode_fused.cuh) instead forms every (token, expert) dot in f64 (the
+//    products of bf16/f32 operands are exact in f64) together with a rigorous bound on how far
+//    the sequential f32 result can be from it: |s_seq - S| <= u * (sum_i |S_i| + sum_i |p_i|)
+//    * (1 + 1e-2), S_i the exact prefix sums (Higham, Accuracy and Stability of Numerical
+//    Algorithms, 2nd ed., eq. 4.4 with products rounded once), plus the rounding of the bias
+//    add and of the f32 store (RF_U below). A token whose top-(used+1) are separated by more
+//    than their bounds has the same ids in the reference; any other token gets its logits from
+//    exact chains (chain_streamed) - about 3% of tokens at the benchmark's distributions.
 #pragma once
 #include "common.cuh"
 #include "router.cuh"
 
 namespace rvc {
-
-struct PlanOut {
-    int32_t *counts, *offsets, *order, *pos_of, *active, *n_active;
-};
 
 struct RouteArgs {
     const void *x;
@@ -35,18 +27,12 @@ struct RouteArgs {
     const float *bias;
     int bias_stride;
     int n_tok, n_experts, n_embd, used;
-    float *lfast, *lbound;  // [n_tok][n_experts] (K1)
-    float *lexact;          // [n_tok][n_experts] exact logits (K0; K1 fallback)
-    uint8_t *xrec;          // Q8_0 records of x (K1), may be NULL
-    unsigned *done_cnt;     // last-CTA counter (zero between launches)
-    unsigned *fallback_cnt; // (K1) cumulative count of tokens routed through the exact fallback
+    float *lexact;          // [n_tok][n_experts] exact logits
+    unsigned *done_cnt;     // last-CTA counter (zero between launches), or NULL: no selection
     int32_t *ids;           // [n_tok][used]
-    float *wts;             // [n_tok][used] (K0)
-    PlanOut plan;           // (K1)
+    float *wts;             // [n_tok][used]
     int *status;
 };
-
-constexpr int RF_MAX_TOK = 64;  // decode tokens per call
 
 template <typename T>
 __device__ __forceinline__ void lds8(const T *p, float v[8]);
@@ -127,7 +113,7 @@ __device__ void block_select(const float *lg, int ne, int used, int32_t *ids, fl
     m = block_max(m, sc.redf);
     double sum = 0.0;
     for (int e = tid; e < ne; e += nth) {
-        const float ex = (float)exp((double)__fsub_rn(sc.p[e], m));
+        const float ex = fd_exp_f32(__fsub_rn(sc.p[e], m));
         sc.p[e] = ex;
         sum += (double)ex;
     }
@@ -211,7 +197,7 @@ __global__ void __launch_bounds__(128) k_router_chains(RouteArgs a, int tpc) {
     float s = -0.0f;
     bool ok = true;
     for (int c = 0; c < C0_CHUNKS; ++c) {
-        if (!mbar_wait(&bars[c], 0, a.status)) ok = false;
+        if (!fd_mbar_wait(&bars[c], 0, a.status)) ok = false;
         if (c == 0) RVC_MARK(0, 1);
         if (active && ok) {
             const WT *wr = reinterpret_cast<const WT *>(smem + el * wrow) + c * ck;
@@ -285,246 +271,6 @@ __device__ float chain_streamed(const WT *wrow, const float *xs, int n) {
     return s;
 }
 
-// Dispatch plan (MoePlan, exec.rs:541-557) of n_pairs <= RF_MAX_TOK * MAX_USED pairs inside one
-// CTA, by ranks: a pair's plan position is the number of pairs with a smaller expert plus the
-// number of earlier pairs with the same expert. ids in shared memory.
-__device__ void rank_plan(const int32_t *s_ids, int n_pairs, int n_experts, PlanOut p, int *s_count, int *s_base) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nth = blockDim.x;
-    for (int e = tid; e < MAX_EXPERTS; e += nth) {
-        int c = 0;
-        if (e < n_experts)
-            for (int q = 0; q < n_pairs; ++q) c += s_ids[q] == e;
-        s_count[e] = c;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        constexpr int PL = MAX_EXPERTS / 32;
-        int run = 0, flags = 0;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane * PL + i;
-            run += e < n_experts ? s_count[e] : 0;
-            flags += (e < n_experts && s_count[e] > 0);
-        }
-        int incl = run, fin = flags;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o), z = __shfl_up_sync(0xffffffffu, fin, o);
-            if (lane >= o) incl += y, fin += z;
-        }
-        int base = incl - run, slot = fin - flags;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = lane * PL + i;
-            if (e < n_experts) {
-                s_base[e] = base;
-                p.offsets[e] = base;
-                p.counts[e] = s_count[e];
-                if (s_count[e] > 0) p.active[slot++] = e;
-                base += s_count[e];
-            }
-        }
-        if (lane == 31) {
-            p.offsets[n_experts] = incl;
-            *p.n_active = fin;
-        }
-    }
-    __syncthreads();
-    for (int q = tid; q < n_pairs; q += nth) {
-        const int e = s_ids[q];
-        int k = s_base[e];
-        for (int r = 0; r < q; ++r) k += s_ids[r] == e;
-        p.order[k] = q;
-        p.pos_of[q] = k;
-    }
-}
-
-// ------------------------------------------------------------------ K1
-constexpr int RF_THREADS = 256;
 constexpr double RF_U = 5.9604644775390625e-08;  // 2^-24, unit roundoff of f32
-
-struct VerifyScratch {
-    int32_t key[MAX_EXPERTS];
-    float l[MAX_EXPERTS], bd[MAX_EXPERTS];
-    int top[MAX_USED + 1];
-    float redf[32];
-};
-
-// grid: min(n_experts, #SMs) CTAs, 256 threads; dynamic smem: one x row as f32 (fallback).
-// The lane K chunk is NB8 groups of 8 elements (n_embd = 256 * NB8); each group's f64 sums are
-// formed separately so every dependent chain is short (8 products, then NB8 group sums).
-template <typename XT, typename WT, int NB8>
-__global__ void __launch_bounds__(RF_THREADS) k_route_fast(RouteArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];  // fallback: one x row as f32
-    __shared__ int s_last, s_nflag;
-    __shared__ int s_flag[RF_MAX_TOK];
-    __shared__ int32_t s_ids[RF_MAX_TOK * MAX_USED];
-    __shared__ int s_count[MAX_EXPERTS], s_base[MAX_EXPERTS];
-    __shared__ union {
-        VerifyScratch v;
-        SelScratch s;
-    } sc;
-    RVC_MARK(1, 0);
-    const XT *x = static_cast<const XT *>(a.x);
-    const WT *w = static_cast<const WT *>(a.w);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ne = a.n_experts;
-    constexpr int chunk = NB8 * 8;
-
-    // 1. every (token, expert) dot in f64 with its bound; warp per dot, lane per K chunk
-    for (int e = blockIdx.x; e < ne; e += gridDim.x) {
-        for (int t = warp; t < a.n_tok; t += RF_THREADS / 32) {
-            const WT *wr = w + (size_t)e * a.n_embd + (size_t)lane * chunk;
-            const XT *xr = x + (size_t)t * a.n_embd + (size_t)lane * chunk;
-            // pass 1: per-group f64 sums (exact-ish) and sum |p| (f32 is enough for a bound)
-            double gsum[NB8];
-            float P = 0.0f;
-#pragma unroll
-            for (int g = 0; g < NB8; ++g) {
-                float wv[8], xv[8];
-                ld8<WT>(wr, g * 8, wv);
-                ld8<XT>(xr, g * 8, xv);
-                double s8 = 0.0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const double p = (double)wv[j] * (double)xv[j];
-                    s8 += p;
-                    P += fabsf(wv[j] * xv[j]);
-                }
-                gsum[g] = s8;
-            }
-            double c = 0.0;
-            float gpre[NB8];
-#pragma unroll
-            for (int g = 0; g < NB8; ++g) gpre[g] = (float)c, c += gsum[g];
-            double incl = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const double y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            const float off = (float)(incl - c);
-            // pass 2: sum over the prefix sums |S_i| (f32; relative error far inside the 1% margin)
-            float A = 0.0f;
-#pragma unroll 1
-            for (int g = 0; g < NB8; ++g) {
-                float wv[8], xv[8];
-                ld8<WT>(wr, g * 8, wv);
-                ld8<XT>(xr, g * 8, xv);
-                float r = off + gpre[g], ag = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    r += wv[j] * xv[j];
-                    ag += fabsf(r);
-                }
-                A += ag;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                A += __shfl_xor_sync(0xffffffffu, A, o);
-                P += __shfl_xor_sync(0xffffffffu, P, o);
-            }
-            const double S = __shfl_sync(0xffffffffu, incl, 31);
-            if (lane == 0) {
-                const double b = a.bias ? (double)__ldg(a.bias + (size_t)t * a.bias_stride + e) : 0.0;
-                const double l = S + b;
-                const double bd = 1.02 * RF_U * ((double)A + (double)P) + 2.02 * RF_U * (fabs(S) + fabs(b)) + 1e-30;
-                a.lfast[(size_t)t * ne + e] = (float)l;
-                a.lbound[(size_t)t * ne + e] = (float)(bd * 1.001);
-            }
-        }
-    }
-    RVC_MARK(1, 1);
-    // 2. Q8_0 of x, spread over every warp of the grid
-    if (a.xrec) {
-        const int nb = a.n_embd / QK;
-        const long long total = (long long)a.n_tok * nb;
-        for (long long i = (long long)blockIdx.x * (RF_THREADS / 32) + warp; i < total;
-             i += (long long)gridDim.x * (RF_THREADS / 32)) {
-            const long long t = i / nb, b = i % nb;
-            const float v = ld_val<XT>(x, (size_t)t * a.n_embd + (size_t)b * QK + lane);
-            uint16_t dbits;
-            int qsum;
-            const int8_t q = quant_q8_lane(v, &dbits, &qsum);
-            q8rec_store(a.xrec + (size_t)t * q8rec_bytes(nb), nb, (int)b, lane, q, dbits, qsum);
-        }
-    }
-    // 3. the last CTA verifies, falls back, selects and plans
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        s_last = atomicAdd(a.done_cnt, 1u) == gridDim.x - 1;
-        s_nflag = 0;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    RVC_MARK(1, 2);
-    const int used = a.used;
-    for (int t = 0; t < a.n_tok; ++t) {
-        VerifyScratch &v = sc.v;
-        float mo = -INFINITY;
-        for (int e = tid; e < ne; e += RF_THREADS) {
-            v.l[e] = __ldcg(a.lfast + (size_t)t * ne + e);
-            v.bd[e] = __ldcg(a.lbound + (size_t)t * ne + e);
-            v.key[e] = total_key(v.l[e]);
-        }
-        __syncthreads();
-        for (int e = tid; e < ne; e += RF_THREADS) {
-            const int32_t k = v.key[e];
-            int rank = 0;
-            for (int f = 0; f < ne; ++f) rank += (v.key[f] > k) | ((v.key[f] == k) & (f < e));
-            if (rank < used)
-                v.top[rank] = e;
-            else
-                mo = fmaxf(mo, v.l[e] + v.bd[e]);  // every expert left out, with its bound
-        }
-        mo = block_max(mo, v.redf);
-        if (tid == 0) {
-            bool ok = true;
-            const float l0 = v.l[v.top[0]];
-            for (int j = 0; j < used; ++j) {
-                const int ej = v.top[j];
-                const float lo = v.l[ej] - v.bd[ej];
-                // strictly above the next pick (or, for the last pick, every expert left out)
-                const bool last = j + 1 == used;
-                const float hi = last ? mo : v.l[v.top[j + 1]] + v.bd[v.top[j + 1]];
-                const float nxt = last ? mo : v.l[v.top[j + 1]];
-                if (!(lo > hi + 1e-6f * (1.0f + fabsf(nxt - l0)))) ok = false;
-                if (!(v.l[ej] - l0 > -80.0f)) ok = false;  // far from underflow in softmax
-                s_ids[t * used + j] = ej;
-            }
-            s_flag[t] = !ok;
-            if (!ok) ++s_nflag;
-        }
-        __syncthreads();
-    }
-    RVC_MARK(1, 3);
-    if (tid == 0 && a.fallback_cnt && s_nflag > 0) atomicAdd(a.fallback_cnt, (unsigned)s_nflag);
-    if (s_nflag > 0) {
-        // exact chains for the ambiguous tokens, one token at a time: x staged in shared memory
-        // as f32, one thread per expert streaming its router row from L2
-        float *xs = reinterpret_cast<float *>(smem);
-        for (int t = 0; t < a.n_tok; ++t) {
-            if (!s_flag[t]) continue;
-            for (int k = tid; k < a.n_embd; k += RF_THREADS) xs[k] = ld_val<XT>(x, (size_t)t * a.n_embd + k);
-            __syncthreads();
-            for (int e = tid; e < ne; e += RF_THREADS) {
-                float v = chain_streamed<XT, WT>(w + (size_t)e * a.n_embd, xs, a.n_embd);
-                if (a.bias) v = __fadd_rn(v, __ldg(a.bias + (size_t)t * a.bias_stride + e));
-                a.lexact[(size_t)t * ne + e] = v;
-            }
-            __syncthreads();
-            block_select(a.lexact + (size_t)t * ne, ne, used, s_ids + t * used, nullptr, sc.s);
-        }
-    }
-    __syncthreads();
-    const int n_pairs = a.n_tok * used;
-    for (int q = tid; q < n_pairs; q += RF_THREADS) a.ids[q] = s_ids[q];
-    RVC_MARK(1, 4);
-    rank_plan(s_ids, n_pairs, ne, a.plan, s_count, s_base);
-    if (tid == 0) *a.done_cnt = 0;
-    RVC_MARK(1, 5);
-}
 
 }  // namespace rvc

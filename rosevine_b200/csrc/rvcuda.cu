@@ -13,7 +13,7 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "experts_decode.cuh"
+#include "decode_fused.cuh"
 #include "pack.cuh"
 #include "router.cuh"
 #include "router_fast.cuh"
@@ -59,11 +59,13 @@ PackedView packed_view(const rvc_moe_weights *w) {
 
 // Workspace carve-up for calls of up to max_tok tokens.
 struct Workspace {
-    // header (first 256 B, cleared by rvc_workspace_reset): int status at 0, the K0 and K1
-    // last-CTA counters at 4 and 8 (each kernel returns its counter to zero), and at 12 the
-    // running count of tokens the fast router sent to its exact fallback.
-    size_t status, logits, lbound, lexact0, lexact1, ids, ids_exact, wts, xrec, counts, offsets, order, pos_of,
-        active, n_active, hrec, ybuf, total;
+    // header (first 256 B, cleared by rvc_workspace_reset): int status at 0, the router's
+    // last-CTA counter at 4, at 12 the running count of tokens routed through the exact
+    // fallback, and the decode kernel's grid barrier: arrival count at 64, generation at 128
+    // (separate cache lines; the count returns to zero after every barrier).
+    size_t status, lfast, lbound, lexact, ids, wts, sel_ids, sel_wts, sel_flag, xrec, hrec, ybuf, plan, counts,
+        offsets, order, pos_of, active, n_active, total;
+    static constexpr size_t HDR_FALLBACK = 12, HDR_BAR_CNT = 64, HDR_BAR_GEN = 128;
     Workspace(int max_tok, int n_embd, int ff, int ne, int used) {
         const size_t nb = n_embd / QK, nbh = ff / QK, pairs = (size_t)max_tok * used;
         size_t o = 0;
@@ -73,22 +75,24 @@ struct Workspace {
             return at;
         };
         status = take(256);
-        logits = take((size_t)max_tok * ne * 4);
+        lfast = take((size_t)max_tok * ne * 4);
         lbound = take((size_t)max_tok * ne * 4);
-        lexact0 = take((size_t)max_tok * ne * 4);
-        lexact1 = take((size_t)max_tok * ne * 4);
+        lexact = take((size_t)max_tok * ne * 4);
         ids = take(pairs * 4);
-        ids_exact = take(pairs * 4);
         wts = take(pairs * 4);
+        sel_ids = take(pairs * 4);
+        sel_wts = take(pairs * 4);
+        sel_flag = take((size_t)max_tok * 4);
         xrec = take((size_t)max_tok * q8rec_bytes((int)nb));
+        hrec = take(pairs * q8rec_bytes((int)nbh));
+        ybuf = take((size_t)std::min(max_tok, FD_MAX_TOK) * used * n_embd * 4);  // decode calls only
+        plan = take(fd_plan_words(std::min(max_tok, FD_MAX_TOK) * used, ne) * 4);
         counts = take((size_t)ne * 4);
         offsets = take((size_t)(ne + 1) * 4);
         order = take(pairs * 4);
         pos_of = take(pairs * 4);
         active = take((size_t)ne * 4);
         n_active = take(4);
-        hrec = take(pairs * q8rec_bytes((int)nbh));
-        ybuf = pairs > (size_t)DN_MAX_PAIRS ? take(pairs * n_embd * 4) : o;  // y of the expert-major path
         total = o;
     }
 };
@@ -110,8 +114,6 @@ int ws_max_tok(size_t bytes, const rvc_moe_weights *w) {
     }
     return lo;
 }
-
-constexpr int DECODE_MAX_PAIRS = 512;  // pairs per call on the decode kernels
 
 // Opt a kernel into the dynamic shared memory it needs beyond the default 48 KB: the opt-in
 // limit is the device's per-block maximum minus the kernel's static shared memory. Done once
@@ -170,64 +172,6 @@ int launch_chains(const RouteArgs &a, int x_dtype, int w_dtype, cudaStream_t st)
     return launch_chains_t<float, float>(a, st);
 }
 
-// K1: verified fast router + Q8_0 of x + plan (n_tok <= RF_MAX_TOK), templated on n_embd / 256.
-template <typename XT, typename WT, int NB8>
-int launch_route_fast_n(RouteArgs a, cudaStream_t st) {
-    const size_t smem = (size_t)a.n_embd * sizeof(float);  // fallback: one x row (below 48 KB)
-    k_route_fast<XT, WT, NB8><<<std::min(a.n_experts, num_sms()), RF_THREADS, smem, st>>>(a);
-    return launched();
-}
-
-template <typename XT, typename WT>
-int launch_route_fast_t(RouteArgs a, cudaStream_t st) {
-    switch (a.n_embd / 256) {
-        case 1: return launch_route_fast_n<XT, WT, 1>(a, st);
-        case 2: return launch_route_fast_n<XT, WT, 2>(a, st);
-        case 4: return launch_route_fast_n<XT, WT, 4>(a, st);
-        case 8: return launch_route_fast_n<XT, WT, 8>(a, st);
-        case 11: return launch_route_fast_n<XT, WT, 11>(a, st);
-        case 16: return launch_route_fast_n<XT, WT, 16>(a, st);
-        default: return RVC_ERR_UNSUPPORTED;
-    }
-}
-
-int launch_route_fast(const RouteArgs &a, int x_dtype, int w_dtype, cudaStream_t st) {
-    const bool xb = x_dtype == RVC_BF16, wb = w_dtype == RVC_BF16;
-    if (xb && wb) return launch_route_fast_t<uint16_t, uint16_t>(a, st);
-    if (xb) return launch_route_fast_t<uint16_t, float>(a, st);
-    if (wb) return launch_route_fast_t<float, uint16_t>(a, st);
-    return launch_route_fast_t<float, float>(a, st);
-}
-
-// Per-device side stream and fork/join events for K0, which runs beside K1 and the gate/up
-// GEMV. The mutex keeps one caller's record/wait pairs together.
-struct SideLane {
-    std::mutex mu;
-    cudaStream_t stream = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-};
-SideLane g_side[64];
-
-int side_lane(SideLane **out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    SideLane &L = g_side[dev];
-    if (!L.stream) {
-        std::lock_guard<std::mutex> lock(L.mu);
-        if (!L.stream) {
-            cudaStream_t s;
-            if ((e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return (int)e;
-            if ((e = cudaEventCreateWithFlags(&L.fork, cudaEventDisableTiming)) != cudaSuccess) return (int)e;
-            if ((e = cudaEventCreateWithFlags(&L.join, cudaEventDisableTiming)) != cudaSuccess) return (int)e;
-            L.stream = s;
-        }
-    }
-    *out = &L;
-    return 0;
-}
-
 int launch_select(const rvc_moe_weights *w, const float *logits, int n_tok, int32_t *ids, float *wts,
                   cudaStream_t st) {
     k_select<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, n_tok, w->n_experts, w->used, ids, wts, nullptr);
@@ -236,24 +180,7 @@ int launch_select(const rvc_moe_weights *w, const float *logits, int n_tok, int3
 
 }  // namespace
 
-// Quantise rows of x to the Q8 planes (used when ids come from the caller).
 namespace rvc {
-template <typename XT>
-__global__ void __launch_bounds__(256) k_quant_rows(const XT *__restrict__ x, int n_tok, int n_embd,
-                                                    uint8_t *__restrict__ xrec) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = n_embd / QK;
-    const long long total = (long long)n_tok * nb;
-    for (long long i = (long long)blockIdx.x * 8 + warp; i < total; i += (long long)gridDim.x * 8) {
-        const long long t = i / nb, b = i % nb;
-        const float v = ld_val<XT>(x, (size_t)t * n_embd + (size_t)b * QK + lane);
-        uint16_t dbits;
-        int qsum;
-        const int8_t q = quant_q8_lane(v, &dbits, &qsum);
-        q8rec_store(xrec + (size_t)t * q8rec_bytes(nb), nb, (int)b, lane, q, dbits, qsum);
-    }
-}
-
 // Block sums for the debug hook: one thread per (input, row, block), reading the packed planes
 // and the reference-format Q8_0 activation blocks, through the same q4q8_sumi as the kernels.
 __global__ void k_debug_block_sums(PackedView pk, int which, int expert, int n_embd, int ff,
@@ -275,7 +202,7 @@ __global__ void k_debug_block_sums(PackedView pk, int which, int expert, int n_e
         if (which == 0) {
             const int s = row / ff, col = row % ff;
             const int prow = (col / 32) * 64 + s * 32 + (col % 32);
-            nibp = pk.gu_nib + (((size_t)expert * 2 * ff + prow) * nblk + b) * 16;
+            nibp = pk.gu_nib + (((size_t)expert * 2 * ff + prow) * nblk + (b ^ (prow & 7))) * 16;
         } else {
             nibp = pk.dn_nib + (((size_t)expert * n_embd + row) * nblk + b) * 16;
         }
@@ -299,83 +226,184 @@ __global__ void k_debug_block_sums(PackedView pk, int which, int expert, int n_e
 
 namespace {
 
-// Expert GEMVs for n_tok <= 64 tokens: (Q8_0 of x,) plan, gate/up, down + combine.
-// quantised: x already in the workspace's Q8 planes; planned: the plan is already built.
-// ids_check: exact-order ids the combine verifies against (may be NULL). join: an event the
-// stream waits for before the down/combine kernel (the exact weights), or NULL.
-int run_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids,
-                const int32_t *ids_check, const float *wts, int n_tok, float *out, void *ws, const Workspace &L,
-                bool quantised, bool planned, cudaEvent_t join, cudaStream_t st) {
-    const int pairs = n_tok * w->used;
-    const int nb = w->n_embd / QK, nbh = w->ff / QK;
-    if (pairs > DECODE_MAX_PAIRS || nbh % 2) return RVC_ERR_UNSUPPORTED;
-    int rc;
-    uint8_t *xrec = at<uint8_t>(ws, L.xrec), *hrec = at<uint8_t>(ws, L.hrec);
-    if (!quantised) {
-        const int blocks = std::min(1184, (int)(((long long)n_tok * nb + 7) / 8));
-        if (x_dtype == RVC_BF16)
-            k_quant_rows<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)x_expert, n_tok, w->n_embd, xrec);
-        else
-            k_quant_rows<float><<<blocks, 256, 0, st>>>((const float *)x_expert, n_tok, w->n_embd, xrec);
-        if ((rc = launched())) return rc;
+// Shared-memory plans of k_fd_route, k_fd_gate and k_fd_down for a call (FdLayout); false if
+// the shapes do not fit. xs, ws: element sizes of the router input and router weight.
+// smax_*: the largest dynamic shared memory each kernel may use.
+bool fd_layout(int n_tok, int used, int n_embd, int ff, int ne, int G, size_t smax_gate, size_t smax_down, int xs,
+               int ws, FdLayout *out) {
+    FdLayout L{};
+    const int nb = n_embd / QK, nbh = ff / QK, pairs = n_tok * used;
+    const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
+    auto r128 = [](size_t x) { return (uint32_t)((x + 127) & ~size_t(127)); };
+    if (ne > FD_MAX_EXPERTS || used > MAX_USED || n_tok > FD_MAX_TOK || pairs > FD_MAX_PAIRS) return false;
+    // k_fd_route: two item buffers (router row + FD_TB x rows)
+    L.r_bytes = 2 * r128((size_t)n_embd * (ws + FD_TB * xs));
+    // k_fd_gate: ring of gate/up slots, two x-record buffers, a wave's dots, the plan
+    L.slot_bytes = FD_ROWS * nb * 18;
+    L.act_bytes = r128((size_t)xrb * std::min(n_tok, 2));
+    L.act_x = L.act_bytes / xrb;
+    const uint32_t gu = r128((size_t)(FD_MAX_SLOTS / 2) * L.act_x * 2 * 32 * 4);
+    const uint32_t plan = r128((size_t)pairs * 5 * 4 + (size_t)(3 * ne + 1) * 4);
+    const size_t fixed = 2 * (size_t)L.act_bytes + gu + plan;
+    if (smax_gate < fixed + 2 * (size_t)L.slot_bytes) return false;
+    L.nslot = (int)std::min<size_t>(FD_MAX_SLOTS, (smax_gate - fixed) / L.slot_bytes);
+    const size_t ring = (size_t)L.nslot * L.slot_bytes;
+    const size_t irow = (size_t)n_embd * (xs + ws) + 32;  // one exact-chain item: both rows, padded
+    if (ring < FD_SCRATCH + irow) return false;
+    L.chain_items = (int)std::min<size_t>(FD_THREADS, (ring - FD_SCRATCH) / irow);
+    uint32_t o = (uint32_t)ring;
+    L.off_act = o, o += 2 * L.act_bytes;
+    L.off_gu = o, o += gu;
+    L.off_plan = o, o += plan;
+    L.bytes = o;
+    // k_fd_down: ring of down slots (up to eps experts' row tiles each), two h-record buffers,
+    // y (if it fits), the plan
+    int g = nbh, h = 8;  // down rows per bulk-copy-aligned group: rg * nbh * 2 % 16 == 0
+    while (h) {
+        const int t = g % h;
+        g = h, h = t;
     }
-    int *status = at<int>(ws, L.status);
-    if (!planned) {
-        k_plan<<<1, PLAN_THREADS, 0, st>>>(ids, pairs, w->n_experts, at<int32_t>(ws, L.counts),
-                                           at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.order),
-                                           at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
-                                           at<int32_t>(ws, L.n_active), status);
-        if ((rc = launched())) return rc;
-    }
-    PlanView plan{at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets), at<int32_t>(ws, L.order),
-                  at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active), at<int32_t>(ws, L.n_active)};
-    PackedView pk = packed_view(w);
-    const int max_active = std::min(w->n_experts, pairs);
-    {
-        const size_t smem = gu_smem_bytes(nb);
-        dim3 grid(w->ff / 32, max_active);
-        switch (nb / 8) {
-#define RVC_GU_CASE(NB8)                                                                                  \
-    case NB8:                                                                                             \
-        if ((rc = set_smem_attr(k_gate_up_decode<NB8>, 16 + NB8))) return rc;                            \
-        k_gate_up_decode<NB8><<<grid, 256, smem, st>>>(pk, w->ff, xrec, plan, w->used, hrec, status); \
-        break;
-            RVC_GU_CASE(1)
-            RVC_GU_CASE(2)
-            RVC_GU_CASE(4)
-            RVC_GU_CASE(8)
-            RVC_GU_CASE(11)
-            RVC_GU_CASE(16)
-#undef RVC_GU_CASE
-            default:
-                return RVC_ERR_UNSUPPORTED;
+    L.rg = 8 / g;
+    if (n_embd % L.rg) return false;
+    const int nq = n_embd / L.rg;
+    L.rpc_max = L.rg * ((nq + G - 1) / G);
+    const size_t tile_max = (size_t)L.rpc_max * nbh * 18;
+    L.d_slot_bytes = (int)r128(std::max(tile_max, (size_t)32768));
+    L.d_act_bytes = r128((size_t)hrb * std::min(pairs, 16));
+    L.act_h = L.d_act_bytes / hrb;
+    const uint32_t dplan = r128((size_t)pairs * 3 * 4 + (size_t)(3 * ne + 1) * 4);
+    const uint32_t y = r128((size_t)pairs * L.rpc_max * 4);
+    const size_t dfixed = 2 * (size_t)L.d_act_bytes + dplan;
+    if (smax_down < dfixed + 2 * (size_t)L.d_slot_bytes) return false;
+    L.y_in_smem = smax_down >= dfixed + y + 4 * (size_t)L.d_slot_bytes;
+    L.d_nslot = (int)std::min<size_t>(FD_MAX_SLOTS, (smax_down - dfixed - (L.y_in_smem ? y : 0)) / L.d_slot_bytes);
+    o = (uint32_t)L.d_nslot * L.d_slot_bytes;
+    L.d_off_act = o, o += 2 * L.d_act_bytes;
+    L.d_off_y = o, o += L.y_in_smem ? y : 0;
+    L.d_off_plan = o, o += dplan;
+    L.d_bytes = o;
+    *out = L;
+    return true;
+}
+
+// Largest dynamic shared memory a kernel may use: the device's opt-in maximum per block minus
+// the kernel's static shared memory. Also opts the kernel in, once per (kernel, device); the
+// table of kernels seen is small and guarded by a mutex.
+struct SmemOptIn {
+    const void *fn;
+    int dev;
+    size_t dyn;
+};
+SmemOptIn g_optin[256];
+int g_n_optin = 0;
+std::mutex g_optin_mu;
+
+template <typename K>
+int fd_smem_max(K kernel, size_t *out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    const void *fn = reinterpret_cast<const void *>(kernel);
+    std::lock_guard<std::mutex> lock(g_optin_mu);
+    for (int i = 0; i < g_n_optin; ++i)
+        if (g_optin[i].fn == fn && g_optin[i].dev == dev) {
+            *out = g_optin[i].dyn;
+            return 0;
         }
-        if ((rc = launched())) return rc;
-    }
-    if (pairs <= DN_MAX_PAIRS) {
-        // every h record fits in shared memory: down + slot-order combine in one kernel
-        const int nbuf = max_active > DN_BATCH ? 2 : 1;
-        const size_t smem = dn_smem_bytes(nbh, nbuf, pairs);
-        if ((rc = set_smem_attr(k_down_combine_decode, 1))) return rc;
-        if (join && (rc = (int)cudaStreamWaitEvent(st, join, 0))) return rc;
-        k_down_combine_decode<<<w->n_embd / DN_ROWS, 256, smem, st>>>(pk, w->n_embd, w->ff, hrec, plan, ids,
-                                                                      ids_check, wts, w->down_scale, n_tok, w->used,
-                                                                      nbuf, out, status);
-        if ((rc = launched())) return rc;
-    } else {
-        // expert-major down into y, then the slot-order combine
-        float *y = at<float>(ws, L.ybuf);
-        if ((rc = set_smem_attr(k_down_expert, 2))) return rc;
-        k_down_expert<<<dim3(w->n_embd / DE_ROWS, max_active), 256, de_smem_bytes(nbh), st>>>(pk, w->n_embd, w->ff,
-                                                                                            hrec, plan, y, status);
-        if ((rc = launched())) return rc;
-        if (join && (rc = (int)cudaStreamWaitEvent(st, join, 0))) return rc;
-        k_combine<<<dim3((w->n_embd + 255) / 256, n_tok), 256, 0, st>>>(y, plan.pos_of, ids, ids_check, wts,
-                                                                         w->down_scale, w->used, w->n_embd, out,
-                                                                         status);
-        if ((rc = launched())) return rc;
-    }
+    if (g_n_optin == 256) return (int)cudaErrorInvalidValue;
+    cudaFuncAttributes fa;
+    if ((e = cudaFuncGetAttributes(&fa, kernel)) != cudaSuccess) return (int)e;
+    int optin = 0;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return (int)e;
+    const int dyn = optin - (int)fa.sharedSizeBytes;
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
+        return (int)e;
+    g_optin[g_n_optin++] = SmemOptIn{fn, dev, (size_t)dyn};
+    *out = (size_t)dyn;
     return 0;
+}
+
+// The three decode kernels on `st`, each on one CTA per SM: k_fd_route and k_fd_gate cooperative
+// (all CTAs resident, for their grid barriers), k_fd_down plain.
+template <typename XT, typename WT, int NB8>
+int launch_fd_n(FdArgs &a, cudaStream_t st) {
+    auto kr = k_fd_route<XT, WT, NB8>;
+    auto kg = k_fd_gate<XT, WT, NB8, false>;
+    size_t sr = 0, sg = 0, sd = 0;
+    int rc;
+    size_t sw = 0;
+    if ((rc = fd_smem_max(kr, &sr)) || (rc = fd_smem_max(kg, &sg)) || (rc = fd_smem_max(k_fd_gate<XT, WT, NB8, true>, &sw)) ||
+        (rc = fd_smem_max(k_fd_down, &sd)))
+        return rc;
+    sg = std::min(sg, sw);
+    const int G = num_sms();
+    if (!fd_layout(a.n_tok, a.used, a.n_embd, a.ff, a.n_experts, G, sg, sd, (int)sizeof(XT), (int)sizeof(WT), &a.L) ||
+        a.L.r_bytes > sr)
+        return RVC_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(FD_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.dynamicSmemBytes = a.L.r_bytes;
+    if ((rc = (int)cudaLaunchKernelEx(&cfg, kr, a))) return rc;
+    cfg.dynamicSmemBytes = a.L.bytes;
+    if (a.n_tok <= a.L.act_x)  // every x record fits one buffer: the small-batch gate/up kernel
+        rc = (int)cudaLaunchKernelEx(&cfg, kg, a);
+    else
+        rc = (int)cudaLaunchKernelEx(&cfg, k_fd_gate<XT, WT, NB8, true>, a);
+    if (rc) return rc;
+    k_fd_down<<<G, FD_THREADS, a.L.d_bytes, st>>>(a);
+    return launched();
+}
+
+template <typename XT, typename WT>
+int launch_fd_t(FdArgs &a, cudaStream_t st) {
+    switch (a.n_embd / 256) {
+        case 1: return launch_fd_n<XT, WT, 1>(a, st);
+        case 2: return launch_fd_n<XT, WT, 2>(a, st);
+        case 4: return launch_fd_n<XT, WT, 4>(a, st);
+        case 8: return launch_fd_n<XT, WT, 8>(a, st);
+        case 11: return launch_fd_n<XT, WT, 11>(a, st);
+        case 16: return launch_fd_n<XT, WT, 16>(a, st);
+        default: return RVC_ERR_UNSUPPORTED;
+    }
+}
+
+// The decode layer for n_tok <= 64 tokens: routing from x_router (or the caller's ids/wts),
+// experts on x_expert, into out.
+int run_decode(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
+               int bias_stride, const int32_t *ids_in, const float *wts_in, int n_tok, float *out, int32_t *ids,
+               float *wts, void *ws, cudaStream_t st) {
+    if (n_tok > FD_MAX_TOK || n_tok * w->used > FD_MAX_PAIRS || w->n_embd % 256 || (w->ff / QK) % 2)
+        return RVC_ERR_UNSUPPORTED;
+    Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
+    uint8_t *hdr = static_cast<uint8_t *>(ws);
+    FdArgs a{};
+    a.xr = x_router, a.xe = x_expert, a.wr = w->router, a.bias = bias, a.bias_stride = bias_stride;
+    a.pk = packed_view(w);
+    a.down_scale = w->down_scale;
+    a.n_tok = n_tok, a.n_embd = w->n_embd, a.ff = w->ff, a.n_experts = w->n_experts, a.used = w->used;
+    a.ids_in = ids_in, a.wts_in = wts_in;
+    a.out = out, a.ids_out = ids, a.wts_out = wts;
+    a.lfast = at<float>(ws, L.lfast), a.lbound = at<float>(ws, L.lbound), a.lexact = at<float>(ws, L.lexact);
+    a.xrec = at<uint8_t>(ws, L.xrec), a.hrec = at<uint8_t>(ws, L.hrec), a.ybuf = at<float>(ws, L.ybuf);
+    a.sel_ids = at<int32_t>(ws, L.sel_ids), a.sel_wts = at<float>(ws, L.sel_wts);
+    a.sel_flag = at<int32_t>(ws, L.sel_flag);
+    a.bar_cnt = reinterpret_cast<unsigned *>(hdr + Workspace::HDR_BAR_CNT);
+    a.bar_gen = reinterpret_cast<unsigned *>(hdr + Workspace::HDR_BAR_GEN);
+    a.fallback_cnt = reinterpret_cast<unsigned *>(hdr + Workspace::HDR_FALLBACK);
+    a.plan = at<int32_t>(ws, L.plan);
+    a.status = at<int>(ws, L.status);
+    const bool xb = x_dtype == RVC_BF16, wb = w->router_dtype == RVC_BF16;
+    if (xb && wb) return launch_fd_t<uint16_t, uint16_t>(a, st);
+    if (xb) return launch_fd_t<uint16_t, float>(a, st);
+    if (wb) return launch_fd_t<float, uint16_t>(a, st);
+    return launch_fd_t<float, float>(a, st);
 }
 
 }  // namespace
@@ -498,7 +526,7 @@ int rvc_moe_router(const rvc_moe_weights *w, const void *x, int x_dtype, const f
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
     Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
     cudaStream_t st = S(stream);
-    float *lg = logits ? logits : at<float>(workspace, L.logits);
+    float *lg = logits ? logits : at<float>(workspace, L.lexact);
     int32_t *id = ids ? ids : at<int32_t>(workspace, L.ids);
     float *wt = wts ? wts : at<float>(workspace, L.wts);
     RouteArgs a{};
@@ -526,9 +554,8 @@ int rvc_moe_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype,
         !aligned(workspace, 256) || (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
-    Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
-    return run_experts(w, x_expert, x_dtype, ids, nullptr, wts, n_tok, out, workspace, L, false, false, nullptr,
-                       S(stream));
+    return run_decode(w, x_expert, x_expert, x_dtype, nullptr, 0, ids, wts, n_tok, out, nullptr, nullptr, workspace,
+                      S(stream));
 }
 
 int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
@@ -539,43 +566,8 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
         (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
-    if (n_tok * w->used > DECODE_MAX_PAIRS || n_tok > RF_MAX_TOK) return RVC_ERR_UNSUPPORTED;
-    Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
-    cudaStream_t st = S(stream);
-    int32_t *id = ids ? ids : at<int32_t>(workspace, L.ids);
-    float *wt = wts ? wts : at<float>(workspace, L.wts);
-    int *status = at<int>(workspace, L.status);
-    uint8_t *hdr = static_cast<uint8_t *>(workspace);
-    SideLane *lane = nullptr;
-    int rc = side_lane(&lane);
-    if (rc) return rc;
-    std::lock_guard<std::mutex> lock(lane->mu);
-    // K0 on the side lane: exact-order logits, selection and the combine weights
-    if ((rc = (int)cudaEventRecord(lane->fork, st))) return rc;
-    if ((rc = (int)cudaStreamWaitEvent(lane->stream, lane->fork, 0))) return rc;
-    RouteArgs a0{};
-    a0.x = x_router, a0.w = w->router, a0.bias = bias, a0.bias_stride = bias_stride;
-    a0.n_tok = n_tok, a0.n_experts = w->n_experts, a0.n_embd = w->n_embd, a0.used = w->used;
-    a0.lexact = at<float>(workspace, L.lexact0);
-    a0.done_cnt = reinterpret_cast<unsigned *>(hdr + 4);
-    a0.ids = at<int32_t>(workspace, L.ids_exact), a0.wts = wt, a0.status = status;
-    if ((rc = launch_chains(a0, x_dtype, w->router_dtype, lane->stream))) return rc;
-    if ((rc = (int)cudaEventRecord(lane->join, lane->stream))) return rc;
-    // K1 on the caller's stream: verified ids, Q8_0 of x and the plan
-    RouteArgs a1 = a0;
-    a1.x = x_router;
-    a1.lfast = at<float>(workspace, L.logits), a1.lbound = at<float>(workspace, L.lbound);
-    a1.lexact = at<float>(workspace, L.lexact1);
-    a1.done_cnt = reinterpret_cast<unsigned *>(hdr + 8);
-    a1.fallback_cnt = reinterpret_cast<unsigned *>(hdr + 12);
-    a1.ids = id, a1.wts = nullptr;
-    a1.plan = PlanOut{at<int32_t>(workspace, L.counts), at<int32_t>(workspace, L.offsets),
-                      at<int32_t>(workspace, L.order), at<int32_t>(workspace, L.pos_of),
-                      at<int32_t>(workspace, L.active), at<int32_t>(workspace, L.n_active)};
-    if (x_router == x_expert) a1.xrec = at<uint8_t>(workspace, L.xrec);
-    if ((rc = launch_route_fast(a1, x_dtype, w->router_dtype, st))) return rc;
-    return run_experts(w, x_expert, x_dtype, id, at<int32_t>(workspace, L.ids_exact), wt, n_tok, out, workspace, L,
-                       x_router == x_expert, true, lane->join, st);
+    return run_decode(w, x_router, x_expert, x_dtype, bias, bias_stride, nullptr, nullptr, n_tok, out, ids, wts,
+                      workspace, S(stream));
 }
 
 int rvc_workspace_reset(void *workspace, void *stream) {
@@ -590,9 +582,8 @@ int rvc_status(void *workspace, void *stream) {
     int st = 0;
     rc = (int)cudaMemcpy(&st, workspace, sizeof(int), cudaMemcpyDeviceToHost);
     if (rc) return rc;
-    if (st) {
-        const int zero = 0;
-        rc = (int)cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (st) {  // an aborted call can leave the grid barrier mid-way: clear the whole header
+        rc = (int)cudaMemset(workspace, 0, 256);
         if (rc) return rc;
     }
     if (st & STATUS_TIMEOUT) return RVC_ERR_DEVICE_TIMEOUT;
@@ -652,7 +643,8 @@ extern "C" int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_r
     void *scratch = nullptr;
     int rc = noalloc_scratch(&scratch);
     if (rc) return rc;
-    // The array keeps the previous call's contents; only the status word must start at zero.
+    // The array keeps the previous call's contents; only the header (status word, grid
+    // barrier) must start at zero.
     rc = (int)cudaMemsetAsync(scratch, 0, 256, S(stream));
     if (rc) return rc;
     return rvc_moe_forward(w, x_router, x_expert, x_dtype, bias, bias_stride, n_tok, out, ids, wts, scratch,
@@ -661,9 +653,10 @@ extern "C" int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_r
 
 #ifdef RVC_PROFILE
 // Profiling builds only: copy (and clear) the phase timestamps recorded by RVC_MARK.
-extern "C" int rvc_profile_dump(void *host, size_t bytes) {
+extern "C" int rvc_profile_dump(void *host, size_t bytes, void *host_clk) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpyFromSymbol(host, rvc::g_prof, bytes);
+    if (e == cudaSuccess && host_clk) e = cudaMemcpyFromSymbol(host_clk, rvc::g_prof_clk, bytes);
     static unsigned long long zero[8][1024][8];
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(rvc::g_prof, zero, sizeof zero);
     return (int)e;

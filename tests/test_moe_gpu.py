@@ -6,11 +6,16 @@ max_i |gpu_i - cpu_i| / max_i |cpu_i|, the denominator guarded by the row's larg
 as scripts/correctness_oracle.py:96-115 guards its relative errors). Rows with exact router
 ties would be excluded and counted; seeded inputs here have none, which the tests assert.
 
-The decode path does better than the tolerance: it reproduces the reference's generic (scalar)
-Q8_0 order (runtime/src/expert_kernel.rs:147-161) and its router order (ops.rs:321-326), so
-logits, weights, ids and the layer output are bit-identical to the oracle's scalar kernel. The
-reference's own AVX2 routine (expert_kernel.rs:163-191) sums in another f32 order; against it
-the bar is the 1e-3 tolerance, which is also how far the reference's two routines are apart.
+The router entry point (rvc_moe_router) reproduces the reference's router order
+(ops.rs:321-326): logits, ids and weights are bit-identical to the oracle. The decode layer
+(rvc_moe_forward) proves its ids equal to the reference's with an error bound on f64 logits
+(exact chains only for tokens the bound cannot separate) and forms the combine weights from
+those logits rounded to f32, so its weights sit within about 1e-6 (relative) of the reference's;
+its expert GEMVs reproduce the generic (scalar) Q8_0 order (expert_kernel.rs:147-161) bit for
+bit, so with the caller's ids and weights (rvc_moe_experts) the output is bit-identical, and
+through the router the output is within DECODE_TOL of the scalar kernel. The reference's own
+AVX2 routine (expert_kernel.rs:163-191) sums in another f32 order; against it the bar is the
+1e-3 tolerance, which is also how far the reference's two routines are apart.
 """
 import numpy as np
 import pytest
@@ -20,6 +25,12 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 ROW_TOL = 1e-3
+DECODE_TOL = 1e-4  # decode layer vs the oracle's scalar kernel (weights from f32-rounded f64 logits)
+W_TOL = 1e-4       # relative error of those weights
+
+
+def rel_err(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30)))
 
 
 def row_rel_err(gpu: np.ndarray, cpu: np.ndarray) -> np.ndarray:
@@ -122,9 +133,8 @@ def test_decode_layer_matches_oracle(layer, weights, oracle, pool, pool_avx2, n_
     got = out.cpu().numpy()
     want, want_ids, want_w, _ = oracle.moe_layer(pool, x, x, weights["w_router"], weights["gate_up"], weights["down"])
     assert np.array_equal(ids.cpu().numpy(), want_ids)
-    assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
-        f"not bit-exact: max row rel err {row_rel_err(got, want).max():.3e}"
+    assert rel_err(wts.cpu().numpy(), want_w) <= W_TOL
+    assert row_rel_err(got, want).max() <= DECODE_TOL
     want_avx2, _, _, _ = oracle.moe_layer(pool_avx2, x, x, weights["w_router"], weights["gate_up"], weights["down"])
     assert row_rel_err(got, want_avx2).max() <= ROW_TOL
 
@@ -144,8 +154,7 @@ def test_decode_f32_inputs_f32_router_and_down_scale(weights, oracle, pool):
     lyr.status()
     want, _, _, _ = oracle.moe_layer(pool, xr, x, wr, weights["gate_up"], weights["down"], down_scale=ds)
     got = out.cpu().numpy()
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
-        f"not bit-exact: max row rel err {row_rel_err(got, want).max():.3e}"
+    assert row_rel_err(got, want).max() <= DECODE_TOL
 
 
 def test_experts_entry_with_caller_ids(layer, weights, oracle, pool):
@@ -170,10 +179,11 @@ def test_repeat_calls_are_deterministic(layer):
     assert torch.equal(a, b)
 
 
-def test_near_ties_take_the_exact_fallback(weights, oracle, pool):
+@pytest.mark.parametrize("n_tok", [3, 16])  # every CTA selects (<= 4 tokens) / one warp per token
+def test_near_ties_take_the_exact_fallback(weights, oracle, pool, n_tok):
     """Two router rows one bf16 ulp apart, both forced into the top-8: their logits differ by
-    less than the fast router's error bound, so the fused layer must recompute those tokens'
-    logits in the exact order (k_route_fast's fallback) and still match bit for bit."""
+    less than the fast router's error bound, so the decode kernel must recompute those tokens'
+    logits in the exact order and still select exactly the reference's ids."""
     from rosevine_b200 import synth
     from rosevine_b200.moe import MoeLayer
     wr = weights["w_router"].copy()
@@ -182,17 +192,17 @@ def test_near_ties_take_the_exact_fallback(weights, oracle, pool):
     bias = np.zeros(128, np.float32)
     bias[[3, 5]] = 8.0
     lyr = MoeLayer(wr, weights["gate_up"], weights["down"], max_tok=16)
-    x = synth.tokens(16, 600)
-    ids = torch.empty((16, 8), dtype=torch.int32, device="cuda")
-    wts = torch.empty((16, 8), dtype=torch.float32, device="cuda")
+    x = synth.tokens(n_tok, 600)
+    ids = torch.empty((n_tok, 8), dtype=torch.int32, device="cuda")
+    wts = torch.empty((n_tok, 8), dtype=torch.float32, device="cuda")
     out = lyr.forward(xdev(x), ids=ids, wts=wts, bias=torch.from_numpy(bias).cuda())
     lyr.status()
     want, want_ids, want_w, _ = oracle.moe_layer(pool, x, x, wr, weights["gate_up"], weights["down"], bias=bias)
-    assert np.isin(want_ids, [3, 5]).sum() == 32  # both near-tied experts selected for every token
+    assert np.isin(want_ids, [3, 5]).sum() == 2 * n_tok  # both near-tied experts selected for every token
     # workspace header counter; a token whose x at the perturbed element is large can still be
-    # separated by the bound, so not necessarily all 16
+    # separated by the bound, so not necessarily every token
     fallbacks = int(lyr.ws[12:16].view(torch.int32).item())
-    assert 8 <= fallbacks <= 16, f"{fallbacks} of 16 tokens took the exact fallback"
+    assert n_tok // 2 <= fallbacks <= n_tok, f"{fallbacks} of {n_tok} tokens took the exact fallback"
     assert np.array_equal(ids.cpu().numpy(), want_ids)
-    assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
-    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert rel_err(wts.cpu().numpy(), want_w) <= W_TOL
+    assert row_rel_err(out.cpu().numpy(), want).max() <= DECODE_TOL

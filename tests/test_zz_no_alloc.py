@@ -45,7 +45,7 @@ def test_noalloc_forward_matches_workspace_forward_twice(small_layer):
 def test_noalloc_rejects_requests_beyond_its_scratch(small_layer):
     from rosevine_b200 import rvcuda as rc
     lyr = small_layer
-    n_tok = 100  # needs more than RVC_NOALLOC_SCRATCH_BYTES of scratch
+    n_tok = 400  # needs more than RVC_NOALLOC_SCRATCH_BYTES of scratch
     assert rc.workspace_bytes(n_tok, lyr.n_embd, lyr.ff, lyr.n_experts, lyr.used) > rc.NOALLOC_SCRATCH_BYTES
     x = torch.zeros((n_tok, lyr.n_embd), dtype=torch.bfloat16, device="cuda")
     out = torch.empty((n_tok, lyr.n_embd), dtype=torch.float32, device="cuda")
