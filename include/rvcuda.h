@@ -148,6 +148,12 @@ int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, cons
 int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,
                          const void *xq8, int n_in, int32_t *out, void *stream);
 
+/* Test hook: one tensor-core tile through the shared-memory layouts and tensor-memory reads
+ * the prefill GEMM uses: d[128][n] = a[128][32] . b[n][32]^T, int8 inputs (device, row-major,
+ * 16-byte aligned), int32 output. n = 16 .. 128, a multiple of 16. status: device int, a
+ * bounded wait that ran out sets bit 1. */
+int rvc_debug_mma_i8(const int8_t *a, const int8_t *b, int n, int32_t *d, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,426 @@
+// prefill.cuh - the MoE layer for prefill batches: a grouped expert GEMM on the 5th-generation
+// tensor cores (tcgen05.mma kind::i8, accumulators in tensor memory), sm_100a.
+//
+// Replaces the reference's per-expert device loop (runtime/src/hip_exec.rs:820-843) for batches
+// above the decode kernels' 64 tokens and computes what its CPU-experts Q8_0 path computes
+// (runtime/src/exec.rs:572-640, expert_pool.rs:282-355, expert_kernel.rs:147-161):
+//
+//   k_pf_gather   Q8_0 records of x in dispatch-plan order (the expert groups contiguous).
+//   k_pf_gemm<GU> for each (expert, 128 packed gate/up rows, 128 tokens) tile: per 32-column
+//                 block b one tcgen05.mma (M=128, N=128, K=32, s8 x s8 -> s32) gives the exact
+//                 int32 block dots D_b; the epilogue warps read D_b from tensor memory and
+//                 accumulate acc = acc + D_b * (dw_b * dx_b) per (row, token) in block order,
+//                 each operation rounded as the scalar reference does; then h = gelu(gate)*up
+//                 and its Q8_0 records (plan order).
+//   k_pf_gemm<DN> the same over the down rows and the h records: y per (pair, row).
+//   k_pf_combine  out[t] = slot-order sum of (y * down_scale) * w (exec.rs:626-638).
+//
+// Operands. Weights stay Q4_0 in HBM (the packed nibble and scale planes of pack.cuh); a stage
+// of 8 K-blocks of a tile's 128 rows (16 KB of nibbles) is brought in by one TMA tensor copy and
+// unpacked by the producer warp to signed int8 (n - 8) in the canonical no-swizzle K-major
+// layout tcgen05 reads (8-row x 16-byte core matrices). Activation tiles (128 tokens x 8 blocks)
+// are TMA tensor copies straight into that layout: the tensor map's dimensions are ordered
+// (16 bytes, rows, 16-byte chunks) so that a chunk's 128 rows land contiguously.
+//
+// Pipeline (one CTA per tile, 17 warps): warp 16 is the producer and MMA issuer (lane 0 issues
+// the TMA copies and the MMAs, all lanes unpack); warps 0-15 are the epilogue, warp w reading
+// tensor-memory lanes 32 (w % 4) .. + 31 (tile rows) and columns 32 (w / 4) .. + 31 (tokens).
+// Two shared-memory stages, four tensor-memory accumulators of 128 columns, mbarriers between
+// the roles; every wait is bounded (a timeout ends in the status word, never in a hang).
+#pragma once
+#include "common.cuh"
+#include "pack.cuh"
+
+#include <cuda.h>
+
+namespace rvc {
+
+constexpr int PF_M = 128;          // rows per tile (tensor-memory lanes)
+constexpr int PF_N = 128;          // tokens per tile (accumulator columns)
+constexpr int PF_KB = 8;           // K-blocks per stage
+constexpr int PF_STAGES = 2;
+constexpr int PF_TBUF = 4;         // tensor-memory accumulators
+constexpr int PF_EPI_WARPS = 16;
+constexpr int PF_THREADS = (PF_EPI_WARPS + 1) * 32;
+constexpr int PF_TMEM_COLS = PF_TBUF * PF_N;  // 512: the whole tensor memory of the SM
+
+// ------------------------------------------------------------------ tcgen05 primitives
+__device__ __forceinline__ void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {  // one full warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // one full warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// named barrier of the 16 epilogue warps of k_pf_gemm
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 6, %0;" ::"n"(PF_EPI_WARPS * 32) : "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major, no swizzle ("interleave"): 8-row x 16-byte core
+// matrices; lbo = bytes between the two 16-byte K halves of a 32-byte K step, sbo = bytes
+// between consecutive 8-row groups (descriptor format: start >> 4 at bits 0-13, lbo >> 4 at
+// 16-29, sbo >> 4 at 32-45, version 1 at 46-47, layout type 0 at 61-63).
+__device__ __forceinline__ uint64_t umma_desc(const void *smem_ptr, uint32_t lbo, uint32_t sbo) {
+    const uint32_t a = smem_u32(smem_ptr);
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
+}
+
+// Instruction descriptor of kind::i8: s32 accumulator (bits 4-5 = 2), A and B signed int8
+// (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] = A * B (+ D if accumulate), one thread.
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from tensor memory; tcgen05.wait::ld before use.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 3-D TMA tensor copy global -> shared, completion on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Signed int8 (n - 8) of four nibble values n in 0..15 (one per byte): adding 0x78 to each byte
+// through (n | 0x80) - 8 cannot borrow across bytes; the xor restores the sign bit.
+__device__ __forceinline__ uint32_t nib_to_s8(uint32_t v) { return ((v | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
+
+// ------------------------------------------------------------------ MMA check (debug ABI)
+// One tile through the same layouts and tensor-memory reads as k_pf_gemm: A [128 rows][32]
+// and B [n rows][32] int8 (row-major in global), D [128][n] int32 = A . B^T. Thread r < 128
+// places row r; warp w < 4 reads tensor-memory lanes 32 w .. 32 w + 31. n = 16 .. 128, step 16.
+__global__ void __launch_bounds__(128) k_debug_mma_i8(const int8_t *__restrict__ A, const int8_t *__restrict__ B,
+                                                      int n, int32_t *__restrict__ D, int *status) {
+    __shared__ __align__(1024) uint8_t sa[2 * PF_M * 16];
+    __shared__ __align__(1024) uint8_t sb[2 * PF_N * 16];
+    __shared__ uint64_t bar;
+    __shared__ uint32_t taddr_s;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (warp == 0) {
+        tmem_alloc(&taddr_s, 128);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    // K halves k = 0, 1 of row r at k * (rows * 16) + r * 16 (core matrices of 8 rows)
+    for (int k = 0; k < 2; ++k) {
+        *reinterpret_cast<int4 *>(sa + k * PF_M * 16 + tid * 16) = *reinterpret_cast<const int4 *>(A + tid * 32 + k * 16);
+        if (tid < n)
+            *reinterpret_cast<int4 *>(sb + k * PF_N * 16 + tid * 16) =
+                *reinterpret_cast<const int4 *>(B + tid * 32 + k * 16);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = taddr_s;
+    if (tid == 0) {
+        mma_i8(taddr, umma_desc(sa, PF_M * 16, 128), umma_desc(sb, PF_N * 16, 128), idesc_i8(PF_M, n), false);
+        mma_commit(&bar);
+    }
+    const bool ok = fd_mbar_wait(&bar, 0, status);
+    tc_fence_after();
+    if (ok) {
+        for (int c0 = 0; c0 < n; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(taddr + ((uint32_t)(32 * warp) << 16) + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (c0 + i < n) D[(size_t)tid * n + c0 + i] = (int32_t)v[i];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(taddr, 128);
+}
+
+// ------------------------------------------------------------------ gather
+// Q8_0 records of x in plan order: record p holds token order[p] / used. One warp per block.
+template <typename XT>
+__global__ void __launch_bounds__(256) k_pf_gather(const XT *__restrict__ x, int n_embd, const int32_t *__restrict__ order,
+                                                   int used, int pairs, uint8_t *__restrict__ xperm) {
+    const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long total = (long long)pairs * nb;
+    for (long long i = (long long)blockIdx.x * 8 + warp; i < total; i += (long long)gridDim.x * 8) {
+        const int p = (int)(i / nb), b = (int)(i - (long long)p * nb);
+        const int t = __ldg(order + p) / used;
+        const float v = ld_val<XT>(x, (size_t)t * n_embd + (size_t)b * QK + lane);
+        uint16_t dbits;
+        int qsum;
+        const int8_t q = quant_q8_lane(v, &dbits, &qsum);
+        q8rec_store(xperm + (size_t)p * xrb, nb, b, lane, q, dbits, qsum);
+    }
+}
+
+// ------------------------------------------------------------------ combine
+// out[t][r] = slot-order sum over j of (y[pos_of[t used + j]][r] * down_scale[e]) * w[t][j].
+__global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
+                                                    const int32_t *__restrict__ ids, const float *__restrict__ wts,
+                                                    const float *__restrict__ down_scale, int used, int n_embd,
+                                                    int n_tok, float *__restrict__ out) {
+    const long long total = (long long)n_tok * n_embd;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / n_embd), r = (int)(i - (long long)t * n_embd);
+        float o = 0.0f;
+        for (int j = 0; j < used; ++j) {
+            const int p = t * used + j;
+            const int e = __ldg(ids + p);
+            const float ds = down_scale ? __ldg(down_scale + e) : 1.0f;
+            const float v = __fmul_rn(__fmul_rn(__ldg(y + (size_t)__ldg(pos_of + p) * n_embd + r), ds), __ldg(wts + p));
+            o = j == 0 ? v : __fadd_rn(o, v);
+        }
+        out[i] = o;
+    }
+}
+
+// ------------------------------------------------------------------ grouped GEMM
+struct PfArgs {
+    // plan (dispatch order): counts / offsets per expert
+    const int32_t *counts, *offsets;
+    int n_experts, pairs;
+    int rows_per_expert;  // 2 ff (gate/up) or n_embd (down)
+    int nblk;             // K blocks (n_embd / 32 or ff / 32)
+    int swizzled;         // the nibble plane's blocks are XOR-swizzled per row (gate/up)
+    const uint16_t *scl;  // weight scales [E][rows][nblk] (f16 bits)
+    const uint8_t *arec;  // activation records in plan order, q8rec_bytes(nblk) each
+    int nh;               // (gate/up) h blocks per pair (ff / 32): the h record geometry
+    uint8_t *hrec;        // (gate/up) out: h records in plan order
+    float *y;             // (down) out: [pairs][n_embd]
+    int n_embd;
+    int *status;
+};
+
+constexpr int PF_GU = 0, PF_DN = 1;
+
+// Shared memory of one stage: unpacked A (8 blocks x 2 halves x 128 rows x 16 B), B (same for
+// 128 tokens), the nibble staging of A (128 rows x 8 blocks x 16 B), scales.
+constexpr int PF_A_BYTES = PF_KB * 2 * PF_M * 16;  // 32 KB
+constexpr int PF_B_BYTES = PF_KB * 2 * PF_N * 16;  // 32 KB
+constexpr int PF_NIB_BYTES = PF_M * PF_KB * 16;    // 16 KB
+constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_NIB_BYTES + PF_M * PF_KB * 4 + PF_N * PF_KB * 4;
+constexpr int PF_SMEM_BYTES = PF_STAGES * PF_STAGE_BYTES + 1024;  // + alignment slack
+
+template <int MODE>
+__global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant__ CUtensorMap map_nib,
+                                                           const __grid_constant__ CUtensorMap map_act, PfArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full_bar[PF_STAGES], stage_free[PF_STAGES], mma_done[PF_TBUF], tmem_free[PF_TBUF];
+    __shared__ uint32_t taddr_s;
+    __shared__ int s_e, s_p0, s_nt;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nblk = a.nblk, rows = a.rows_per_expert;
+    const int row0 = blockIdx.x * PF_M;  // tile rows within the expert
+
+    // tile -> (expert, token tile): blockIdx.y indexes the token tiles of all experts in order
+    if (tid == 0) {
+        int y = blockIdx.y, e = 0;
+        s_e = -1;
+        for (; e < a.n_experts; ++e) {
+            const int nt = (__ldg(a.counts + e) + PF_N - 1) / PF_N;
+            if (y < nt) break;
+            y -= nt;
+        }
+        if (e < a.n_experts) {
+            s_e = e;
+            s_p0 = __ldg(a.offsets + e) + y * PF_N;
+            s_nt = min(PF_N, __ldg(a.counts + e) - y * PF_N);
+        }
+    }
+    __syncthreads();
+    if (s_e < 0) return;
+    const int e = s_e, p0 = s_p0, nt = s_nt;
+    const int nst = (nblk + PF_KB - 1) / PF_KB;
+
+    if (warp == 0) {
+        tmem_alloc(&taddr_s, PF_TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int s = 0; s < PF_STAGES; ++s) mbar_init(&full_bar[s], 1), mbar_init(&stage_free[s], 1 + PF_EPI_WARPS);
+        for (int s = 0; s < PF_TBUF; ++s) mbar_init(&mma_done[s], 1), mbar_init(&tmem_free[s], PF_EPI_WARPS);
+        fence_barrier_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = taddr_s;
+    const uint32_t idesc = idesc_i8(PF_M, PF_N);
+    auto stage_ptr = [&](int s) { return smem + (size_t)s * PF_STAGE_BYTES; };
+
+    if (warp == PF_EPI_WARPS) {
+        // ------------------------------------------------ producer + MMA issuer
+        const size_t wrow0 = (size_t)e * rows + row0;  // first weight row of the tile
+        const int arb = q8rec_bytes(nblk);
+        bool ok = true;
+        for (int st = 0; st < nst && ok; ++st) {
+            const int s = st % PF_STAGES;
+            uint8_t *sp = stage_ptr(s);
+            uint8_t *sA = sp, *sB = sp + PF_A_BYTES, *sN = sB + PF_B_BYTES;
+            float *sdw = reinterpret_cast<float *>(sN + PF_NIB_BYTES);
+            float *sdx = sdw + PF_M * PF_KB;
+            if (st >= PF_STAGES) ok &= fd_mbar_wait(&stage_free[s], ((st / PF_STAGES) - 1) & 1u, a.status);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const int kb0 = st * PF_KB, kn = min(PF_KB, nblk - kb0);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full_bar[s], PF_NIB_BYTES + PF_B_BYTES);
+                tma_load_3d(sN, &map_nib, 0, kb0, (int)wrow0, &full_bar[s]);  // [128 rows][8 blocks][16 B]
+                tma_load_3d(sB, &map_act, 0, p0, 2 * kb0, &full_bar[s]);     // [16 halves][128 tokens][16 B]
+            }
+            // scales of the stage (f32): dw [row][j], dx [token][j]
+            for (int i = lane; i < PF_M * PF_KB; i += 32) {
+                const int r = i / PF_KB, j = i % PF_KB;
+                sdw[i] = j < kn ? f16_bits_to_f32(__ldg(a.scl + (wrow0 + r) * nblk + kb0 + j)) : 0.0f;
+            }
+            for (int i = lane; i < PF_N * PF_KB; i += 32) {
+                const int n = i / PF_KB, j = i % PF_KB;
+                sdx[i] = (n < nt && j < kn)
+                             ? reinterpret_cast<const float *>(a.arec + (size_t)(p0 + n) * arb + nblk * 32)[kb0 + j]
+                             : 0.0f;
+            }
+            ok &= fd_mbar_wait(&full_bar[s], (st / PF_STAGES) & 1u, a.status);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            // unpack: task (row r, block j, half k): 16 int8 at sA + (j * 2 + k) * 2048 + r * 16
+            for (int i = lane; i < PF_M * PF_KB * 2; i += 32) {
+                const int r = i >> 4, j = (i >> 1) & 7, k = i & 1;
+                const int pos = a.swizzled ? (j ^ (r & 7)) : j;  // the tile's rows start at a multiple of 8
+                const uint4 nb4 = *reinterpret_cast<const uint4 *>(sN + r * (PF_KB * 16) + pos * 16);
+                const int sh = 4 * k;
+                uint4 o;
+                o.x = nib_to_s8((nb4.x >> sh) & 0x0F0F0F0Fu);
+                o.y = nib_to_s8((nb4.y >> sh) & 0x0F0F0F0Fu);
+                o.z = nib_to_s8((nb4.z >> sh) & 0x0F0F0F0Fu);
+                o.w = nib_to_s8((nb4.w >> sh) & 0x0F0F0F0Fu);
+                *reinterpret_cast<uint4 *>(sA + (j * 2 + k) * (PF_M * 16) + r * 16) = o;
+            }
+            fence_proxy_async_smem();
+            __threadfence_block();  // the scales above, for the epilogue warps that wait on the MMAs
+            __syncwarp();
+            if (lane == 0) {
+                for (int j = 0; j < kn && ok; ++j) {
+                    const int b = kb0 + j, buf = b % PF_TBUF;
+                    if (b >= PF_TBUF) ok &= fd_mbar_wait(&tmem_free[buf], ((b / PF_TBUF) - 1) & 1u, a.status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    mma_i8(taddr + buf * PF_N, umma_desc(sA + j * 2 * (PF_M * 16), PF_M * 16, 128),
+                           umma_desc(sB + j * 2 * (PF_N * 16), PF_N * 16, 128), idesc, false);
+                    mma_commit(&mma_done[buf]);
+                }
+                mma_commit(&stage_free[s]);  // the stage's buffers are free once its MMAs are done
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+        }
+        if (!ok) set_status(a.status, STATUS_TIMEOUT);
+    } else {
+        // ------------------------------------------------ epilogue: scale and accumulate
+        const int m = 32 * (warp & 3) + lane;  // tile row (tensor-memory lane)
+        const int cg = warp >> 2;              // token columns 32 cg .. 32 cg + 31
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        bool ok = true;
+        for (int b = 0; b < nblk; ++b) {
+            const int buf = b % PF_TBUF, st = b / PF_KB, s = st % PF_STAGES, j = b % PF_KB;
+            ok &= fd_mbar_wait(&mma_done[buf], (b / PF_TBUF) & 1u, a.status);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            uint32_t v[32];
+            tmem_ld32(taddr + ((uint32_t)(32 * (warp & 3)) << 16) + buf * PF_N + cg * 32, v);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_free[buf]);
+            const float *sdw = reinterpret_cast<const float *>(stage_ptr(s) + PF_A_BYTES + PF_B_BYTES + PF_NIB_BYTES);
+            const float *sdx = sdw + PF_M * PF_KB;
+            const float dw = sdw[m * PF_KB + j];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float dx = sdx[(cg * 32 + i) * PF_KB + j];
+                acc[i] = __fadd_rn(acc[i], __fmul_rn((float)(int32_t)v[i], __fmul_rn(dw, dx)));
+            }
+            if (j == PF_KB - 1 || b == nblk - 1) {  // done with this stage's scales
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&stage_free[s]);
+            }
+        }
+        if (!ok) set_status(a.status, STATUS_TIMEOUT);
+        // ------------------------------------------------ outputs
+        if (MODE == PF_DN) {
+            if (ok) {
+                float *yrow = a.y + (size_t)p0 * a.n_embd + row0 + m;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (cg * 32 + i < nt) yrow[(size_t)(cg * 32 + i) * a.n_embd] = acc[i];
+            }
+        } else {
+            // rows: unit u = m / 64 of the tile; m % 64 < 32 gate, else up; column m % 32.
+            // Gate values go through shared memory (stage 0, free now) to the up threads.
+            float *sg = reinterpret_cast<float *>(smem);  // [2 units][32 columns][128 tokens]
+            named_sync_epi();
+            const int u = m >> 6, col = m & 31;
+            const bool gate = (m & 63) < 32;
+            if (gate) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sg[(u * 32 + col) * PF_N + cg * 32 + i] = acc[i];
+            }
+            named_sync_epi();
+            if (!gate && ok) {
+                const int hrb = q8rec_bytes(a.nh);
+                const int q = (row0 >> 6) + u;  // h block within the expert's ff columns
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int n = cg * 32 + i;
+                    const float hv = __fmul_rn(gelu_tanh(sg[(u * 32 + col) * PF_N + n]), acc[i]);
+                    uint16_t dbits;
+                    int qsum;
+                    const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);  // the warp's 32 lanes: one block
+                    if (n < nt) q8rec_store(a.hrec + (size_t)(p0 + n) * hrb, a.nh, q, lane, qv, dbits, qsum);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(taddr, PF_TMEM_COLS);
+}
+
+}  // namespace rvc

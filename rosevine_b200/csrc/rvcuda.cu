@@ -15,6 +15,9 @@
 #include "common.cuh"
 #include "decode_fused.cuh"
 #include "pack.cuh"
+#include "prefill.cuh"
+
+#include <cudaTypedefs.h>
 #include "router.cuh"
 #include "router_fast.cuh"
 
@@ -63,8 +66,8 @@ struct Workspace {
     // last-CTA counter at 4, at 12 the running count of tokens routed through the exact
     // fallback, and the decode kernel's grid barrier: arrival count at 64, generation at 128
     // (separate cache lines; the count returns to zero after every barrier).
-    size_t status, lfast, lbound, lexact, ids, wts, sel_ids, sel_wts, sel_flag, xrec, hrec, ybuf, plan, counts,
-        offsets, order, pos_of, active, n_active, total;
+    size_t status, lfast, lbound, lexact, ids, wts, sel_ids, sel_wts, sel_flag, xrec, hrec, ybuf, xperm, plan,
+        counts, offsets, order, pos_of, active, n_active, total;
     static constexpr size_t HDR_FALLBACK = 12, HDR_BAR_CNT = 64, HDR_BAR_GEN = 128;
     Workspace(int max_tok, int n_embd, int ff, int ne, int used) {
         const size_t nb = n_embd / QK, nbh = ff / QK, pairs = (size_t)max_tok * used;
@@ -85,7 +88,8 @@ struct Workspace {
         sel_flag = take((size_t)max_tok * 4);
         xrec = take((size_t)max_tok * q8rec_bytes((int)nb));
         hrec = take(pairs * q8rec_bytes((int)nbh));
-        ybuf = take((size_t)std::min(max_tok, FD_MAX_TOK) * used * n_embd * 4);  // decode calls only
+        ybuf = take(pairs * n_embd * 4);
+        xperm = max_tok > FD_MAX_TOK ? take(pairs * q8rec_bytes((int)nb)) : o;  // prefill calls only
         plan = take(fd_plan_words(std::min(max_tok, FD_MAX_TOK) * used, ne) * 4);
         counts = take((size_t)ne * 4);
         offsets = take((size_t)(ne + 1) * 4);
@@ -374,6 +378,98 @@ int launch_fd_t(FdArgs &a, cudaStream_t st) {
     }
 }
 
+// ------------------------------------------------------------------ prefill
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+int tensor_map_encode() {
+    std::lock_guard<std::mutex> lock(g_encode_mu);
+    if (g_encode) return 0;
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return (int)e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return (int)cudaErrorNotSupported;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return 0;
+}
+
+// A 3-D byte tensor map (dims d0 innermost; strides of dims 1 and 2 in bytes), box b0 x b1 x b2,
+// no swizzle, out-of-range elements read as zero.
+int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+          uint32_t b0, uint32_t b1, uint32_t b2) {
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {s1, s2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+// The prefill layer (n_tok > 64): the reference-order router (logits, selection, plan), Q8_0
+// of x in plan order, the tensor-core gate/up and down GEMMs, the slot-order combine.
+int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
+                int bias_stride, int n_tok, float *out, int32_t *ids, float *wts, void *ws, size_t ws_bytes,
+                cudaStream_t st) {
+    int rc;
+    if ((rc = tensor_map_encode())) return rc;
+    const int ne = w->n_experts, used = w->used, pairs = n_tok * used;
+    const int nb = w->n_embd / QK, nbh = w->ff / QK;
+    if (nb % PF_KB || (2 * w->ff) % PF_M || w->n_embd % PF_M || ne > MAX_EXPERTS) return RVC_ERR_UNSUPPORTED;
+    Workspace L(n_tok, w->n_embd, w->ff, ne, used);
+    int32_t *id = ids ? ids : at<int32_t>(ws, L.ids);
+    float *wt = wts ? wts : at<float>(ws, L.wts);
+    int32_t *counts = at<int32_t>(ws, L.counts), *offsets = at<int32_t>(ws, L.offsets);
+    int32_t *order = at<int32_t>(ws, L.order), *pos_of = at<int32_t>(ws, L.pos_of);
+    int *status = at<int>(ws, L.status);
+    // 1. router in the reference's order, selection, plan
+    if ((rc = rvc_moe_router(w, x_router, x_dtype, bias, bias_stride, n_tok, id, wt, nullptr, nullptr, nullptr, ws,
+                             ws_bytes, st)))
+        return rc;
+    k_plan<<<1, PLAN_THREADS, 0, st>>>(id, pairs, ne, counts, offsets, order, pos_of, at<int32_t>(ws, L.active),
+                                       at<int32_t>(ws, L.n_active), status);
+    if ((rc = launched())) return rc;
+    // 2. Q8_0 of x in plan order
+    uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
+    const int gblocks = (int)std::min<long long>(4096, ((long long)pairs * nb + 7) / 8);
+    if (x_dtype == RVC_BF16)
+        k_pf_gather<uint16_t><<<gblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, order, used, pairs, xperm);
+    else
+        k_pf_gather<float><<<gblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, order, used, pairs, xperm);
+    if ((rc = launched())) return rc;
+    // 3. gate/up and down GEMMs
+    const PackedView pk = packed_view(w);
+    CUtensorMap m_gu, m_x, m_dn, m_h;
+    const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
+    if ((rc = map3d(&m_gu, pk.gu_nib, 16, nb, (uint64_t)ne * 2 * w->ff, 16, (uint64_t)nb * 16, 16, PF_KB, PF_M)) ||
+        (rc = map3d(&m_x, xperm, 16, pairs, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
+        (rc = map3d(&m_dn, pk.dn_nib, 16, nbh, (uint64_t)ne * w->n_embd, 16, (uint64_t)nbh * 16, 16, PF_KB, PF_M)) ||
+        (rc = map3d(&m_h, hrec, 16, pairs, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)))
+        return rc;
+    size_t smax = 0;
+    if ((rc = fd_smem_max(k_pf_gemm<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm<PF_DN>, &smax))) return rc;
+    if (smax < (size_t)PF_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
+    const int tiles_y = (pairs + PF_N - 1) / PF_N + ne;  // an upper bound on the (expert, token tile) count
+    PfArgs g{};
+    g.counts = counts, g.offsets = offsets, g.n_experts = ne, g.pairs = pairs;
+    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.scl = pk.gu_scl, g.arec = xperm;
+    g.nh = nbh, g.hrec = hrec, g.n_embd = w->n_embd, g.status = status;
+    k_pf_gemm<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_gu, m_x, g);
+    if ((rc = launched())) return rc;
+    PfArgs d = g;
+    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.scl = pk.dn_scl, d.arec = hrec;
+    d.hrec = nullptr, d.y = at<float>(ws, L.ybuf);
+    k_pf_gemm<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_dn, m_h, d);
+    if ((rc = launched())) return rc;
+    // 4. slot-order combine
+    k_pf_combine<<<4 * num_sms(), 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
+                                                w->n_embd, n_tok, out);
+    return launched();
+}
+
 // The decode layer for n_tok <= 64 tokens: routing from x_router (or the caller's ids/wts),
 // experts on x_expert, into out.
 int run_decode(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
@@ -566,6 +662,9 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
         (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
+    if (n_tok > FD_MAX_TOK)
+        return run_prefill(w, x_router, x_expert, x_dtype, bias, bias_stride, n_tok, out, ids, wts, workspace,
+                           workspace_bytes, S(stream));
     return run_decode(w, x_router, x_expert, x_dtype, bias, bias_stride, nullptr, nullptr, n_tok, out, ids, wts,
                       workspace, S(stream));
 }
@@ -589,6 +688,13 @@ int rvc_status(void *workspace, void *stream) {
     if (st & STATUS_TIMEOUT) return RVC_ERR_DEVICE_TIMEOUT;
     if (st & STATUS_BAD_INDEX) return RVC_ERR_DEVICE_INDEX;
     return 0;
+}
+
+int rvc_debug_mma_i8(const int8_t *a, const int8_t *b, int n, int32_t *d, int *status, void *stream) {
+    if (!a || !b || !d || n < 16 || n > PF_N || n % 16 || !aligned(a, 16) || !aligned(b, 16))
+        return (int)cudaErrorInvalidValue;
+    k_debug_mma_i8<<<1, 128, 0, S(stream)>>>(a, b, n, d, status);
+    return launched();
 }
 
 int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,

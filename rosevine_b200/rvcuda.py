@@ -31,6 +31,7 @@ EXPORTS = [
     "rvc_event_elapsed", "rvc_upload_async", "rvc_download_async", "rvc_event_record_on", "rvc_stream_sync",
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
+    "rvc_debug_mma_i8",
 ]
 
 
@@ -95,6 +96,7 @@ def lib() -> ctypes.CDLL:
             "rvc_status": ([P, P], I),
             "rvc_debug_block_sums": ([W, I, I, P, I, P, I, P, P], I),
             "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
+            "rvc_debug_mma_i8": ([P, P, I, P, P, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -287,3 +289,9 @@ def debug_block_sums(w: MoeWeights, which: int, expert: int, rows, n_rows: int, 
     nblk = w.n_embd // 32 if which == 0 else w.ff // 32
     check(lib().rvc_debug_block_sums(ctypes.byref(w), which, expert, _ptr(rows, n_rows * 4), n_rows,
                                      _ptr(xq8, n_in * nblk * 34), n_in, _ptr(out, n_in * n_rows * nblk * 4), stream))
+
+
+def debug_mma_i8(a, b, n: int, d, status, stream: int | None = None) -> None:
+    """d[128][n] = a[128][32] . b[n][32]^T through one tensor-core tile (int8 in, int32 out)."""
+    check(lib().rvc_debug_mma_i8(_ptr(a, 128 * 32), _ptr(b, n * 32), n, _ptr(d, 128 * n * 4), _ptr(status, 4),
+                                 stream))
