@@ -38,7 +38,7 @@ namespace rvc {
 constexpr int PF_M = 128;          // rows per tile (tensor-memory lanes)
 constexpr int PF_N = 128;          // tokens per tile (accumulator columns)
 constexpr int PF_KB = 8;           // K-blocks per stage
-constexpr int PF_STAGES = 2;
+constexpr int PF_STAGES = 3;
 constexpr int PF_TBUF = 4;         // tensor-memory accumulators
 constexpr int PF_EPI_WARPS = 16;
 constexpr int PF_THREADS = (PF_EPI_WARPS + 1) * 32;
@@ -106,6 +106,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 2-D TMA tensor copy global -> shared, completion on `bar`.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // 3-D TMA tensor copy global -> shared, completion on `bar`.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, uint64_t *bar) {
@@ -232,19 +241,22 @@ struct PfArgs {
 constexpr int PF_GU = 0, PF_DN = 1;
 
 // Shared memory of one stage: unpacked A (8 blocks x 2 halves x 128 rows x 16 B), B (same for
-// 128 tokens), the nibble staging of A (128 rows x 8 blocks x 16 B), scales.
+// 128 tokens), the tokens' block scales (128 tokens x 8 f32); after the stages, one buffer for
+// the nibbles of A (128 rows x 8 blocks x 16 B), refilled as soon as they are unpacked.
 constexpr int PF_A_BYTES = PF_KB * 2 * PF_M * 16;  // 32 KB
 constexpr int PF_B_BYTES = PF_KB * 2 * PF_N * 16;  // 32 KB
 constexpr int PF_NIB_BYTES = PF_M * PF_KB * 16;    // 16 KB
-constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_NIB_BYTES + PF_M * PF_KB * 4 + PF_N * PF_KB * 4;
-constexpr int PF_SMEM_BYTES = PF_STAGES * PF_STAGE_BYTES + 1024;  // + alignment slack
+constexpr int PF_DX_BYTES = PF_N * PF_KB * 4;      // 4 KB
+constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_DX_BYTES;
+constexpr int PF_SMEM_BYTES = PF_STAGES * PF_STAGE_BYTES + PF_NIB_BYTES + 1024;  // + alignment slack
 
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant__ CUtensorMap map_nib,
-                                                           const __grid_constant__ CUtensorMap map_act, PfArgs a) {
+                                                           const __grid_constant__ CUtensorMap map_act,
+                                                           const __grid_constant__ CUtensorMap map_dx, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full_bar[PF_STAGES], stage_free[PF_STAGES], mma_done[PF_TBUF], tmem_free[PF_TBUF];
+    __shared__ uint64_t full_bar[PF_STAGES], stage_free[PF_STAGES], mma_done[PF_TBUF], tmem_free[PF_TBUF], nib_full;
     __shared__ uint32_t taddr_s;
     __shared__ int s_e, s_p0, s_nt;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -278,6 +290,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
     if (tid == 0) {
         for (int s = 0; s < PF_STAGES; ++s) mbar_init(&full_bar[s], 1), mbar_init(&stage_free[s], 1 + PF_EPI_WARPS);
         for (int s = 0; s < PF_TBUF; ++s) mbar_init(&mma_done[s], 1), mbar_init(&tmem_free[s], PF_EPI_WARPS);
+        mbar_init(&nib_full, 1);
         fence_barrier_init();
     }
     tc_fence_before();
@@ -289,52 +302,63 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
 
     if (warp == PF_EPI_WARPS) {
         // ------------------------------------------------ producer + MMA issuer
+        // B tiles and token scales go out two stages ahead; the nibbles of the next stage as soon
+        // as this stage's are unpacked.
         const size_t wrow0 = (size_t)e * rows + row0;  // first weight row of the tile
-        const int arb = q8rec_bytes(nblk);
+        uint8_t *const sN = smem + (size_t)PF_STAGES * PF_STAGE_BYTES;
+        auto issue_nib = [&](int st) {
+            mbar_arrive_expect_tx(&nib_full, PF_NIB_BYTES);
+            tma_load_3d(sN, &map_nib, 0, st * PF_KB, (int)wrow0, &nib_full);  // [128 rows][8 blocks][16 B]
+        };
+        auto issue_bx = [&](int st) {
+            const int s = st % PF_STAGES;
+            uint8_t *sB = stage_ptr(s) + PF_A_BYTES;
+            mbar_arrive_expect_tx(&full_bar[s], PF_B_BYTES + PF_DX_BYTES);
+            tma_load_3d(sB, &map_act, 0, p0, 2 * st * PF_KB, &full_bar[s]);            // [16 halves][128 tokens][16 B]
+            tma_load_2d(sB + PF_B_BYTES, &map_dx, st * PF_KB * 4, p0, &full_bar[s]);  // [128 tokens][8 f32]
+        };
+        if (lane == 0) {
+            issue_nib(0);
+            for (int st = 0; st < min(nst, 2); ++st) issue_bx(st);
+        }
         bool ok = true;
         for (int st = 0; st < nst && ok; ++st) {
             const int s = st % PF_STAGES;
-            uint8_t *sp = stage_ptr(s);
-            uint8_t *sA = sp, *sB = sp + PF_A_BYTES, *sN = sB + PF_B_BYTES;
-            float *sdw = reinterpret_cast<float *>(sN + PF_NIB_BYTES);
-            float *sdx = sdw + PF_M * PF_KB;
-            if (st >= PF_STAGES) ok &= fd_mbar_wait(&stage_free[s], ((st / PF_STAGES) - 1) & 1u, a.status);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            uint8_t *sA = stage_ptr(s), *sB = sA + PF_A_BYTES;
             const int kb0 = st * PF_KB, kn = min(PF_KB, nblk - kb0);
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&full_bar[s], PF_NIB_BYTES + PF_B_BYTES);
-                tma_load_3d(sN, &map_nib, 0, kb0, (int)wrow0, &full_bar[s]);  // [128 rows][8 blocks][16 B]
-                tma_load_3d(sB, &map_act, 0, p0, 2 * kb0, &full_bar[s]);     // [16 halves][128 tokens][16 B]
+            const int sa = st + 2;  // the stage whose B tile goes out now
+            if (sa < nst) {
+                if (sa >= PF_STAGES) ok &= fd_mbar_wait(&stage_free[sa % PF_STAGES], ((sa / PF_STAGES) - 1) & 1u, a.status);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                if (lane == 0) issue_bx(sa);
             }
-            // scales of the stage (f32): dw [row][j], dx [token][j]
-            for (int i = lane; i < PF_M * PF_KB; i += 32) {
-                const int r = i / PF_KB, j = i % PF_KB;
-                sdw[i] = j < kn ? f16_bits_to_f32(__ldg(a.scl + (wrow0 + r) * nblk + kb0 + j)) : 0.0f;
-            }
-            for (int i = lane; i < PF_N * PF_KB; i += 32) {
-                const int n = i / PF_KB, j = i % PF_KB;
-                sdx[i] = (n < nt && j < kn)
-                             ? reinterpret_cast<const float *>(a.arec + (size_t)(p0 + n) * arb + nblk * 32)[kb0 + j]
-                             : 0.0f;
-            }
-            ok &= fd_mbar_wait(&full_bar[s], (st / PF_STAGES) & 1u, a.status);
+            ok &= fd_mbar_wait(&nib_full, (uint32_t)st & 1u, a.status);
             if (!__all_sync(0xffffffffu, ok)) break;
-            // unpack: task (row r, block j, half k): 16 int8 at sA + (j * 2 + k) * 2048 + r * 16
-            for (int i = lane; i < PF_M * PF_KB * 2; i += 32) {
-                const int r = i >> 4, j = (i >> 1) & 7, k = i & 1;
-                const int pos = a.swizzled ? (j ^ (r & 7)) : j;  // the tile's rows start at a multiple of 8
+            // unpack: task (row r, block j) -> halves 0, 1 at sA + (2 j + k) * 2048 + r * 16. The 8
+            // lanes of one 16-byte access phase take 8 consecutive rows (distinct write banks) and
+            // blocks whose stored positions differ (distinct read banks): the block is fixed when the
+            // rows are swizzled (position j ^ (r & 7); the tile's rows start at a multiple of 8),
+            // and runs along the diagonal when they are not.
+#pragma unroll 4
+            for (int i = lane; i < PF_M * PF_KB; i += 32) {
+                const int l = i & 7, g = i >> 3, c = g >> 4;
+                const int r = (g & 15) * 8 + l;
+                const int j = a.swizzled ? c : ((l + c) & 7);
+                const int pos = a.swizzled ? (c ^ l) : j;
                 const uint4 nb4 = *reinterpret_cast<const uint4 *>(sN + r * (PF_KB * 16) + pos * 16);
-                const int sh = 4 * k;
-                uint4 o;
-                o.x = nib_to_s8((nb4.x >> sh) & 0x0F0F0F0Fu);
-                o.y = nib_to_s8((nb4.y >> sh) & 0x0F0F0F0Fu);
-                o.z = nib_to_s8((nb4.z >> sh) & 0x0F0F0F0Fu);
-                o.w = nib_to_s8((nb4.w >> sh) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(sA + (j * 2 + k) * (PF_M * 16) + r * 16) = o;
+                uint4 lo, hi;
+                lo.x = nib_to_s8(nb4.x & 0x0F0F0F0Fu), hi.x = nib_to_s8((nb4.x >> 4) & 0x0F0F0F0Fu);
+                lo.y = nib_to_s8(nb4.y & 0x0F0F0F0Fu), hi.y = nib_to_s8((nb4.y >> 4) & 0x0F0F0F0Fu);
+                lo.z = nib_to_s8(nb4.z & 0x0F0F0F0Fu), hi.z = nib_to_s8((nb4.z >> 4) & 0x0F0F0F0Fu);
+                lo.w = nib_to_s8(nb4.w & 0x0F0F0F0Fu), hi.w = nib_to_s8((nb4.w >> 4) & 0x0F0F0F0Fu);
+                *reinterpret_cast<uint4 *>(sA + (2 * j) * (PF_M * 16) + r * 16) = lo;
+                *reinterpret_cast<uint4 *>(sA + (2 * j + 1) * (PF_M * 16) + r * 16) = hi;
             }
-            fence_proxy_async_smem();
-            __threadfence_block();  // the scales above, for the epilogue warps that wait on the MMAs
+            fence_proxy_async_smem();  // the A tile for the tensor core; the nibble reads before the refill
             __syncwarp();
+            if (lane == 0 && st + 1 < nst) issue_nib(st + 1);
+            ok &= fd_mbar_wait(&full_bar[s], (uint32_t)(st / PF_STAGES) & 1u, a.status);
+            if (!__all_sync(0xffffffffu, ok)) break;
             if (lane == 0) {
                 for (int j = 0; j < kn && ok; ++j) {
                     const int b = kb0 + j, buf = b % PF_TBUF;
@@ -357,9 +381,28 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
         float acc[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        // this row's weight scales (f16 pairs): the current stage's 8 and, loaded a stage ahead,
+        // the next 8
+        const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + ((size_t)e * rows + row0 + m) * nblk);
+        const int nw = nblk >> 1;  // f16 pairs per row (nblk is even)
+#define PF_LOAD_DW(st, w0, w1, w2, w3)                                      \
+    {                                                                       \
+        const int k0 = (st) * (PF_KB / 2);                                  \
+        w0 = k0 + 0 < nw ? __ldg(srow + k0 + 0) : 0u;                       \
+        w1 = k0 + 1 < nw ? __ldg(srow + k0 + 1) : 0u;                       \
+        w2 = k0 + 2 < nw ? __ldg(srow + k0 + 2) : 0u;                       \
+        w3 = k0 + 3 < nw ? __ldg(srow + k0 + 3) : 0u;                       \
+    }
+        uint32_t c0, c1, c2, c3, n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+        PF_LOAD_DW(0, c0, c1, c2, c3);
+        if (nst > 1) PF_LOAD_DW(1, n0, n1, n2, n3);
         bool ok = true;
         for (int b = 0; b < nblk; ++b) {
             const int buf = b % PF_TBUF, st = b / PF_KB, s = st % PF_STAGES, j = b % PF_KB;
+            if (j == 0 && b > 0) {
+                c0 = n0, c1 = n1, c2 = n2, c3 = n3;
+                if (st + 1 < nst) PF_LOAD_DW(st + 1, n0, n1, n2, n3);
+            }
             ok &= fd_mbar_wait(&mma_done[buf], (b / PF_TBUF) & 1u, a.status);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
@@ -369,15 +412,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_free[buf]);
-            const float *sdw = reinterpret_cast<const float *>(stage_ptr(s) + PF_A_BYTES + PF_B_BYTES + PF_NIB_BYTES);
-            const float *sdx = sdw + PF_M * PF_KB;
-            const float dw = sdw[m * PF_KB + j];
+            const float *sdx = reinterpret_cast<const float *>(stage_ptr(s) + PF_A_BYTES + PF_B_BYTES);
+            const uint32_t wpair = (j >> 1) == 0 ? c0 : (j >> 1) == 1 ? c1 : (j >> 1) == 2 ? c2 : c3;
+            const float dw = f16_bits_to_f32((uint16_t)((j & 1) ? (wpair >> 16) : (wpair & 0xFFFFu)));
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const float dx = sdx[(cg * 32 + i) * PF_KB + j];
                 acc[i] = __fadd_rn(acc[i], __fmul_rn((float)(int32_t)v[i], __fmul_rn(dw, dx)));
             }
-            if (j == PF_KB - 1 || b == nblk - 1) {  // done with this stage's scales
+            if (j == PF_KB - 1 || b == nblk - 1) {  // done with this stage's token scales
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&stage_free[s]);
             }

@@ -395,6 +395,19 @@ int tensor_map_encode() {
     return 0;
 }
 
+// A 2-D byte tensor map (d0 innermost; stride of dim 1 in bytes), box b0 x b1, no swizzle,
+// out-of-range elements read as zero.
+int map2d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t s1, uint32_t b0, uint32_t b1) {
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {s1};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
 // A 3-D byte tensor map (dims d0 innermost; strides of dims 1 and 2 in bytes), box b0 x b1 x b2,
 // no swizzle, out-of-range elements read as zero.
 int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
@@ -442,12 +455,16 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     if ((rc = launched())) return rc;
     // 3. gate/up and down GEMMs
     const PackedView pk = packed_view(w);
-    CUtensorMap m_gu, m_x, m_dn, m_h;
+    CUtensorMap m_gu, m_x, m_xd, m_dn, m_h, m_hd;
     const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
+    // weight nibbles [rows][blocks][16 B]; activation quants as [halves][rows][16 B] (a chunk's
+    // rows contiguous: the canonical K-major layout); activation block scales [rows][blocks] f32
     if ((rc = map3d(&m_gu, pk.gu_nib, 16, nb, (uint64_t)ne * 2 * w->ff, 16, (uint64_t)nb * 16, 16, PF_KB, PF_M)) ||
         (rc = map3d(&m_x, xperm, 16, pairs, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
+        (rc = map2d(&m_xd, xperm + (size_t)nb * 32, (uint64_t)nb * 4, pairs, xrb, PF_KB * 4, PF_N)) ||
         (rc = map3d(&m_dn, pk.dn_nib, 16, nbh, (uint64_t)ne * w->n_embd, 16, (uint64_t)nbh * 16, 16, PF_KB, PF_M)) ||
-        (rc = map3d(&m_h, hrec, 16, pairs, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)))
+        (rc = map3d(&m_h, hrec, 16, pairs, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)) ||
+        (rc = map2d(&m_hd, hrec + (size_t)nbh * 32, (uint64_t)nbh * 4, pairs, hrb, PF_KB * 4, PF_N)))
         return rc;
     size_t smax = 0;
     if ((rc = fd_smem_max(k_pf_gemm<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm<PF_DN>, &smax))) return rc;
@@ -457,12 +474,12 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     g.counts = counts, g.offsets = offsets, g.n_experts = ne, g.pairs = pairs;
     g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.scl = pk.gu_scl, g.arec = xperm;
     g.nh = nbh, g.hrec = hrec, g.n_embd = w->n_embd, g.status = status;
-    k_pf_gemm<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_gu, m_x, g);
+    k_pf_gemm<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
     if ((rc = launched())) return rc;
     PfArgs d = g;
     d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.scl = pk.dn_scl, d.arec = hrec;
     d.hrec = nullptr, d.y = at<float>(ws, L.ybuf);
-    k_pf_gemm<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_dn, m_h, d);
+    k_pf_gemm<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
     if ((rc = launched())) return rc;
     // 4. slot-order combine
     k_pf_combine<<<4 * num_sms(), 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
