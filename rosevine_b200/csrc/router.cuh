@@ -149,7 +149,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
                                                        int32_t *__restrict__ counts, int32_t *__restrict__ offsets,
                                                        int32_t *__restrict__ order, int32_t *__restrict__ pos_of,
                                                        int32_t *__restrict__ active, int32_t *__restrict__ n_active,
-                                                       int *status) {
+                                                       int *status, int align = 1, int2 *__restrict__ tiles = nullptr,
+                                                       int32_t *__restrict__ n_tiles = nullptr, int tile_rows = 128) {
     __shared__ int s_count[MAX_EXPERTS];
     __shared__ int s_base[MAX_EXPERTS];
     __shared__ int s_warp[32][MAX_EXPERTS];  // per-warp counts within a chunk
@@ -173,7 +174,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
         for (int i = 0; i < MAX_EXPERTS / 32; ++i) {
             int e = lane * (MAX_EXPERTS / 32) + i;
             local[i] = run;
-            run += e < n_experts ? s_count[e] : 0;
+            run += e < n_experts ? (s_count[e] + align - 1) / align * align : 0;
         }
         int incl = run;
 #pragma unroll
@@ -212,6 +213,29 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
             if (e < n_experts && s_count[e] > 0) active[slot++] = e;
         }
         if (lane == 31) *n_active = fin;
+        if (tiles) {
+            // (expert | positions << 8, first position) per tile of up to tile_rows positions
+            int nt_l = 0;
+#pragma unroll
+            for (int i = 0; i < MAX_EXPERTS / 32; ++i) {
+                int e = lane * (MAX_EXPERTS / 32) + i;
+                nt_l += e < n_experts ? (s_count[e] + tile_rows - 1) / tile_rows : 0;
+            }
+            int tinc = nt_l;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                int y = __shfl_up_sync(0xffffffffu, tinc, o);
+                if (lane >= o) tinc += y;
+            }
+            int k = tinc - nt_l;
+            for (int i = 0; i < MAX_EXPERTS / 32; ++i) {
+                int e = lane * (MAX_EXPERTS / 32) + i;
+                if (e >= n_experts) break;
+                for (int c = 0; c < s_count[e]; c += tile_rows)
+                    tiles[k++] = make_int2(e | (min(tile_rows, s_count[e] - c) << 8), s_base[e] + c);
+            }
+            if (lane == 31) *n_tiles = tinc;
+        }
     }
     __syncthreads();
     // stable scatter, one chunk of PLAN_THREADS pairs at a time

@@ -66,11 +66,17 @@ struct Workspace {
     // last-CTA counter at 4, at 12 the running count of tokens routed through the exact
     // fallback, and the decode kernel's grid barrier: arrival count at 64, generation at 128
     // (separate cache lines; the count returns to zero after every barrier).
-    size_t status, lfast, lbound, lexact, ids, wts, sel_ids, sel_wts, sel_flag, xrec, hrec, ybuf, xperm, plan,
-        counts, offsets, order, pos_of, active, n_active, total;
+    size_t status, lfast, lbound, lexact, ids, wts, sel_ids, sel_wts, sel_flag, xrec, hrec, ybuf, xperm, xd, hd,
+        tiles, n_tiles, plan, counts, offsets, order, pos_of, active, n_active, total;
+    // prefill plan positions: the expert groups start at multiples of 4, so at most 3 unused
+    // positions per expert; ppad (a multiple of 4) is the pitch of the block-major scale planes
+    size_t ppos, ppad;
     static constexpr size_t HDR_FALLBACK = 12, HDR_BAR_CNT = 64, HDR_BAR_GEN = 128;
     Workspace(int max_tok, int n_embd, int ff, int ne, int used) {
         const size_t nb = n_embd / QK, nbh = ff / QK, pairs = (size_t)max_tok * used;
+        const bool prefill = max_tok > FD_MAX_TOK;
+        ppos = prefill ? pairs + 3 * (size_t)ne : pairs;
+        ppad = (ppos + 3) / 4 * 4;
         size_t o = 0;
         auto take = [&](size_t bytes) {
             size_t at = o;
@@ -87,13 +93,18 @@ struct Workspace {
         sel_wts = take(pairs * 4);
         sel_flag = take((size_t)max_tok * 4);
         xrec = take((size_t)max_tok * q8rec_bytes((int)nb));
-        hrec = take(pairs * q8rec_bytes((int)nbh));
-        ybuf = take(pairs * n_embd * 4);
-        xperm = max_tok > FD_MAX_TOK ? take(pairs * q8rec_bytes((int)nb)) : o;  // prefill calls only
+        hrec = take(ppos * q8rec_bytes((int)nbh));
+        ybuf = take(ppos * n_embd * 4);
+        // prefill calls only
+        xperm = prefill ? take(ppos * q8rec_bytes((int)nb)) : o;
+        xd = prefill ? take(nb * ppad * 4) : o;
+        hd = prefill ? take(nbh * ppad * 4) : o;
+        tiles = prefill ? take((pairs / 128 + 1 + (size_t)ne) * 8) : o;
+        n_tiles = take(4);
         plan = take(fd_plan_words(std::min(max_tok, FD_MAX_TOK) * used, ne) * 4);
         counts = take((size_t)ne * 4);
         offsets = take((size_t)(ne + 1) * 4);
-        order = take(pairs * 4);
+        order = take(ppos * 4);  // indexed by plan position
         pos_of = take(pairs * 4);
         active = take((size_t)ne * 4);
         n_active = take(4);
@@ -395,14 +406,15 @@ int tensor_map_encode() {
     return 0;
 }
 
-// A 2-D byte tensor map (d0 innermost; stride of dim 1 in bytes), box b0 x b1, no swizzle,
-// out-of-range elements read as zero.
-int map2d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t s1, uint32_t b0, uint32_t b1) {
+// A 2-D tensor map of bytes or f32 (d0 innermost, in elements; stride of dim 1 in bytes), box
+// b0 x b1 elements, no swizzle, out-of-range elements read as zero.
+int map2d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t s1, uint32_t b0, uint32_t b1,
+          CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
     const cuuint64_t dims[2] = {d0, d1};
     const cuuint64_t strides[1] = {s1};
     const cuuint32_t box[2] = {b0, b1};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+    const CUresult r = g_encode(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
@@ -442,43 +454,51 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     if ((rc = rvc_moe_router(w, x_router, x_dtype, bias, bias_stride, n_tok, id, wt, nullptr, nullptr, nullptr, ws,
                              ws_bytes, st)))
         return rc;
+    int2 *tiles = at<int2>(ws, L.tiles);
+    int32_t *n_tiles = at<int32_t>(ws, L.n_tiles);
     k_plan<<<1, PLAN_THREADS, 0, st>>>(id, pairs, ne, counts, offsets, order, pos_of, at<int32_t>(ws, L.active),
-                                       at<int32_t>(ws, L.n_active), status);
+                                       at<int32_t>(ws, L.n_active), status, 4, tiles, n_tiles, PF_N);
     if ((rc = launched())) return rc;
-    // 2. Q8_0 of x in plan order
+    // 2. Q8_0 of x, once per token, to its plan positions
     uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
-    const int gblocks = (int)std::min<long long>(4096, ((long long)pairs * nb + 7) / 8);
+    float *xd = at<float>(ws, L.xd), *hd = at<float>(ws, L.hd);
+    const int ppos = (int)L.ppos, ppad = (int)L.ppad;
+    const int qblocks = (int)std::min<long long>(8 * num_sms(), ((long long)n_tok * nb + 7) / 8);
     if (x_dtype == RVC_BF16)
-        k_pf_gather<uint16_t><<<gblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, order, used, pairs, xperm);
+        k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
+                                                      xd, ppad);
     else
-        k_pf_gather<float><<<gblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, order, used, pairs, xperm);
+        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xd,
+                                                   ppad);
     if ((rc = launched())) return rc;
     // 3. gate/up and down GEMMs
     const PackedView pk = packed_view(w);
     CUtensorMap m_gu, m_x, m_xd, m_dn, m_h, m_hd;
     const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
-    // weight nibbles [rows][blocks][16 B]; activation quants as [halves][rows][16 B] (a chunk's
-    // rows contiguous: the canonical K-major layout); activation block scales [rows][blocks] f32
+    // weight nibbles [rows][blocks][16 B]; activation quants as [halves][positions][16 B] (a
+    // chunk's positions contiguous: the canonical K-major layout); activation block scales
+    // [blocks][positions] f32
     if ((rc = map3d(&m_gu, pk.gu_nib, 16, nb, (uint64_t)ne * 2 * w->ff, 16, (uint64_t)nb * 16, 16, PF_KB, PF_M)) ||
-        (rc = map3d(&m_x, xperm, 16, pairs, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_xd, xperm + (size_t)nb * 32, (uint64_t)nb * 4, pairs, xrb, PF_KB * 4, PF_N)) ||
+        (rc = map3d(&m_x, xperm, 16, ppos, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
+        (rc = map2d(&m_xd, xd, ppad, nb, (uint64_t)ppad * 4, PF_N, PF_KB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
         (rc = map3d(&m_dn, pk.dn_nib, 16, nbh, (uint64_t)ne * w->n_embd, 16, (uint64_t)nbh * 16, 16, PF_KB, PF_M)) ||
-        (rc = map3d(&m_h, hrec, 16, pairs, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_hd, hrec + (size_t)nbh * 32, (uint64_t)nbh * 4, pairs, hrb, PF_KB * 4, PF_N)))
+        (rc = map3d(&m_h, hrec, 16, ppos, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)) ||
+        (rc = map2d(&m_hd, hd, ppad, nbh, (uint64_t)ppad * 4, PF_N, PF_KB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
         return rc;
     size_t smax = 0;
     if ((rc = fd_smem_max(k_pf_gemm<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm<PF_DN>, &smax))) return rc;
     if (smax < (size_t)PF_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
-    const int tiles_y = (pairs + PF_N - 1) / PF_N + ne;  // an upper bound on the (expert, token tile) count
+    const int tiles_y = pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
     PfArgs g{};
-    g.counts = counts, g.offsets = offsets, g.n_experts = ne, g.pairs = pairs;
-    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.scl = pk.gu_scl, g.arec = xperm;
-    g.nh = nbh, g.hrec = hrec, g.n_embd = w->n_embd, g.status = status;
+    g.tiles = tiles, g.n_tiles = n_tiles;
+    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.scl = pk.gu_scl;
+    g.nh = nbh, g.hrec = hrec, g.hd = hd, g.ppad = ppad, g.n_embd = w->n_embd, g.status = status;
+    g.negzero2 = 0x8000000080000000ull;
     k_pf_gemm<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
     if ((rc = launched())) return rc;
     PfArgs d = g;
-    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.scl = pk.dn_scl, d.arec = hrec;
-    d.hrec = nullptr, d.y = at<float>(ws, L.ybuf);
+    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.scl = pk.dn_scl;
+    d.hrec = nullptr, d.hd = nullptr, d.y = at<float>(ws, L.ybuf);
     k_pf_gemm<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
     if ((rc = launched())) return rc;
     // 4. slot-order combine
