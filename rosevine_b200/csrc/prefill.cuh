@@ -49,11 +49,26 @@ namespace rvc {
 constexpr int PF_M = 128;          // rows per tile (tensor-memory lanes)
 constexpr int PF_N = 128;          // tokens per tile (accumulator columns)
 constexpr int PF_KB = 8;           // K-blocks per stage
-constexpr int PF_STAGES = 3;
-constexpr int PF_TBUF = 4;         // tensor-memory accumulators
-constexpr int PF_EPI_WARPS = 8;
-constexpr int PF_THREADS = (PF_EPI_WARPS + 1) * 32;
-constexpr int PF_TMEM_COLS = PF_TBUF * PF_N;  // 512: the whole tensor memory of the SM
+constexpr int PF_A_SLOTS = 2;      // unpacked weight tiles
+constexpr int PF_B_SLOTS = 3;      // activation tiles
+constexpr int PF_DX_SLOTS = 4;     // activation block scales
+constexpr int PF_NIB_SLOTS = 2;    // weight nibbles
+constexpr int PF_TBUF = 2;         // tensor-memory accumulators (ping-pong)
+constexpr int PF_EPI_WARPS = 8;    // warps 0-7
+constexpr int PF_UNPACK_WARPS = 3; // warps 8-10
+constexpr int PF_MMA_WARP = PF_EPI_WARPS + PF_UNPACK_WARPS;  // warp 11: TMA copies and MMAs
+constexpr int PF_THREADS = (PF_MMA_WARP + 1) * 32;
+constexpr int PF_TMEM_COLS = PF_TBUF * PF_N;  // 256 of the SM's 512 columns
+
+// The tensor-memory accumulators start every block at the bits of 1.5 * 2^23: the int32 sum
+// C + D of a block dot D (|D| < 2^22) then reads as the float 1.5 * 2^23 + D exactly, and one
+// exact subtraction gives (float)D.
+constexpr uint32_t PF_MAGIC_BITS = 0x4B400000u;
+constexpr float PF_MAGIC = 12582912.0f;
+// An activation block with quants q, scale d and sum(q) = qs enters the GEMM as the pair
+// (d, -(C + 8 qs)): the MMA of the unsigned nibbles n gives C + sum n q, and adding the offset
+// leaves sum (n - 8) q exactly (all values integers below 2^24).
+__device__ __forceinline__ float2 pf_scale_offset(float d, int qs) { return make_float2(d, -(PF_MAGIC + 8.0f * (float)qs)); }
 
 // ------------------------------------------------------------------ tcgen05 primitives
 __device__ __forceinline__ void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {  // one full warp
@@ -223,12 +238,12 @@ __global__ void __launch_bounds__(128) k_debug_mma_i8(const int8_t *__restrict__
 
 // ------------------------------------------------------------------ quantise + scatter
 // Q8_0 of x, once per token: warp task (token t, block b) quantises the block and writes it into
-// the records of the token's `used` plan positions pos_of[t used + j], with the block scale also
-// in the block-major plane xd[b][position] the GEMM's scale tiles come from.
+// the records of the token's `used` plan positions pos_of[t used + j], and the block's (scale,
+// offset) pair into the block-major plane xso[b][position] the GEMM's scale tiles come from.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int n_embd, int n_tok, int used,
                                                   const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
-                                                  float *__restrict__ xd, int ppad) {
+                                                  float2 *__restrict__ xso, int ppad) {
     const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = n_tok * nb;
@@ -238,11 +253,11 @@ __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int 
         uint16_t dbits;
         int qsum;
         const int8_t q = quant_q8_lane(v, &dbits, &qsum);
-        const float d = f16_bits_to_f32(dbits);
+        const float2 so = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
         for (int j = 0; j < used; ++j) {
             const int k = __ldg(pos_of + t * used + j);
             q8rec_store(xperm + (size_t)k * xrb, nb, b, lane, q, dbits, qsum);
-            if (lane == 0) xd[(size_t)b * ppad + k] = d;
+            if (lane == 0) xso[(size_t)b * ppad + k] = so;
         }
     }
 }
@@ -275,10 +290,11 @@ struct PfArgs {
     int rows_per_expert;  // 2 ff (gate/up) or n_embd (down)
     int nblk;             // K blocks (n_embd / 32 or ff / 32)
     int swizzled;         // the nibble plane's blocks are XOR-swizzled per row (gate/up)
+    const uint8_t *nib;   // weight nibbles [E][rows][nblk][16] (for the L2 prefetch; copies go through the map)
     const uint16_t *scl;  // weight scales [E][rows][nblk] (f16 bits)
     int nh;               // (gate/up) h blocks per pair (ff / 32): the h record geometry
     uint8_t *hrec;        // (gate/up) out: h records by plan position
-    float *hd;            // (gate/up) out: h block scales, block-major [nh][ppad]
+    float2 *hso;          // (gate/up) out: h block (scale, offset) pairs, block-major [nh][ppad]
     int ppad;
     float *y;             // (down) out: [positions][n_embd]
     int n_embd;
@@ -288,23 +304,21 @@ struct PfArgs {
 
 constexpr int PF_GU = 0, PF_DN = 1;
 
-// Shared memory of one stage: unpacked A (8 blocks x 2 halves x 128 rows x 16 B), B (same for
-// 128 tokens), the tokens' block scales (8 blocks x 128 tokens f32); after the stages one
-// buffer for the nibbles of A (128 rows x 8 blocks x 16 B), refilled as soon as they are
-// unpacked, and the constant A tile of -8 (one block).
+// Shared memory: rings of unpacked A tiles (8 blocks x 2 halves x 128 rows x 16 B), B tiles
+// (the same for 128 positions), the positions' block scales (8 blocks x 128 f32) and weight
+// nibbles (128 rows x 8 blocks x 16 B), and the constant A tile of -8 (one block).
 constexpr int PF_A_BYTES = PF_KB * 2 * PF_M * 16;  // 32 KB
 constexpr int PF_B_BYTES = PF_KB * 2 * PF_N * 16;  // 32 KB
 constexpr int PF_NIB_BYTES = PF_M * PF_KB * 16;    // 16 KB
-constexpr int PF_DX_BYTES = PF_N * PF_KB * 4;      // 4 KB
-constexpr int PF_C_BYTES = 2 * PF_M * 16;          // 4 KB
-constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_DX_BYTES;
-constexpr int PF_SMEM_BYTES = PF_STAGES * PF_STAGE_BYTES + PF_NIB_BYTES + PF_C_BYTES + 1024;  // + alignment slack
+constexpr int PF_DX_BYTES = PF_N * PF_KB * 8;      // 8 KB: (scale, offset) per position and block
+constexpr int PF_OFF_B = PF_A_SLOTS * PF_A_BYTES;
+constexpr int PF_OFF_DX = PF_OFF_B + PF_B_SLOTS * PF_B_BYTES;
+constexpr int PF_OFF_NIB = PF_OFF_DX + PF_DX_SLOTS * PF_DX_BYTES;
+constexpr int PF_OFF_C = PF_OFF_NIB + PF_NIB_SLOTS * PF_NIB_BYTES;
+constexpr int PF_SMEM_BYTES = PF_OFF_C + 1024;  // + alignment slack
+static_assert(PF_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm");
+static_assert(4 * 32 * PF_N * 4 <= PF_OFF_B + PF_B_SLOTS * PF_B_BYTES, "gate/up staging of the outputs");
 
-// The tensor-memory accumulators start every block at the bits of 1.5 * 2^23: the int32 sum
-// C + D of a block dot D (|D| < 2^22) then reads as the float 1.5 * 2^23 + D exactly, and one
-// exact subtraction gives (float)D.
-constexpr uint32_t PF_MAGIC_BITS = 0x4B400000u;
-constexpr float PF_MAGIC = 12582912.0f;
 
 // Bounded mbarrier wait, inline (a call would make the caller save its live accumulators).
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, int *status) {
@@ -357,18 +371,35 @@ __device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void named_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
+// All threads of the unpack warps: the AND of `ok` over them (a barrier, id 7).
+__device__ __forceinline__ bool unpack_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 7, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "n"(PF_UNPACK_WARPS * 32)
+        : "memory");
+    return r != 0;
+}
+
 // One (expert, 128 weight rows, up to 128 plan positions) tile per CTA. Per 32-column block b:
 //   D = C + u8(n) . q     (tcgen05.mma kind::i8, A unsigned: the nibbles as stored)
 //   D = D + (-8) . q      (A signed: a constant tile), so D = C + sum (n - 8) q exactly;
 // the epilogue warps read D, put C back for block b + 4, and accumulate
 //   acc = acc + ((float)(D - C) * (dw_b * dx_b))   (each operation rounded, as the reference).
+// Roles: warps 0-7 epilogue, 8-10 unpack the nibbles of stage st into A slot st % 2, warp 11
+// (one lane) copies B tiles and scales two stages ahead and issues the MMAs. Barriers per ring
+// slot: nib_full (TMA -> unpack), a_full (unpack -> MMA), a_free (MMAs done -> unpack),
+// b_full (TMA -> MMA; the epilogue learns of the scales through mma_done), b_free (MMAs done ->
+// TMA), dx_free (epilogue -> TMA), mma_done / tmem_free per accumulator.
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant__ CUtensorMap map_nib,
                                                            const __grid_constant__ CUtensorMap map_act,
                                                            const __grid_constant__ CUtensorMap map_dx, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full_bar[PF_STAGES], stage_free[PF_STAGES], mma_done[PF_TBUF], tmem_free[PF_TBUF], nib_full;
+    __shared__ uint64_t nib_full[PF_NIB_SLOTS], a_full[PF_A_SLOTS], a_free[PF_A_SLOTS], b_full[PF_B_SLOTS],
+        b_free[PF_B_SLOTS], dx_free[PF_DX_SLOTS], mma_done[PF_TBUF], tmem_free[PF_TBUF];
     __shared__ uint32_t taddr_s;
     if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -379,68 +410,111 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
     const int ncg = (nt + 31) >> 5;  // 32-token column groups holding tokens
     const int nch = (nt + 63) >> 6;  // 64-token column halves holding tokens (epilogue warps 4 ch .. + 3)
     const int nst = (nblk + PF_KB - 1) / PF_KB;
-    uint8_t *const sN = smem + (size_t)PF_STAGES * PF_STAGE_BYTES;
-    uint8_t *const sC = sN + PF_NIB_BYTES;
+    const int wrow0 = e * rows + row0;  // first weight row of the tile
 
     if (warp == 0) {
         tmem_alloc(&taddr_s, PF_TMEM_COLS);
         tmem_relinquish();
     }
-    if (tid == 0) {
-        for (int s = 0; s < PF_STAGES; ++s) mbar_init(&full_bar[s], 1), mbar_init(&stage_free[s], 1 + 4 * nch);
+    if (tid == PF_MMA_WARP * 32) {
+        for (int s = 0; s < PF_NIB_SLOTS; ++s) mbar_init(&nib_full[s], 1);
+        for (int s = 0; s < PF_A_SLOTS; ++s) mbar_init(&a_full[s], 1), mbar_init(&a_free[s], 1);
+        for (int s = 0; s < PF_B_SLOTS; ++s) mbar_init(&b_full[s], 1), mbar_init(&b_free[s], 1);
+        for (int s = 0; s < PF_DX_SLOTS; ++s) mbar_init(&dx_free[s], 4 * nch);
         for (int s = 0; s < PF_TBUF; ++s) mbar_init(&mma_done[s], 1), mbar_init(&tmem_free[s], 4 * nch);
-        mbar_init(&nib_full, 1);
         fence_barrier_init();
-    }
-    if (warp == PF_EPI_WARPS) {  // the constant tile: int8 -8 everywhere
-        for (int i = lane; i < PF_C_BYTES / 16; i += 32)
-            reinterpret_cast<uint4 *>(sC)[i] = make_uint4(0xF8F8F8F8u, 0xF8F8F8F8u, 0xF8F8F8F8u, 0xF8F8F8F8u);
-        fence_proxy_async_smem();
+        // the whole weight tile (rows contiguous in the nibble plane) and its scales toward L2
+        bulk_prefetch_l2(a.nib + (size_t)wrow0 * nblk * 16, (uint32_t)(PF_M * nblk * 16));
+        bulk_prefetch_l2(a.scl + (size_t)wrow0 * nblk, (uint32_t)(PF_M * nblk * 2) & ~15u);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t taddr = taddr_s;
-    auto stage_ptr = [&](int s) { return smem + (size_t)s * PF_STAGE_BYTES; };
 
-    if (warp == PF_EPI_WARPS) {
-        // ------------------------------------------------ producer + MMA issuer
-        // B tiles and token scales go out two stages ahead; the nibbles of the next stage as soon
-        // as this stage's are unpacked.
-        const uint32_t id_u = idesc_i8(PF_M, ncg * 32, false), id_s = idesc_i8(PF_M, ncg * 32, true);
-        const uint64_t dC = umma_desc(sC, PF_M * 16, 128);
-        const int wrow0 = e * rows + row0;  // first weight row of the tile
-        auto issue_nib = [&](int st) {
-            mbar_arrive_expect_tx(&nib_full, PF_NIB_BYTES);
-            tma_load_3d(sN, &map_nib, 0, st * PF_KB, wrow0, &nib_full);  // [128 rows][8 blocks][16 B]
-        };
-        auto issue_bx = [&](int st) {
-            const int s = st % PF_STAGES;
-            uint8_t *sB = stage_ptr(s) + PF_A_BYTES;
-            mbar_arrive_expect_tx(&full_bar[s], PF_B_BYTES + PF_DX_BYTES);
-            tma_load_3d(sB, &map_act, 0, p0, 2 * st * PF_KB, &full_bar[s]);      // [16 halves][128 tokens][16 B]
-            tma_load_2d(sB + PF_B_BYTES, &map_dx, p0, st * PF_KB, &full_bar[s]);  // [8 blocks][128 tokens] f32
-        };
+    if (warp == PF_MMA_WARP) {
+        // ------------------------------------------------ TMA copies of B and scales, MMAs
         if (lane == 0) {
-            issue_nib(0);
+            const uint32_t id_u = idesc_i8(PF_M, ncg * 32, false);
+            auto issue_bx = [&](int st) {
+                uint8_t *sB = smem + PF_OFF_B + (st % PF_B_SLOTS) * PF_B_BYTES;
+                uint8_t *sX = smem + PF_OFF_DX + (st % PF_DX_SLOTS) * PF_DX_BYTES;
+                uint64_t *bar = &b_full[st % PF_B_SLOTS];
+                mbar_arrive_expect_tx(bar, PF_B_BYTES + PF_DX_BYTES);
+                tma_load_3d(sB, &map_act, 0, p0, 2 * st * PF_KB, bar);  // [16 halves][128 positions][16 B]
+                tma_load_2d(sX, &map_dx, 2 * p0, st * PF_KB, bar);      // [8 blocks][128 positions] f32 pairs
+            };
             for (int st = 0; st < min(nst, 2); ++st) issue_bx(st);
+            bool ok = true;
+            for (int st = 0; st < nst && ok; ++st) {
+                const int sa = st % PF_A_SLOTS, sb = st % PF_B_SLOTS;
+                const int kb0 = st * PF_KB, kn = min(PF_KB, nblk - kb0);
+                ok = pf_wait(&a_full[sa], (uint32_t)(st / PF_A_SLOTS) & 1u, a.status) &&
+                     pf_wait(&b_full[sb], (uint32_t)(st / PF_B_SLOTS) & 1u, a.status);
+                const uint8_t *sA = smem + sa * PF_A_BYTES, *sB = smem + PF_OFF_B + sb * PF_B_BYTES;
+                for (int j = 0; j < kn && ok; ++j) {
+                    const int b = kb0 + j, buf = b % PF_TBUF;
+                    // Issued only once the epilogue has read block b - 1 (and put C back in its
+                    // accumulator): a tcgen05.ld or .st waits for every MMA in flight, so no MMA
+                    // may be queued while the epilogue moves an accumulator (measured on B200);
+                    // the epilogue's arithmetic on block b - 1 then overlaps this MMA.
+                    // tmem_free[k] completes phase 0 at the initial fill, phase p + 1 once block
+                    // 2 p + k has been read.
+                    ok = b == 0 ? pf_wait(&tmem_free[0], 0, a.status)
+                                : pf_wait(&tmem_free[(b - 1) % PF_TBUF], (uint32_t)((b - 1) / PF_TBUF + 1) & 1u, a.status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t dB = umma_desc(sB + j * 2 * (PF_N * 16), PF_N * 16, 128);
+                    mma_i8(taddr + buf * PF_N, umma_desc(sA + j * 2 * (PF_M * 16), PF_M * 16, 128), dB, id_u, true);
+                    mma_commit(&mma_done[buf]);
+                }
+                if (!ok) break;
+                mma_commit(&a_free[sa]);
+                mma_commit(&b_free[sb]);
+                // B of stage st + 2 into the slot of stage st - 1 (its MMAs are in flight or done),
+                // its scales into the slot of stage st - 2 (the epilogue is past it by now)
+                const int sn = st + 2;
+                if (sn < nst) {
+                    if (sn >= PF_B_SLOTS)
+                        ok &= pf_wait(&b_free[sn % PF_B_SLOTS], (uint32_t)(sn / PF_B_SLOTS - 1) & 1u, a.status);
+                    if (ok && sn >= PF_DX_SLOTS)
+                        ok &= pf_wait(&dx_free[sn % PF_DX_SLOTS], (uint32_t)(sn / PF_DX_SLOTS - 1) & 1u, a.status);
+                    if (ok) issue_bx(sn);
+                }
+            }
+            if (!ok) set_status(a.status, STATUS_TIMEOUT);
         }
+        __syncwarp();
+    } else if (warp >= PF_EPI_WARPS) {
+        // ------------------------------------------------ unpack
+        const int ut = tid - PF_EPI_WARPS * 32;  // 0 .. 95
+        auto issue_nib = [&](int st) {
+            uint64_t *bar = &nib_full[st % PF_NIB_SLOTS];
+            mbar_arrive_expect_tx(bar, PF_NIB_BYTES);
+            tma_load_3d(smem + PF_OFF_NIB + (st % PF_NIB_SLOTS) * PF_NIB_BYTES, &map_nib, 0, st * PF_KB, wrow0,
+                        bar);  // [128 rows][8 blocks][16 B]
+        };
+        if (ut == 0)
+            for (int st = 0; st < min(nst, PF_NIB_SLOTS); ++st) issue_nib(st);
         bool ok = true;
-        for (int st = 0; st < nst && ok; ++st) {
-            const int s = st % PF_STAGES;
-            uint8_t *sA = stage_ptr(s), *sB = sA + PF_A_BYTES;
-            const int kb0 = st * PF_KB, kn = min(PF_KB, nblk - kb0);
-            // slot s last held stage st - 3, complete since the previous iteration's wait
-            ok &= pf_wait(&nib_full, (uint32_t)st & 1u, a.status);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            // unpack: task (row r, block j) -> nibble bytes split into halves 0, 1 at
+        for (int st = 0; st < nst; ++st) {
+            const int sa = st % PF_A_SLOTS, sn = st % PF_NIB_SLOTS;
+            ok = pf_wait(&nib_full[sn], (uint32_t)(st / PF_NIB_SLOTS) & 1u, a.status);
+            if (ok && st >= PF_A_SLOTS) ok = pf_wait(&a_free[sa], (uint32_t)(st / PF_A_SLOTS - 1) & 1u, a.status);
+            if (!unpack_all(ok)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *sN = smem + PF_OFF_NIB + sn * PF_NIB_BYTES;
+            uint8_t *sA = smem + sa * PF_A_BYTES;
+            // task (row r, block j) -> nibble bytes split into halves 0, 1 at
             // sA + (2 j + k) * 2048 + r * 16. The 8 lanes of one 16-byte access phase take 8
             // consecutive rows (distinct write banks) and blocks whose stored positions differ
             // (distinct read banks): the block is fixed when the rows are swizzled (position
             // j ^ (r & 7); the tile's rows start at a multiple of 8), and runs along the diagonal
             // when they are not.
 #pragma unroll 2
-            for (int i = lane; i < PF_M * PF_KB; i += 32) {
+            for (int i = ut; i < PF_M * PF_KB; i += PF_UNPACK_WARPS * 32) {
                 const int l = i & 7, g = i >> 3, c = g >> 4;
                 const int r = (g & 15) * 8 + l;
                 const int j = a.swizzled ? c : ((l + c) & 7);
@@ -454,33 +528,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
                 *reinterpret_cast<uint4 *>(sA + (2 * j + 1) * (PF_M * 16) + r * 16) = hi;
             }
             fence_proxy_async_smem();  // the A tile for the tensor core; the nibble reads before the refill
-            __syncwarp();
-            if (lane == 0 && st + 1 < nst) issue_nib(st + 1);
-            ok &= pf_wait(&full_bar[s], (uint32_t)(st / PF_STAGES) & 1u, a.status);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            if (lane == 0) {
-                for (int j = 0; j < kn && ok; ++j) {
-                    const int b = kb0 + j, buf = b % PF_TBUF;
-                    // the epilogue has read the accumulator's previous block and put C back
-                    ok &= pf_wait(&tmem_free[buf], (b / PF_TBUF) & 1u, a.status);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint64_t dB = umma_desc(sB + j * 2 * (PF_N * 16), PF_N * 16, 128);
-                    mma_i8(taddr + buf * PF_N, umma_desc(sA + j * 2 * (PF_M * 16), PF_M * 16, 128), dB, id_u, true);
-                    mma_i8(taddr + buf * PF_N, dC, dB, id_s, true);
-                    mma_commit(&mma_done[buf]);
-                }
-                mma_commit(&stage_free[s]);  // the stage's buffers are free once its MMAs are done
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            // B tile of stage st + 2 into the slot of stage st - 1, once that stage is consumed (its
-            // MMAs and the epilogue's reads of its scales): the unpack of st + 1 then overlaps the
-            // epilogue of st
-            const int sa = st + 2;
-            if (ok && sa < nst) {
-                if (sa >= PF_STAGES) ok &= pf_wait(&stage_free[sa % PF_STAGES], ((sa / PF_STAGES) - 1) & 1u, a.status);
-                if (!__all_sync(0xffffffffu, ok)) break;
-                if (lane == 0) issue_bx(sa);
+            unpack_all(true);
+            if (ut == 0) {
+                mbar_arrive(&a_full[sa]);
+                if (st + PF_NIB_SLOTS < nst) issue_nib(st + PF_NIB_SLOTS);
             }
         }
         if (!ok) set_status(a.status, STATUS_TIMEOUT);
@@ -503,68 +554,61 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
         float2 acc[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
-        // this row's weight scales (f16 pairs), 8 per stage: loaded at the stage's start from L1,
-        // where a prefetch one stage earlier has put them (no registers held across the stage)
-        const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + ((size_t)e * rows + row0 + m) * nblk);
-        const int nw = nblk >> 1;  // f16 pairs per row (nblk is even)
-        uint32_t c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+        // this row's weight scales (f16): one per block from L1, where a prefetch a stage ahead
+        // has put them
+        const uint16_t *srow = a.scl + ((size_t)e * rows + row0 + m) * nblk;
         asm volatile("prefetch.global.L1 [%0];" ::"l"(srow));
-        const float2 negc = make_float2(-PF_MAGIC, -PF_MAGIC);
         const uint64_t nz2 = a.negzero2;
         bool ok = true;
         for (int b = 0; b < nblk; ++b) {
-            const int buf = b % PF_TBUF, st = b / PF_KB, s = st % PF_STAGES, j = b % PF_KB;
+            const int buf = b % PF_TBUF, st = b / PF_KB, j = b % PF_KB;
             if (j == 0) {
-                const int k0 = st * (PF_KB / 2);
-                c0 = k0 + 0 < nw ? __ldg(srow + k0 + 0) : 0u;
-                c1 = k0 + 1 < nw ? __ldg(srow + k0 + 1) : 0u;
-                c2 = k0 + 2 < nw ? __ldg(srow + k0 + 2) : 0u;
-                c3 = k0 + 3 < nw ? __ldg(srow + k0 + 3) : 0u;
-                if (k0 + PF_KB / 2 < nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + k0 + PF_KB / 2));
-                if (k0 + PF_KB / 2 + 3 < nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + k0 + PF_KB / 2 + 3));
+                if (b + PF_KB < nblk) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + b + PF_KB));
+                if (b + 2 * PF_KB - 1 < nblk) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + b + 2 * PF_KB - 1));
             }
+            const float dw = f16_bits_to_f32(__ldg(srow + b));
             ok &= pf_wait(&mma_done[buf], (b / PF_TBUF) & 1u, a.status);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const float4 *sdx = reinterpret_cast<const float4 *>(stage_ptr(s) + PF_A_BYTES + PF_B_BYTES) +
-                                (j * PF_N + ch * 64) / 4;
-            const uint32_t wpair = (j >> 1) == 0 ? c0 : (j >> 1) == 1 ? c1 : (j >> 1) == 2 ? c2 : c3;
-            const float dw = f16_bits_to_f32((uint16_t)((j & 1) ? (wpair >> 16) : (wpair & 0xFFFFu)));
+            // (scale, offset) pairs of this warp's positions for block j: float4 k holds positions
+            // 2k and 2k + 1
+            const float4 *sso = reinterpret_cast<const float4 *>(smem + PF_OFF_DX + (st % PF_DX_SLOTS) * PF_DX_BYTES) +
+                                (j * PF_N + ch * 64) / 2;
             const float2 dw2 = make_float2(dw, dw);
-            // 16 columns at a time (4 chunks when both groups hold tokens); after the last read
-            // C goes back for block b + 4
-            const int nck = 2 * ng;
+            // both 32-column groups read, C put back, the MMA of block b + 1 released; then the
+            // arithmetic of block b overlaps that MMA
+            uint32_t v0[32], v1[32];
+            tmem_ld32(tw + buf * PF_N, v0);
+            if (ng > 1) tmem_ld32(tw + buf * PF_N + 32, v1);
+            tmem_ld_wait(v0);
+            if (ng > 1) tmem_ld_wait(v1);
+            tmem_fill32(tw + buf * PF_N, PF_MAGIC_BITS);
+            if (ng > 1) tmem_fill32(tw + buf * PF_N + 32, PF_MAGIC_BITS);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_free[buf]);
 #pragma unroll
-            for (int ck = 0; ck < 4; ++ck) {
-                if (ck < nck) {
-                    uint32_t v[16];
-                    tmem_ld16(tw + buf * PF_N + ck * 16, v);
-                    tmem_ld_wait(v);
-                    if (ck == nck - 1) {
-                        tmem_fill32(tw + buf * PF_N, PF_MAGIC_BITS);
-                        if (ng > 1) tmem_fill32(tw + buf * PF_N + 32, PF_MAGIC_BITS);
-                        tmem_st_wait();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tmem_free[buf]);
-                    }
+            for (int g = 0; g < 2; ++g) {
+                if (g < ng) {
+                    const uint32_t *v = g == 0 ? v0 : v1;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 dx = sdx[ck * 4 + q];
-                        const float2 s0 = f2_mul(dw2, make_float2(dx.x, dx.y));
-                        const float2 s1 = f2_mul(dw2, make_float2(dx.z, dx.w));
-                        const float2 t0 =
-                            f2_add(make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), negc);
-                        const float2 t1 =
-                            f2_add(make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), negc);
-                        acc[ck * 8 + 2 * q] = f2_add(acc[ck * 8 + 2 * q], f2_prod(t0, s0, nz2));
-                        acc[ck * 8 + 2 * q + 1] = f2_add(acc[ck * 8 + 2 * q + 1], f2_prod(t1, s1, nz2));
+                    for (int q = 0; q < 8; ++q) {  // positions 4 q .. 4 q + 3 of the group
+                        const float4 L0 = sso[g * 16 + 2 * q], L1 = sso[g * 16 + 2 * q + 1];
+                        const float2 s0 = f2_mul(dw2, make_float2(L0.x, L0.z));
+                        const float2 s1 = f2_mul(dw2, make_float2(L1.x, L1.z));
+                        const float2 t0 = f2_add(make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])),
+                                                 make_float2(L0.y, L0.w));
+                        const float2 t1 = f2_add(make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])),
+                                                 make_float2(L1.y, L1.w));
+                        acc[g * 16 + 2 * q] = f2_add(acc[g * 16 + 2 * q], f2_prod(t0, s0, nz2));
+                        acc[g * 16 + 2 * q + 1] = f2_add(acc[g * 16 + 2 * q + 1], f2_prod(t1, s1, nz2));
                     }
                 }
             }
             if (j == PF_KB - 1 || b == nblk - 1) {  // done with this stage's token scales
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&stage_free[s]);
+                if (lane == 0) mbar_arrive(&dx_free[st % PF_DX_SLOTS]);
             }
         }
         if (!ok) set_status(a.status, STATUS_TIMEOUT);
@@ -582,7 +626,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
             }
         } else {
             // rows: unit u = m / 64 of the tile; m % 64 < 32 gate, else up; column m % 32.
-            // Both go through shared memory (stage 0, free now): [gate/up][2 units][32 columns]
+            // Both go through shared memory (the A and B rings, free now): [gate/up][2 units][32 columns]
             // [128 tokens], so that no accumulator is live across the quantisation calls.
             float *sg = reinterpret_cast<float *>(smem);
             const int nthr = nch * 4 * 32;
@@ -606,7 +650,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
                     const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);  // the warp's 32 lanes: one block
                     if (n < nt) {
                         q8rec_store(a.hrec + (size_t)(p0 + n) * hrb, a.nh, q, lane, qv, dbits, qsum);
-                        if (lane == 0) a.hd[(size_t)q * a.ppad + p0 + n] = f16_bits_to_f32(dbits);
+                        if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + n] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
                     }
                 }
             }
@@ -615,6 +659,197 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(taddr, PF_TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ grouped GEMM, register accumulators
+// The same tiles, with the block dots from mma.sync.m16n8k32 (u8 nibbles x s8 quants, s32
+// accumulators in registers): each compute warp multiplies, scales and accumulates its own
+// 32 rows x 64 positions, so a block's integers never leave the registers that receive them.
+// A fragments come straight from the nibble tile: the 32-bit word at byte 4 (lane % 4) of a row's
+// block holds elements 4 (lane % 4) .. + 3 in its low nibbles and the same + 16 in its high
+// nibbles, which are exactly the a0 / a2 (a1 / a3 for row + 8) registers of the fragment.
+// Every operand arrives by TMA; the compute warps wait once per stage of 8 blocks.
+constexpr int PM_WARPS = 8;  // 4 row groups of 32 x 2 position halves of 64
+constexpr int PM_THREADS = (PM_WARPS + 1) * 32;
+constexpr int PM_STAGES = 3;
+constexpr int PM_OFF_B = PF_NIB_BYTES;
+constexpr int PM_OFF_SO = PM_OFF_B + PF_B_BYTES;
+constexpr int PM_STAGE_BYTES = PM_OFF_SO + PF_DX_BYTES;  // 56 KB
+constexpr int PM_SMEM_BYTES = PM_STAGES * PM_STAGE_BYTES + 1024;
+constexpr int PM_H_PITCH = 33;  // gate/up staging [unit][gate|up][position][33]
+static_assert(PM_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm_ms");
+static_assert(2 * 2 * PF_N * PM_H_PITCH * 4 <= PM_STAGES * PM_STAGE_BYTES, "gate/up staging");
+
+// d = a . b + (c, c, c, c): 16 x 8 s32 from 16 x 32 u8 (row-major) and 32 x 8 s8 (column-major).
+__device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1, uint32_t c) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_constant__ CUtensorMap map_nib,
+                                                              const __grid_constant__ CUtensorMap map_act,
+                                                              const __grid_constant__ CUtensorMap map_so, PfArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[PM_STAGES], empty[PM_STAGES];
+    if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nblk = a.nblk, rows = a.rows_per_expert;
+    const int row0 = blockIdx.x * PF_M;
+    const int2 td = __ldg(a.tiles + blockIdx.y);
+    const int e = td.x & 0xFF, nt = td.x >> 8, p0 = td.y;
+    const int nch = (nt + 63) >> 6;  // position halves holding tokens (compute warps 4 ch .. + 3)
+    const int nst = (nblk + PF_KB - 1) / PF_KB;
+    const int wrow0 = e * rows + row0;
+    if (tid == PM_WARPS * 32) {
+        for (int s = 0; s < PM_STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 4 * nch);
+        fence_barrier_init();
+        bulk_prefetch_l2(a.nib + (size_t)wrow0 * nblk * 16, (uint32_t)(PF_M * nblk * 16));
+        bulk_prefetch_l2(a.scl + (size_t)wrow0 * nblk, (uint32_t)(PF_M * nblk * 2) & ~15u);
+    }
+    __syncthreads();
+
+    if (warp == PM_WARPS) {
+        // ------------------------------------------------ producer: one lane issues every copy
+        if (lane == 0) {
+            bool ok = true;
+            for (int st = 0; st < nst && ok; ++st) {
+                const int s = st % PM_STAGES;
+                if (st >= PM_STAGES) ok = pf_wait(&empty[s], (uint32_t)(st / PM_STAGES - 1) & 1u, a.status);
+                if (!ok) break;
+                uint8_t *base = smem + s * PM_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], PM_STAGE_BYTES);
+                tma_load_3d(base, &map_nib, 0, st * PF_KB, wrow0, &full[s]);                // [128 rows][8 blocks][16 B]
+                tma_load_3d(base + PM_OFF_B, &map_act, 0, p0, 2 * st * PF_KB, &full[s]);    // [16 halves][128 positions][16 B]
+                tma_load_2d(base + PM_OFF_SO, &map_so, 2 * p0, st * PF_KB, &full[s]);       // [8 blocks][128 positions][2] f32
+            }
+            if (!ok) set_status(a.status, STATUS_TIMEOUT);
+        }
+        __syncwarp();
+    } else if ((warp >> 2) < nch) {
+        // ------------------------------------------------ compute
+        const int wr = warp & 3, wc = warp >> 2;
+        const int g = lane >> 2, tq = lane & 3;
+        const int nj = min(8, (nt - 64 * wc + 7) >> 3);  // 8-position fragments holding tokens
+        float2 acc[2][8][2];  // [row fragment][position fragment][rows g, g + 8]: positions 2 tq, 2 tq + 1
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[i][jj][0] = acc[i][jj][1] = make_float2(0.0f, 0.0f);
+        // the thread's 4 rows: 32 wr + 16 i + 8 h + g
+        const uint16_t *srow = a.scl + ((size_t)wrow0 + 32 * wr + g) * nblk;
+        const uint64_t nz2 = a.negzero2;
+        bool ok = true;
+        for (int st = 0; st < nst; ++st) {
+            const int s = st % PM_STAGES;
+            if (lane == 0) ok = pf_wait(&full[s], (uint32_t)(st / PM_STAGES) & 1u, a.status);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const uint8_t *sN = smem + s * PM_STAGE_BYTES, *sB = sN + PM_OFF_B;
+            const float4 *sSO = reinterpret_cast<const float4 *>(sN + PM_OFF_SO);
+            const int kn = min(PF_KB, nblk - st * PF_KB);
+            for (int jb = 0; jb < kn; ++jb) {
+                const int b = st * PF_KB + jb;
+                float dw[2][2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) dw[i][h] = f16_bits_to_f32(__ldg(srow + (size_t)(16 * i + 8 * h) * nblk + b));
+                uint32_t af[2][4];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int r = 32 * wr + 16 * i + g;  // r and r + 8 share r & 7: one swizzled position
+                    const int pos = a.swizzled ? (jb ^ (r & 7)) : jb;
+                    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(sN + r * (PF_KB * 16) + pos * 16 + 4 * tq);
+                    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(sN + (r + 8) * (PF_KB * 16) + pos * 16 + 4 * tq);
+                    af[i][0] = w0 & 0x0F0F0F0Fu, af[i][1] = w1 & 0x0F0F0F0Fu;
+                    af[i][2] = (w0 >> 4) & 0x0F0F0F0Fu, af[i][3] = (w1 >> 4) & 0x0F0F0F0Fu;
+                }
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    if (jj < nj) {
+                        const int n = 64 * wc + 8 * jj + g;  // the B column this lane supplies
+                        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sB + (2 * jb) * (PF_N * 16) + n * 16 + 4 * tq);
+                        const uint32_t b1 =
+                            *reinterpret_cast<const uint32_t *>(sB + (2 * jb + 1) * (PF_N * 16) + n * 16 + 4 * tq);
+                        // (scale, offset) of positions 64 wc + 8 jj + 2 tq and + 1
+                        const float4 so = sSO[(jb * PF_N + 64 * wc + 8 * jj + 2 * tq) >> 1];
+                        const float2 off = make_float2(so.y, so.w), dx = make_float2(so.x, so.z);
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            uint32_t d[4];
+                            mma_u8s8(d, af[i][0], af[i][1], af[i][2], af[i][3], b0, b1, PF_MAGIC_BITS);
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const float2 sc = f2_mul(make_float2(dw[i][h], dw[i][h]), dx);
+                                const float2 t = f2_add(make_float2(__uint_as_float(d[2 * h]), __uint_as_float(d[2 * h + 1])), off);
+                                acc[i][jj][h] = f2_add(acc[i][jj][h], f2_prod(t, sc, nz2));
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) set_status(a.status, STATUS_TIMEOUT);
+        // ------------------------------------------------ outputs
+        if (MODE == PF_DN) {
+            if (ok) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = row0 + 32 * wr + 16 * i + 8 * h + g, tok = 64 * wc + 8 * jj + 2 * tq;
+                            if (tok < nt) a.y[(size_t)(p0 + tok) * a.n_embd + row] = acc[i][jj][h].x;
+                            if (tok + 1 < nt) a.y[(size_t)(p0 + tok + 1) * a.n_embd + row] = acc[i][jj][h].y;
+                        }
+            }
+        } else {
+            // rows 32 wr .. + 31 of the tile are unit u = wr / 2, gate (wr even) or up, column
+            // 16 i + 8 h + g. Staged as H[u][gate | up][position][33] in the (now consumed) stage
+            // buffers; then one warp per (position, unit): h = gelu(gate) * up over the unit's 32
+            // columns, quantised as one Q8_0 block (lane = column).
+            float *H = reinterpret_cast<float *>(smem);
+            const int nthr = 4 * nch * 32;
+            named_sync_n(6, nthr);
+            const int u = wr >> 1, x = wr & 1;
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int c = 16 * i + 8 * h + g, tok = 64 * wc + 8 * jj + 2 * tq;
+                        float *hp = H + ((size_t)(u * 2 + x) * PF_N + tok) * PM_H_PITCH + c;
+                        hp[0] = acc[i][jj][h].x;
+                        hp[PM_H_PITCH] = acc[i][jj][h].y;
+                    }
+            named_sync_n(6, nthr);
+            if (ok) {
+                const int hrb = q8rec_bytes(a.nh);
+#pragma unroll 1
+                for (int item = warp; item < 2 * nt; item += 4 * nch) {
+                    const int uu = item & 1, tok = item >> 1;
+                    const float gv = H[((size_t)(uu * 2) * PF_N + tok) * PM_H_PITCH + lane];
+                    const float uv = H[((size_t)(uu * 2 + 1) * PF_N + tok) * PM_H_PITCH + lane];
+                    const float hv = __fmul_rn(gelu_tanh(gv), uv);
+                    uint16_t dbits;
+                    int qsum;
+                    const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);
+                    const int q = (row0 >> 6) + uu;  // h block within the expert's ff columns
+                    q8rec_store(a.hrec + (size_t)(p0 + tok) * hrb, a.nh, q, lane, qv, dbits, qsum);
+                    if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + tok] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
+                }
+            }
+        }
+    }
 }
 
 }  // namespace rvc

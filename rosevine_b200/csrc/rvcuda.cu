@@ -97,8 +97,8 @@ struct Workspace {
         ybuf = take(ppos * n_embd * 4);
         // prefill calls only
         xperm = prefill ? take(ppos * q8rec_bytes((int)nb)) : o;
-        xd = prefill ? take(nb * ppad * 4) : o;
-        hd = prefill ? take(nbh * ppad * 4) : o;
+        xd = prefill ? take(nb * ppad * 8) : o;   // (scale, offset) f32 pairs, block-major
+        hd = prefill ? take(nbh * ppad * 8) : o;
         tiles = prefill ? take((pairs / 128 + 1 + (size_t)ne) * 8) : o;
         n_tiles = take(4);
         plan = take(fd_plan_words(std::min(max_tok, FD_MAX_TOK) * used, ne) * 4);
@@ -461,14 +461,14 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     if ((rc = launched())) return rc;
     // 2. Q8_0 of x, once per token, to its plan positions
     uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
-    float *xd = at<float>(ws, L.xd), *hd = at<float>(ws, L.hd);
+    float2 *xso = at<float2>(ws, L.xd), *hso = at<float2>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
     const int qblocks = (int)std::min<long long>(8 * num_sms(), ((long long)n_tok * nb + 7) / 8);
     if (x_dtype == RVC_BF16)
         k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
-                                                      xd, ppad);
+                                                      xso, ppad);
     else
-        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xd,
+        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xso,
                                                    ppad);
     if ((rc = launched())) return rc;
     // 3. gate/up and down GEMMs
@@ -476,30 +476,32 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     CUtensorMap m_gu, m_x, m_xd, m_dn, m_h, m_hd;
     const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
     // weight nibbles [rows][blocks][16 B]; activation quants as [halves][positions][16 B] (a
-    // chunk's positions contiguous: the canonical K-major layout); activation block scales
-    // [blocks][positions] f32
+    // chunk's positions contiguous: the canonical K-major layout); activation (scale, offset)
+    // pairs [blocks][positions][2] f32
     if ((rc = map3d(&m_gu, pk.gu_nib, 16, nb, (uint64_t)ne * 2 * w->ff, 16, (uint64_t)nb * 16, 16, PF_KB, PF_M)) ||
         (rc = map3d(&m_x, xperm, 16, ppos, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_xd, xd, ppad, nb, (uint64_t)ppad * 4, PF_N, PF_KB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
+        (rc = map2d(&m_xd, xso, 2 * (uint64_t)ppad, nb, (uint64_t)ppad * 8, 2 * PF_N, PF_KB,
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
         (rc = map3d(&m_dn, pk.dn_nib, 16, nbh, (uint64_t)ne * w->n_embd, 16, (uint64_t)nbh * 16, 16, PF_KB, PF_M)) ||
         (rc = map3d(&m_h, hrec, 16, ppos, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_hd, hd, ppad, nbh, (uint64_t)ppad * 4, PF_N, PF_KB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+        (rc = map2d(&m_hd, hso, 2 * (uint64_t)ppad, nbh, (uint64_t)ppad * 8, 2 * PF_N, PF_KB,
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
         return rc;
     size_t smax = 0;
-    if ((rc = fd_smem_max(k_pf_gemm<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm<PF_DN>, &smax))) return rc;
-    if (smax < (size_t)PF_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
+    if ((rc = fd_smem_max(k_pf_gemm_ms<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm_ms<PF_DN>, &smax))) return rc;
+    if (smax < (size_t)PM_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
     const int tiles_y = pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
     PfArgs g{};
     g.tiles = tiles, g.n_tiles = n_tiles;
-    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.scl = pk.gu_scl;
-    g.nh = nbh, g.hrec = hrec, g.hd = hd, g.ppad = ppad, g.n_embd = w->n_embd, g.status = status;
+    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
+    g.nh = nbh, g.hrec = hrec, g.hso = hso, g.ppad = ppad, g.n_embd = w->n_embd, g.status = status;
     g.negzero2 = 0x8000000080000000ull;
-    k_pf_gemm<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
+    k_pf_gemm_ms<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
     if ((rc = launched())) return rc;
     PfArgs d = g;
-    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.scl = pk.dn_scl;
-    d.hrec = nullptr, d.hd = nullptr, d.y = at<float>(ws, L.ybuf);
-    k_pf_gemm<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PF_THREADS, PF_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
+    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
+    d.hrec = nullptr, d.hso = nullptr, d.y = at<float>(ws, L.ybuf);
+    k_pf_gemm_ms<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
     if ((rc = launched())) return rc;
     // 4. slot-order combine
     k_pf_combine<<<4 * num_sms(), 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
