@@ -663,22 +663,27 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
 
 // ------------------------------------------------------------------ grouped GEMM, register accumulators
 // The same tiles, with the block dots from mma.sync.m16n8k32 (u8 nibbles x s8 quants, s32
-// accumulators in registers): each compute warp multiplies, scales and accumulates its own
-// 32 rows x 64 positions, so a block's integers never leave the registers that receive them.
+// accumulators in registers): each of 16 warps multiplies, scales and accumulates its own
+// 32 rows x 32 positions, so a block's integers never leave the registers that receive them.
 // A fragments come straight from the nibble tile: the 32-bit word at byte 4 (lane % 4) of a row's
 // block holds elements 4 (lane % 4) .. + 3 in its low nibbles and the same + 16 in its high
 // nibbles, which are exactly the a0 / a2 (a1 / a3 for row + 8) registers of the fragment.
-// Every operand arrives by TMA; the compute warps wait once per stage of 8 blocks.
-constexpr int PM_WARPS = 8;  // 4 row groups of 32 x 2 position halves of 64
-constexpr int PM_THREADS = (PM_WARPS + 1) * 32;
+// Stages of 8 blocks arrive by TMA (nibbles, quants, (scale, offset) pairs); the weight scales of
+// the next stage are loaded by all threads during a stage and stored (as f32, block-major) at its
+// end, and one CTA barrier per stage both publishes them and frees the stage's buffers.
+constexpr int PM_WARPS = 16;  // 4 row groups of 32 x 4 position groups of 32
+constexpr int PM_THREADS = PM_WARPS * 32;
 constexpr int PM_STAGES = 3;
 constexpr int PM_OFF_B = PF_NIB_BYTES;
 constexpr int PM_OFF_SO = PM_OFF_B + PF_B_BYTES;
 constexpr int PM_STAGE_BYTES = PM_OFF_SO + PF_DX_BYTES;  // 56 KB
-constexpr int PM_SMEM_BYTES = PM_STAGES * PM_STAGE_BYTES + 1024;
+constexpr int PM_DW_BYTES = PF_KB * PF_M * 4;            // 4 KB: [8 blocks][128 rows] f32
+constexpr int PM_OFF_DW = PM_STAGES * PM_STAGE_BYTES;
+constexpr int PM_SMEM_BYTES = PM_OFF_DW + 2 * PM_DW_BYTES + 1024;
 constexpr int PM_H_PITCH = 33;  // gate/up staging [unit][gate|up][position][33]
 static_assert(PM_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm_ms");
 static_assert(2 * 2 * PF_N * PM_H_PITCH * 4 <= PM_STAGES * PM_STAGE_BYTES, "gate/up staging");
+static_assert(PF_M * (PF_KB / 2) == PM_THREADS, "one weight-scale word per thread and stage");
 
 // d = a . b + (c, c, c, c): 16 x 8 s32 from 16 x 32 u8 (row-major) and 32 x 8 s8 (column-major).
 __device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -695,70 +700,70 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                                                               const __grid_constant__ CUtensorMap map_so, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[PM_STAGES], empty[PM_STAGES];
+    __shared__ uint64_t full[PM_STAGES];
     if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nblk = a.nblk, rows = a.rows_per_expert;
     const int row0 = blockIdx.x * PF_M;
     const int2 td = __ldg(a.tiles + blockIdx.y);
     const int e = td.x & 0xFF, nt = td.x >> 8, p0 = td.y;
-    const int nch = (nt + 63) >> 6;  // position halves holding tokens (compute warps 4 ch .. + 3)
     const int nst = (nblk + PF_KB - 1) / PF_KB;
     const int wrow0 = e * rows + row0;
-    if (tid == PM_WARPS * 32) {
-        for (int s = 0; s < PM_STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], 4 * nch);
+    auto issue = [&](int st) {  // thread 0
+        const int s = st % PM_STAGES;
+        uint8_t *base = smem + s * PM_STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], PM_STAGE_BYTES);
+        tma_load_3d(base, &map_nib, 0, st * PF_KB, wrow0, &full[s]);              // [128 rows][8 blocks][16 B]
+        tma_load_3d(base + PM_OFF_B, &map_act, 0, p0, 2 * st * PF_KB, &full[s]);  // [16 halves][128 positions][16 B]
+        tma_load_2d(base + PM_OFF_SO, &map_so, 2 * p0, st * PF_KB, &full[s]);     // [8 blocks][128 positions][2] f32
+    };
+    // weight scales: thread t loads the f16 pair (blocks 2 (t % 4), + 1) of tile row t / 4
+    const int sr = tid >> 2, sw = tid & 3;
+    const uint16_t *sp = a.scl + (size_t)(wrow0 + sr) * nblk + 2 * sw;
+    float *const sdw = reinterpret_cast<float *>(smem + PM_OFF_DW);
+    auto ld_dw = [&](int st) { return st * PF_KB + 2 * sw < nblk ? __ldg(reinterpret_cast<const uint32_t *>(sp + st * PF_KB)) : 0u; };
+    auto st_dw = [&](int st, uint32_t w) {
+        float *d = sdw + (st & 1) * (PF_KB * PF_M);
+        d[(2 * sw) * PF_M + sr] = f16_bits_to_f32((uint16_t)(w & 0xFFFFu));
+        d[(2 * sw + 1) * PF_M + sr] = f16_bits_to_f32((uint16_t)(w >> 16));
+    };
+    if (tid == 0) {
+        for (int s = 0; s < PM_STAGES; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
-        bulk_prefetch_l2(a.nib + (size_t)wrow0 * nblk * 16, (uint32_t)(PF_M * nblk * 16));
-        bulk_prefetch_l2(a.scl + (size_t)wrow0 * nblk, (uint32_t)(PF_M * nblk * 2) & ~15u);
+        for (int st = 0; st < min(nst, PM_STAGES); ++st) issue(st);
     }
+    st_dw(0, ld_dw(0));
     __syncthreads();
 
-    if (warp == PM_WARPS) {
-        // ------------------------------------------------ producer: one lane issues every copy
-        if (lane == 0) {
-            bool ok = true;
-            for (int st = 0; st < nst && ok; ++st) {
-                const int s = st % PM_STAGES;
-                if (st >= PM_STAGES) ok = pf_wait(&empty[s], (uint32_t)(st / PM_STAGES - 1) & 1u, a.status);
-                if (!ok) break;
-                uint8_t *base = smem + s * PM_STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[s], PM_STAGE_BYTES);
-                tma_load_3d(base, &map_nib, 0, st * PF_KB, wrow0, &full[s]);                // [128 rows][8 blocks][16 B]
-                tma_load_3d(base + PM_OFF_B, &map_act, 0, p0, 2 * st * PF_KB, &full[s]);    // [16 halves][128 positions][16 B]
-                tma_load_2d(base + PM_OFF_SO, &map_so, 2 * p0, st * PF_KB, &full[s]);       // [8 blocks][128 positions][2] f32
-            }
-            if (!ok) set_status(a.status, STATUS_TIMEOUT);
-        }
-        __syncwarp();
-    } else if ((warp >> 2) < nch) {
-        // ------------------------------------------------ compute
-        const int wr = warp & 3, wc = warp >> 2;
-        const int g = lane >> 2, tq = lane & 3;
-        const int nj = min(8, (nt - 64 * wc + 7) >> 3);  // 8-position fragments holding tokens
-        float2 acc[2][8][2];  // [row fragment][position fragment][rows g, g + 8]: positions 2 tq, 2 tq + 1
+    const int wr = warp & 3, wc = warp >> 2;  // rows 32 wr .., positions 32 wc ..
+    const int g = lane >> 2, tq = lane & 3;
+    const bool active = 32 * wc < nt;
+    const int nj = active ? min(4, (nt - 32 * wc + 7) >> 3) : 0;  // 8-position fragments holding tokens
+    float2 acc[2][4][2];  // [row fragment][position fragment][rows g, g + 8]: positions 2 tq, 2 tq + 1
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[i][jj][0] = acc[i][jj][1] = make_float2(0.0f, 0.0f);
-        // the thread's 4 rows: 32 wr + 16 i + 8 h + g
-        const uint16_t *srow = a.scl + ((size_t)wrow0 + 32 * wr + g) * nblk;
-        const uint64_t nz2 = a.negzero2;
-        bool ok = true;
-        for (int st = 0; st < nst; ++st) {
-            const int s = st % PM_STAGES;
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj][0] = acc[i][jj][1] = make_float2(0.0f, 0.0f);
+    const uint64_t nz2 = a.negzero2;
+    bool ok = true;
+    for (int st = 0; st < nst; ++st) {
+        const int s = st % PM_STAGES;
+        const uint32_t wnext = st + 1 < nst ? ld_dw(st + 1) : 0u;  // lands during this stage
+        if (active) {
             if (lane == 0) ok = pf_wait(&full[s], (uint32_t)(st / PM_STAGES) & 1u, a.status);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
+        }
+        if (active && ok) {
             const uint8_t *sN = smem + s * PM_STAGE_BYTES, *sB = sN + PM_OFF_B;
             const float4 *sSO = reinterpret_cast<const float4 *>(sN + PM_OFF_SO);
+            const float *dwp = sdw + (st & 1) * (PF_KB * PF_M) + 32 * wr + g;
             const int kn = min(PF_KB, nblk - st * PF_KB);
             for (int jb = 0; jb < kn; ++jb) {
-                const int b = st * PF_KB + jb;
                 float dw[2][2];
 #pragma unroll
                 for (int i = 0; i < 2; ++i)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) dw[i][h] = f16_bits_to_f32(__ldg(srow + (size_t)(16 * i + 8 * h) * nblk + b));
+                    for (int h = 0; h < 2; ++h) dw[i][h] = dwp[jb * PF_M + 16 * i + 8 * h];
                 uint32_t af[2][4];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -770,14 +775,14 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                     af[i][2] = (w0 >> 4) & 0x0F0F0F0Fu, af[i][3] = (w1 >> 4) & 0x0F0F0F0Fu;
                 }
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
+                for (int jj = 0; jj < 4; ++jj) {
                     if (jj < nj) {
-                        const int n = 64 * wc + 8 * jj + g;  // the B column this lane supplies
+                        const int n = 32 * wc + 8 * jj + g;  // the B column this lane supplies
                         const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sB + (2 * jb) * (PF_N * 16) + n * 16 + 4 * tq);
                         const uint32_t b1 =
                             *reinterpret_cast<const uint32_t *>(sB + (2 * jb + 1) * (PF_N * 16) + n * 16 + 4 * tq);
-                        // (scale, offset) of positions 64 wc + 8 jj + 2 tq and + 1
-                        const float4 so = sSO[(jb * PF_N + 64 * wc + 8 * jj + 2 * tq) >> 1];
+                        // (scale, offset) of positions 32 wc + 8 jj + 2 tq and + 1
+                        const float4 so = sSO[(jb * PF_N + 32 * wc + 8 * jj + 2 * tq) >> 1];
                         const float2 off = make_float2(so.y, so.w), dx = make_float2(so.x, so.z);
 #pragma unroll
                         for (int i = 0; i < 2; ++i) {
@@ -793,60 +798,66 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        if (!ok) set_status(a.status, STATUS_TIMEOUT);
-        // ------------------------------------------------ outputs
-        if (MODE == PF_DN) {
-            if (ok) {
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int row = row0 + 32 * wr + 16 * i + 8 * h + g, tok = 64 * wc + 8 * jj + 2 * tq;
-                            if (tok < nt) a.y[(size_t)(p0 + tok) * a.n_embd + row] = acc[i][jj][h].x;
-                            if (tok + 1 < nt) a.y[(size_t)(p0 + tok + 1) * a.n_embd + row] = acc[i][jj][h].y;
-                        }
-            }
-        } else {
-            // rows 32 wr .. + 31 of the tile are unit u = wr / 2, gate (wr even) or up, column
-            // 16 i + 8 h + g. Staged as H[u][gate | up][position][33] in the (now consumed) stage
-            // buffers; then one warp per (position, unit): h = gelu(gate) * up over the unit's 32
-            // columns, quantised as one Q8_0 block (lane = column).
-            float *H = reinterpret_cast<float *>(smem);
-            const int nthr = 4 * nch * 32;
-            named_sync_n(6, nthr);
-            const int u = wr >> 1, x = wr & 1;
+        if (st + 1 < nst) st_dw(st + 1, wnext);
+        // the stage's buffers are consumed and the next scales in place; a timeout anywhere ends
+        // every thread's loop here, together
+        if (__syncthreads_or(!ok)) {
+            ok = false;
+            break;
+        }
+        if (tid == 0 && st + PM_STAGES < nst) issue(st + PM_STAGES);
+    }
+    if (!ok) set_status(a.status, STATUS_TIMEOUT);
+    // ------------------------------------------------ outputs
+    if (MODE == PF_DN) {
+        if (ok && active) {
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj)
+                for (int jj = 0; jj < 4; ++jj)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int c = 16 * i + 8 * h + g, tok = 64 * wc + 8 * jj + 2 * tq;
+                        const int row = row0 + 32 * wr + 16 * i + 8 * h + g, tok = 32 * wc + 8 * jj + 2 * tq;
+                        if (tok < nt) a.y[(size_t)(p0 + tok) * a.n_embd + row] = acc[i][jj][h].x;
+                        if (tok + 1 < nt) a.y[(size_t)(p0 + tok + 1) * a.n_embd + row] = acc[i][jj][h].y;
+                    }
+        }
+    } else {
+        // rows 32 wr .. + 31 of the tile are unit u = wr / 2, gate (wr even) or up, column
+        // 16 i + 8 h + g. Staged as H[u][gate | up][position][33] in the (consumed) stage buffers;
+        // then one warp per (position, unit): h = gelu(gate) * up over the unit's 32 columns,
+        // quantised as one Q8_0 block (lane = column).
+        float *H = reinterpret_cast<float *>(smem);
+        const int u = wr >> 1, x = wr & 1;
+        if (active) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int c = 16 * i + 8 * h + g, tok = 32 * wc + 8 * jj + 2 * tq;
                         float *hp = H + ((size_t)(u * 2 + x) * PF_N + tok) * PM_H_PITCH + c;
                         hp[0] = acc[i][jj][h].x;
                         hp[PM_H_PITCH] = acc[i][jj][h].y;
                     }
-            named_sync_n(6, nthr);
-            if (ok) {
-                const int hrb = q8rec_bytes(a.nh);
+        }
+        __syncthreads();
+        if (ok) {
+            const int hrb = q8rec_bytes(a.nh);
 #pragma unroll 1
-                for (int item = warp; item < 2 * nt; item += 4 * nch) {
-                    const int uu = item & 1, tok = item >> 1;
-                    const float gv = H[((size_t)(uu * 2) * PF_N + tok) * PM_H_PITCH + lane];
-                    const float uv = H[((size_t)(uu * 2 + 1) * PF_N + tok) * PM_H_PITCH + lane];
-                    const float hv = __fmul_rn(gelu_tanh(gv), uv);
-                    uint16_t dbits;
-                    int qsum;
-                    const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);
-                    const int q = (row0 >> 6) + uu;  // h block within the expert's ff columns
-                    q8rec_store(a.hrec + (size_t)(p0 + tok) * hrb, a.nh, q, lane, qv, dbits, qsum);
-                    if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + tok] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
-                }
+            for (int item = warp; item < 2 * nt; item += PM_WARPS) {
+                const int uu = item & 1, tok = item >> 1;
+                const float gv = H[((size_t)(uu * 2) * PF_N + tok) * PM_H_PITCH + lane];
+                const float uv = H[((size_t)(uu * 2 + 1) * PF_N + tok) * PM_H_PITCH + lane];
+                const float hv = __fmul_rn(gelu_tanh(gv), uv);
+                uint16_t dbits;
+                int qsum;
+                const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);
+                const int q = (row0 >> 6) + uu;  // h block within the expert's ff columns
+                q8rec_store(a.hrec + (size_t)(p0 + tok) * hrb, a.nh, q, lane, qv, dbits, qsum);
+                if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + tok] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
             }
         }
     }
