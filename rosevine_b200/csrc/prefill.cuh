@@ -668,22 +668,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant
 // A fragments come straight from the nibble tile: the 32-bit word at byte 4 (lane % 4) of a row's
 // block holds elements 4 (lane % 4) .. + 3 in its low nibbles and the same + 16 in its high
 // nibbles, which are exactly the a0 / a2 (a1 / a3 for row + 8) registers of the fragment.
-// Stages of 8 blocks arrive by TMA (nibbles, quants, (scale, offset) pairs); the weight scales of
-// the next stage are loaded by all threads during a stage and stored (as f32, block-major) at its
-// end, and one CTA barrier per stage both publishes them and frees the stage's buffers.
+// Stages of 8 blocks arrive by TMA (nibbles, quants, (scale, offset) pairs); each warp keeps its
+// own rows' weight scales a stage ahead in its slice of shared memory, and runs through the
+// stages on its own: per stage it waits for the copies (full) and releases the buffers (empty);
+// thread 0 refills a slot once every warp holding tokens is past it. Warps whose 32 positions
+// hold no token leave at once.
 constexpr int PM_WARPS = 16;  // 4 row groups of 32 x 4 position groups of 32
 constexpr int PM_THREADS = PM_WARPS * 32;
 constexpr int PM_STAGES = 3;
 constexpr int PM_OFF_B = PF_NIB_BYTES;
 constexpr int PM_OFF_SO = PM_OFF_B + PF_B_BYTES;
 constexpr int PM_STAGE_BYTES = PM_OFF_SO + PF_DX_BYTES;  // 56 KB
-constexpr int PM_DW_BYTES = PF_KB * PF_M * 4;            // 4 KB: [8 blocks][128 rows] f32
+constexpr int PM_DW_WARP = 2 * PF_KB * 32;               // f32 per warp: [2 stages][8 blocks][32 rows]
 constexpr int PM_OFF_DW = PM_STAGES * PM_STAGE_BYTES;
-constexpr int PM_SMEM_BYTES = PM_OFF_DW + 2 * PM_DW_BYTES + 1024;
+constexpr int PM_SMEM_BYTES = PM_OFF_DW + PM_WARPS * PM_DW_WARP * 4 + 1024;
 constexpr int PM_H_PITCH = 33;  // gate/up staging [unit][gate|up][position][33]
 static_assert(PM_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm_ms");
 static_assert(2 * 2 * PF_N * PM_H_PITCH * 4 <= PM_STAGES * PM_STAGE_BYTES, "gate/up staging");
-static_assert(PF_M * (PF_KB / 2) == PM_THREADS, "one weight-scale word per thread and stage");
 
 // d = a . b + (c, c, c, c): 16 x 8 s32 from 16 x 32 u8 (row-major) and 32 x 8 s8 (column-major).
 __device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -700,7 +701,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                                                               const __grid_constant__ CUtensorMap map_so, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[PM_STAGES];
+    __shared__ uint64_t full[PM_STAGES], empty[PM_STAGES];
     if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nblk = a.nblk, rows = a.rows_per_expert;
@@ -709,6 +710,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
     const int e = td.x & 0xFF, nt = td.x >> 8, p0 = td.y;
     const int nst = (nblk + PF_KB - 1) / PF_KB;
     const int wrow0 = e * rows + row0;
+    const int n_active = 4 * min(4, (nt + 31) >> 5);  // warps 0 .. n_active - 1 hold tokens
     auto issue = [&](int st) {  // thread 0
         const int s = st % PM_STAGES;
         uint8_t *base = smem + s * PM_STAGE_BYTES;
@@ -717,28 +719,38 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         tma_load_3d(base + PM_OFF_B, &map_act, 0, p0, 2 * st * PF_KB, &full[s]);  // [16 halves][128 positions][16 B]
         tma_load_2d(base + PM_OFF_SO, &map_so, 2 * p0, st * PF_KB, &full[s]);     // [8 blocks][128 positions][2] f32
     };
-    // weight scales: thread t loads the f16 pair (blocks 2 (t % 4), + 1) of tile row t / 4
-    const int sr = tid >> 2, sw = tid & 3;
-    const uint16_t *sp = a.scl + (size_t)(wrow0 + sr) * nblk + 2 * sw;
-    float *const sdw = reinterpret_cast<float *>(smem + PM_OFF_DW);
-    auto ld_dw = [&](int st) { return st * PF_KB + 2 * sw < nblk ? __ldg(reinterpret_cast<const uint32_t *>(sp + st * PF_KB)) : 0u; };
-    auto st_dw = [&](int st, uint32_t w) {
-        float *d = sdw + (st & 1) * (PF_KB * PF_M);
-        d[(2 * sw) * PF_M + sr] = f16_bits_to_f32((uint16_t)(w & 0xFFFFu));
-        d[(2 * sw + 1) * PF_M + sr] = f16_bits_to_f32((uint16_t)(w >> 16));
-    };
     if (tid == 0) {
-        for (int s = 0; s < PM_STAGES; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < PM_STAGES; ++s) mbar_init(&full[s], 1), mbar_init(&empty[s], n_active);
         fence_barrier_init();
+        bulk_prefetch_l2(a.nib + (size_t)wrow0 * nblk * 16, (uint32_t)(PF_M * nblk * 16));
         for (int st = 0; st < min(nst, PM_STAGES); ++st) issue(st);
     }
-    st_dw(0, ld_dw(0));
     __syncthreads();
+    if (warp >= n_active) return;
 
     const int wr = warp & 3, wc = warp >> 2;  // rows 32 wr .., positions 32 wc ..
     const int g = lane >> 2, tq = lane & 3;
-    const bool active = 32 * wc < nt;
-    const int nj = active ? min(4, (nt - 32 * wc + 7) >> 3) : 0;  // 8-position fragments holding tokens
+    const int nj = min(4, (nt - 32 * wc + 7) >> 3);  // 8-position fragments holding tokens
+    // the warp's weight scales: lane l loads row 32 wr + l's 8 scales of a stage one stage ahead
+    // (four f16 pairs) and stores them as f32 in the warp's own slice [2][8 blocks][32 rows]
+    const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + (size_t)(wrow0 + 32 * wr + lane) * nblk);
+    float *const sdw = reinterpret_cast<float *>(smem + PM_OFF_DW) + warp * PM_DW_WARP;
+    uint32_t wn[4];
+    auto ld_dw = [&](int st) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wn[k] = st * PF_KB + 2 * k < nblk ? __ldg(srow + (st * PF_KB) / 2 + k) : 0u;
+    };
+    auto st_dw = [&](int st) {
+        float *d = sdw + (st & 1) * (PF_KB * 32) + lane;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            d[(2 * k) * 32] = f16_bits_to_f32((uint16_t)(wn[k] & 0xFFFFu));
+            d[(2 * k + 1) * 32] = f16_bits_to_f32((uint16_t)(wn[k] >> 16));
+        }
+    };
+    ld_dw(0);
+    st_dw(0);
+    __syncwarp();
     float2 acc[2][4][2];  // [row fragment][position fragment][rows g, g + 8]: positions 2 tq, 2 tq + 1
 #pragma unroll
     for (int i = 0; i < 2; ++i)
@@ -746,24 +758,22 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         for (int jj = 0; jj < 4; ++jj) acc[i][jj][0] = acc[i][jj][1] = make_float2(0.0f, 0.0f);
     const uint64_t nz2 = a.negzero2;
     bool ok = true;
-    for (int st = 0; st < nst; ++st) {
+    for (int st = 0; st < nst && ok; ++st) {
         const int s = st % PM_STAGES;
-        const uint32_t wnext = st + 1 < nst ? ld_dw(st + 1) : 0u;  // lands during this stage
-        if (active) {
-            if (lane == 0) ok = pf_wait(&full[s], (uint32_t)(st / PM_STAGES) & 1u, a.status);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-        }
-        if (active && ok) {
+        if (st + 1 < nst) ld_dw(st + 1);  // lands during this stage
+        if (lane == 0) ok = pf_wait(&full[s], (uint32_t)(st / PM_STAGES) & 1u, a.status);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok) {
             const uint8_t *sN = smem + s * PM_STAGE_BYTES, *sB = sN + PM_OFF_B;
             const float4 *sSO = reinterpret_cast<const float4 *>(sN + PM_OFF_SO);
-            const float *dwp = sdw + (st & 1) * (PF_KB * PF_M) + 32 * wr + g;
+            const float *dwp = sdw + (st & 1) * (PF_KB * 32) + g;
             const int kn = min(PF_KB, nblk - st * PF_KB);
             for (int jb = 0; jb < kn; ++jb) {
                 float dw[2][2];
 #pragma unroll
                 for (int i = 0; i < 2; ++i)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) dw[i][h] = dwp[jb * PF_M + 16 * i + 8 * h];
+                    for (int h = 0; h < 2; ++h) dw[i][h] = dwp[jb * 32 + 16 * i + 8 * h];
                 uint32_t af[2][4];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -799,19 +809,22 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                 }
             }
         }
-        if (st + 1 < nst) st_dw(st + 1, wnext);
-        // the stage's buffers are consumed and the next scales in place; a timeout anywhere ends
-        // every thread's loop here, together
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's buffers
+        if (st + 1 < nst) st_dw(st + 1);
+        __syncwarp();
+        // thread 0 refills the slot of the previous stage once every warp holding tokens is past it
+        if (tid == 0 && st >= 1 && st - 1 + PM_STAGES < nst) {
+            const int sp = st - 1;
+            ok = ok && pf_wait(&empty[sp % PM_STAGES], (uint32_t)(sp / PM_STAGES) & 1u, a.status);
+            if (ok) issue(sp + PM_STAGES);
         }
-        if (tid == 0 && st + PM_STAGES < nst) issue(st + PM_STAGES);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (!ok) set_status(a.status, STATUS_TIMEOUT);
     // ------------------------------------------------ outputs
     if (MODE == PF_DN) {
-        if (ok && active) {
+        if (ok) {
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -828,9 +841,11 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         // 16 i + 8 h + g. Staged as H[u][gate | up][position][33] in the (consumed) stage buffers;
         // then one warp per (position, unit): h = gelu(gate) * up over the unit's 32 columns,
         // quantised as one Q8_0 block (lane = column).
+        // (the stage buffers are free once every warp holding tokens is past its last stage)
         float *H = reinterpret_cast<float *>(smem);
         const int u = wr >> 1, x = wr & 1;
-        if (active) {
+        named_sync_n(6, n_active * 32);
+        {
 #pragma unroll
             for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -843,11 +858,11 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                         hp[PM_H_PITCH] = acc[i][jj][h].y;
                     }
         }
-        __syncthreads();
+        named_sync_n(6, n_active * 32);
         if (ok) {
             const int hrb = q8rec_bytes(a.nh);
 #pragma unroll 1
-            for (int item = warp; item < 2 * nt; item += PM_WARPS) {
+            for (int item = warp; item < 2 * nt; item += n_active) {
                 const int uu = item & 1, tok = item >> 1;
                 const float gv = H[((size_t)(uu * 2) * PF_N + tok) * PM_H_PITCH + lane];
                 const float uv = H[((size_t)(uu * 2 + 1) * PF_N + tok) * PM_H_PITCH + lane];
