@@ -237,49 +237,75 @@ __global__ void __launch_bounds__(128) k_debug_mma_i8(const int8_t *__restrict__
 }
 
 // ------------------------------------------------------------------ quantise + scatter
-// Q8_0 of x, once per token: warp task (token t, block b) quantises the block and writes it into
-// the records of the token's `used` plan positions pos_of[t used + j], and the block's (scale,
-// offset) pair into the block-major plane xso[b][position] the GEMM's scale tiles come from.
+// Q8_0 of x, once per token: warp w quantises 8 blocks of token w / (nb / 8) one by one (the
+// next block's values loaded while this one is processed) and writes each into the records of
+// the token's
+// `used` plan positions pos_of[t used + j], with the block's (scale, offset) pair in the
+// block-major plane xso[b][position] the GEMM's scale tiles come from.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int n_embd, int n_tok, int used,
                                                   const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
                                                   float2 *__restrict__ xso, int ppad) {
     const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int total = n_tok * nb;
-    for (int i = blockIdx.x * 8 + warp; i < total; i += gridDim.x * 8) {
-        const int t = i / nb, b = i - t * nb;
-        const float v = ld_val<XT>(x, (size_t)t * n_embd + (size_t)b * QK + lane);
+    const int lane = threadIdx.x & 31;
+    const int nc = (nb + 7) / 8, wi = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (wi >= n_tok * nc) return;
+    const int t = wi / nc, b0 = (wi - t * nc) * 8, b1 = min(nb, b0 + 8);
+    const int my_pos = lane < used ? __ldg(pos_of + (size_t)t * used + lane) : 0;
+    const size_t xrow = (size_t)t * n_embd + lane;
+    float v = ld_val<XT>(x, xrow + (size_t)b0 * QK);
+    for (int b = b0; b < b1; ++b) {
+        const float vn = b + 1 < b1 ? ld_val<XT>(x, xrow + (size_t)(b + 1) * QK) : 0.0f;
         uint16_t dbits;
         int qsum;
         const int8_t q = quant_q8_lane(v, &dbits, &qsum);
         const float2 so = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
         for (int j = 0; j < used; ++j) {
-            const int k = __ldg(pos_of + t * used + j);
+            const int k = __shfl_sync(0xffffffffu, my_pos, j);
             q8rec_store(xperm + (size_t)k * xrb, nb, b, lane, q, dbits, qsum);
             if (lane == 0) xso[(size_t)b * ppad + k] = so;
         }
+        v = vn;
     }
 }
 
 // ------------------------------------------------------------------ combine
-// out[t][r] = slot-order sum over j of (y[pos_of[t used + j]][r] * down_scale[e]) * w[t][j].
+// out[t][r] = slot-order sum over j of (y[pos_of[t used + j]][r] * down_scale[e]) * w[t][j]
+// (exec.rs:626-638), one CTA per token, four rows per thread and step.
 __global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
                                                     const int32_t *__restrict__ ids, const float *__restrict__ wts,
                                                     const float *__restrict__ down_scale, int used, int n_embd,
                                                     int n_tok, float *__restrict__ out) {
-    const long long total = (long long)n_tok * n_embd;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / n_embd), r = (int)(i - (long long)t * n_embd);
-        float o = 0.0f;
+    __shared__ const float4 *s_row[MAX_USED];
+    __shared__ float s_ds[MAX_USED], s_w[MAX_USED];
+    const int t = blockIdx.x;
+    if (threadIdx.x < used) {
+        const int p = t * used + threadIdx.x;
+        s_row[threadIdx.x] = reinterpret_cast<const float4 *>(y + (size_t)__ldg(pos_of + p) * n_embd);
+        s_ds[threadIdx.x] = down_scale ? __ldg(down_scale + __ldg(ids + p)) : 1.0f;
+        s_w[threadIdx.x] = __ldg(wts + p);
+    }
+    __syncthreads();
+    float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)t * n_embd);
+    const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    for (int r = threadIdx.x; r < n_embd / 4; r += blockDim.x) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < used; ++j) {
-            const int p = t * used + j;
-            const int e = __ldg(ids + p);
-            const float ds = down_scale ? __ldg(down_scale + e) : 1.0f;
-            const float v = __fmul_rn(__fmul_rn(__ldg(y + (size_t)__ldg(pos_of + p) * n_embd + r), ds), __ldg(wts + p));
-            o = j == 0 ? v : __fadd_rn(o, v);
+            const float4 v = __ldg(s_row[j] + r);
+            const float ds = s_ds[j], w = s_w[j];
+            const float4 c = make_float4(__fmul_rn(__fmul_rn(v.x, ds), w), __fmul_rn(__fmul_rn(v.y, ds), w),
+                                         __fmul_rn(__fmul_rn(v.z, ds), w), __fmul_rn(__fmul_rn(v.w, ds), w));
+            if (j == 0)
+                o = c;
+            else
+                o = make_float4(__fadd_rn(o.x, c.x), __fadd_rn(o.y, c.y), __fadd_rn(o.z, c.z), __fadd_rn(o.w, c.w));
         }
-        out[i] = o;
+        if (aligned) {
+            o4[r] = o;
+        } else {  // a caller's output that is only 4-byte aligned
+            float *op = out + (size_t)t * n_embd + 4 * r;
+            op[0] = o.x, op[1] = o.y, op[2] = o.z, op[3] = o.w;
+        }
     }
 }
 

@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
                                                        int32_t *__restrict__ order, int32_t *__restrict__ pos_of,
                                                        int32_t *__restrict__ active, int32_t *__restrict__ n_active,
                                                        int *status, int align = 1, int2 *__restrict__ tiles = nullptr,
-                                                       int32_t *__restrict__ n_tiles = nullptr, int tile_rows = 128) {
+                                                       int32_t *__restrict__ n_tiles = nullptr, int tile_rows = 128,
+                                                       bool stable = true) {
     __shared__ int s_count[MAX_EXPERTS];
     __shared__ int s_base[MAX_EXPERTS];
     __shared__ int s_warp[32][MAX_EXPERTS];  // per-warp counts within a chunk
@@ -238,6 +239,18 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
         }
     }
     __syncthreads();
+    if (!stable) {
+        // positions within a group in arrival order (callers whose results do not depend on
+        // the order inside a group): one shared-memory atomic per pair
+        for (int p = tid; p < n_pairs; p += PLAN_THREADS) {
+            const int e = ids[p];
+            if (e < 0 || e >= n_experts) continue;
+            const int k = atomicAdd(&s_base[e], 1);
+            order[k] = p;
+            pos_of[p] = k;
+        }
+        return;
+    }
     // stable scatter, one chunk of PLAN_THREADS pairs at a time
     for (int c0 = 0; c0 < n_pairs; c0 += PLAN_THREADS) {
         const int p = c0 + tid;

@@ -457,13 +457,14 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     int2 *tiles = at<int2>(ws, L.tiles);
     int32_t *n_tiles = at<int32_t>(ws, L.n_tiles);
     k_plan<<<1, PLAN_THREADS, 0, st>>>(id, pairs, ne, counts, offsets, order, pos_of, at<int32_t>(ws, L.active),
-                                       at<int32_t>(ws, L.n_active), status, 4, tiles, n_tiles, PF_N);
+                                       at<int32_t>(ws, L.n_active), status, 4, tiles, n_tiles, PF_N,
+                                       false);
     if ((rc = launched())) return rc;
     // 2. Q8_0 of x, once per token, to its plan positions
     uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
     float2 *xso = at<float2>(ws, L.xd), *hso = at<float2>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
-    const int qblocks = (int)std::min<long long>(8 * num_sms(), ((long long)n_tok * nb + 7) / 8);
+    const int qblocks = (n_tok * ((nb + 7) / 8) + 7) / 8;  // one warp per 8 blocks of a token
     if (x_dtype == RVC_BF16)
         k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
                                                       xso, ppad);
@@ -504,7 +505,7 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     k_pf_gemm_ms<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
     if ((rc = launched())) return rc;
     // 4. slot-order combine
-    k_pf_combine<<<4 * num_sms(), 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
+    k_pf_combine<<<n_tok, 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
                                                 w->n_embd, n_tok, out);
     return launched();
 }
