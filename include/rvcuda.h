@@ -119,6 +119,38 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
                     void *workspace, size_t workspace_bytes, void *stream);
 
 /* Zero the workspace's status word (call once after allocating a workspace). */
+/* ---------------------------------------------------------------- expert parallelism
+ * No reference counterpart: the reference runs every expert on one device. A rank routes its
+ * own tokens (rvc_moe_router), quantises the rows it sends (rvc_quant_q8_rows), runs its
+ * resident experts on the rows it receives (rvc_ep_experts) and sums the partial outputs
+ * returned for its tokens (rvc_ep_reduce); the exchanges between these calls are the caller's
+ * (NCCL all-to-allv). */
+
+/* Bytes of one Q8_0 row record of this backend: per 32-element block 32 int8 quants, then all
+ * blocks' f32 scales, then all blocks' int32 quant sums (n_embd / 32 * 40 bytes). */
+size_t rvc_q8_record_bytes(int n_embd);
+
+/* Q8_0 records (quantised as the reference quantises activations) of x [n_rows][n_embd]. */
+int rvc_quant_q8_rows(const void *x, int x_dtype, int n_rows, int n_embd, void *records, void *stream);
+
+/* Workspace for rvc_ep_experts calls of up to max_pairs (row, expert) pairs. */
+size_t rvc_ep_workspace_bytes(int max_pairs, int n_embd, int ff, int n_experts);
+
+/* The resident experts (w: this rank's n_experts, ids local) over n_rows received records.
+ * Row r's pairs are row_start[r] .. row_start[r + 1] - 1 (at most 16, in the token's slot
+ * order), with expert pair_expert[p] and routing weight pair_w[p]. partial[r] [n_embd] f32 =
+ * slot-order sum over the row's pairs of (y * down_scale[e]) * w, y the expert output of the
+ * reference's CPU-experts Q8_0 path; the block dots are exact and each pair's y is bit-identical
+ * to that path's. */
+int rvc_ep_experts(const rvc_moe_weights *w, const void *records, int n_rows, const int32_t *row_start,
+                   const int32_t *pair_expert, const float *pair_w, int n_pairs, float *partial, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* out[t] = partial[src_row[k0]] + partial[src_row[k0 + 1]] + ... (f32, in that order) over
+ * k in src_start[t] .. src_start[t + 1] - 1; a token with no entry gets zeros. */
+int rvc_ep_reduce(const float *partial, const int32_t *src_start, const int32_t *src_row, int n_tok, int n_embd,
+                  float *out, void *stream);
+
 int rvc_workspace_reset(void *workspace, void *stream);
 
 /* Synchronise `stream`, then read and clear the workspace's device status word:

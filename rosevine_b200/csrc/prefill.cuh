@@ -270,17 +270,28 @@ __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int 
 }
 
 // ------------------------------------------------------------------ combine
-// out[t][r] = slot-order sum over j of (y[pos_of[t used + j]][r] * down_scale[e]) * w[t][j]
-// (exec.rs:626-638), one CTA per token, four rows per thread and step.
+// out[t][r] = slot-order sum over j of (y[pos_of[p_j]][r] * down_scale[e_j]) * w_j (exec.rs:626-638)
+// over the pairs p_j of token (or received row) t: t used .. + used - 1, or with row_start
+// row_start[t] .. row_start[t + 1] - 1 (at most MAX_USED); one CTA per token, four rows per
+// thread and step.
 __global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
                                                     const int32_t *__restrict__ ids, const float *__restrict__ wts,
                                                     const float *__restrict__ down_scale, int used, int n_embd,
-                                                    int n_tok, float *__restrict__ out) {
+                                                    int n_tok, float *__restrict__ out,
+                                                    const int32_t *__restrict__ row_start, int *status) {
     __shared__ const float4 *s_row[MAX_USED];
     __shared__ float s_ds[MAX_USED], s_w[MAX_USED];
     const int t = blockIdx.x;
+    const int pb = row_start ? __ldg(row_start + t) : t * used;
+    if (row_start) {
+        used = __ldg(row_start + t + 1) - pb;
+        if (used < 0 || used > MAX_USED) {
+            if (threadIdx.x == 0) set_status(status, STATUS_BAD_INDEX);
+            used = 0;
+        }
+    }
     if (threadIdx.x < used) {
-        const int p = t * used + threadIdx.x;
+        const int p = pb + threadIdx.x;
         s_row[threadIdx.x] = reinterpret_cast<const float4 *>(y + (size_t)__ldg(pos_of + p) * n_embd);
         s_ds[threadIdx.x] = down_scale ? __ldg(down_scale + __ldg(ids + p)) : 1.0f;
         s_w[threadIdx.x] = __ldg(wts + p);
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y,
     float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)t * n_embd);
     const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int r = threadIdx.x; r < n_embd / 4; r += blockDim.x) {
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);  // a row with no pair (never from the router) reads 0
         for (int j = 0; j < used; ++j) {
             const float4 v = __ldg(s_row[j] + r);
             const float ds = s_ds[j], w = s_w[j];
@@ -306,6 +317,69 @@ __global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y,
             float *op = out + (size_t)t * n_embd + 4 * r;
             op[0] = o.x, op[1] = o.y, op[2] = o.z, op[3] = o.w;
         }
+    }
+}
+
+// ------------------------------------------------------------------ expert parallelism
+// Q8_0 records of n_rows rows of x (the rows a rank sends to the ranks holding their experts).
+template <typename XT>
+__global__ void __launch_bounds__(256) k_quant_rows(const XT *__restrict__ x, int n_embd, int n_rows,
+                                                    uint8_t *__restrict__ rec) {
+    const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
+    const int lane = threadIdx.x & 31;
+    const long long total = (long long)n_rows * nb;
+    for (long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += (long long)gridDim.x * 8) {
+        const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
+        uint16_t dbits;
+        int qsum;
+        const int8_t q = quant_q8_lane(ld_val<XT>(x, (size_t)r * n_embd + (size_t)b * QK + lane), &dbits, &qsum);
+        q8rec_store(rec + (size_t)r * xrb, nb, b, lane, q, dbits, qsum);
+    }
+}
+
+// Received records to plan positions: warp task (row r, block b) copies the block into the
+// records of the row's pairs row_start[r] .. row_start[r + 1] - 1, with its (scale, offset) pair.
+__global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ rec, int nb, int n_rows,
+                                                    const int32_t *__restrict__ row_start,
+                                                    const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
+                                                    float2 *__restrict__ xso, int ppad) {
+    const int xrb = q8rec_bytes(nb);
+    const int lane = threadIdx.x & 31;
+    const long long total = (long long)n_rows * nb;
+    for (long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += (long long)gridDim.x * 8) {
+        const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
+        const uint8_t *src = rec + (size_t)r * xrb;
+        const uint8_t q = src[b * 32 + lane];
+        const float d = reinterpret_cast<const float *>(src + nb * 32)[b];
+        const int qs = reinterpret_cast<const int *>(src + nb * 36)[b];
+        const int p1 = __ldg(row_start + r + 1);
+        for (int p = __ldg(row_start + r); p < p1; ++p) {
+            const int k = __ldg(pos_of + p);
+            uint8_t *dst = xperm + (size_t)k * xrb;
+            dst[b * 32 + lane] = q;
+            if (lane == 0) {
+                reinterpret_cast<float *>(dst + nb * 32)[b] = d;
+                reinterpret_cast<int *>(dst + nb * 36)[b] = qs;
+                xso[(size_t)b * ppad + k] = pf_scale_offset(d, qs);
+            }
+        }
+    }
+}
+
+// Owner-side sum of the partials returned for its tokens: out[t] = partial[src_row[k0]] +
+// partial[src_row[k0 + 1]] + ... over k in src_start[t] .. src_start[t + 1] - 1 (rank order).
+__global__ void __launch_bounds__(256) k_ep_reduce(const float *__restrict__ partial, const int32_t *__restrict__ src_start,
+                                                   const int32_t *__restrict__ src_row, int n_embd,
+                                                   float *__restrict__ out) {
+    const int t = blockIdx.x;
+    const int k0 = __ldg(src_start + t), k1 = __ldg(src_start + t + 1);
+    for (int r = threadIdx.x; r < n_embd / 4; r += blockDim.x) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = k0; k < k1; ++k) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(partial + (size_t)__ldg(src_row + k) * n_embd) + r);
+            o = k == k0 ? v : make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
+        }
+        reinterpret_cast<float4 *>(out + (size_t)t * n_embd)[r] = o;
     }
 }
 

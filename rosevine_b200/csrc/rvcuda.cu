@@ -434,46 +434,15 @@ int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-// The prefill layer (n_tok > 64): the reference-order router (logits, selection, plan), Q8_0
-// of x in plan order, the tensor-core gate/up and down GEMMs, the slot-order combine.
-int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
-                int bias_stride, int n_tok, float *out, int32_t *ids, float *wts, void *ws, size_t ws_bytes,
-                cudaStream_t st) {
+// Gate/up and down GEMMs over the plan positions already filled (xperm records, xso pairs):
+// y [positions][n_embd] in the workspace.
+int pf_gemms(const rvc_moe_weights *w, const Workspace &L, void *ws, int n_pairs, cudaStream_t st) {
     int rc;
-    if ((rc = tensor_map_encode())) return rc;
-    const int ne = w->n_experts, used = w->used, pairs = n_tok * used;
-    const int nb = w->n_embd / QK, nbh = w->ff / QK;
-    if (nb % PF_KB || (2 * w->ff) % PF_M || w->n_embd % PF_M || ne > MAX_EXPERTS) return RVC_ERR_UNSUPPORTED;
-    Workspace L(n_tok, w->n_embd, w->ff, ne, used);
-    int32_t *id = ids ? ids : at<int32_t>(ws, L.ids);
-    float *wt = wts ? wts : at<float>(ws, L.wts);
-    int32_t *counts = at<int32_t>(ws, L.counts), *offsets = at<int32_t>(ws, L.offsets);
-    int32_t *order = at<int32_t>(ws, L.order), *pos_of = at<int32_t>(ws, L.pos_of);
-    int *status = at<int>(ws, L.status);
-    // 1. router in the reference's order, selection, plan
-    if ((rc = rvc_moe_router(w, x_router, x_dtype, bias, bias_stride, n_tok, id, wt, nullptr, nullptr, nullptr, ws,
-                             ws_bytes, st)))
-        return rc;
-    int2 *tiles = at<int2>(ws, L.tiles);
-    int32_t *n_tiles = at<int32_t>(ws, L.n_tiles);
-    k_plan<<<1, PLAN_THREADS, 0, st>>>(id, pairs, ne, counts, offsets, order, pos_of, at<int32_t>(ws, L.active),
-                                       at<int32_t>(ws, L.n_active), status, 4, tiles, n_tiles, PF_N,
-                                       false);
-    if ((rc = launched())) return rc;
-    // 2. Q8_0 of x, once per token, to its plan positions
+    const int ne = w->n_experts, nb = w->n_embd / QK, nbh = w->ff / QK;
+    const PackedView pk = packed_view(w);
     uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
     float2 *xso = at<float2>(ws, L.xd), *hso = at<float2>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
-    const int qblocks = (n_tok * ((nb + 7) / 8) + 7) / 8;  // one warp per 8 blocks of a token
-    if (x_dtype == RVC_BF16)
-        k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
-                                                      xso, ppad);
-    else
-        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xso,
-                                                   ppad);
-    if ((rc = launched())) return rc;
-    // 3. gate/up and down GEMMs
-    const PackedView pk = packed_view(w);
     CUtensorMap m_gu, m_x, m_xd, m_dn, m_h, m_hd;
     const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
     // weight nibbles [rows][blocks][16 B]; activation quants as [halves][positions][16 B] (a
@@ -491,11 +460,11 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     size_t smax = 0;
     if ((rc = fd_smem_max(k_pf_gemm_ms<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm_ms<PF_DN>, &smax))) return rc;
     if (smax < (size_t)PM_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
-    const int tiles_y = pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
+    const int tiles_y = n_pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
     PfArgs g{};
-    g.tiles = tiles, g.n_tiles = n_tiles;
+    g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles);
     g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
-    g.nh = nbh, g.hrec = hrec, g.hso = hso, g.ppad = ppad, g.n_embd = w->n_embd, g.status = status;
+    g.nh = nbh, g.hrec = hrec, g.hso = hso, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
     g.negzero2 = 0x8000000080000000ull;
     k_pf_gemm_ms<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
     if ((rc = launched())) return rc;
@@ -503,12 +472,65 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
     d.hrec = nullptr, d.hso = nullptr, d.y = at<float>(ws, L.ybuf);
     k_pf_gemm_ms<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
-    if ((rc = launched())) return rc;
-    // 4. slot-order combine
-    k_pf_combine<<<n_tok, 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used,
-                                                w->n_embd, n_tok, out);
     return launched();
 }
+
+int pf_supported(const rvc_moe_weights *w) {
+    const int nb = w->n_embd / QK;
+    if (nb % PF_KB || (2 * w->ff) % PF_M || w->n_embd % PF_M || w->n_experts > MAX_EXPERTS || w->used > MAX_USED)
+        return RVC_ERR_UNSUPPORTED;
+    return tensor_map_encode();
+}
+
+// Plan of n_pairs (pair -> expert ids) into expert groups starting at multiples of 4
+// positions, with the tile list; positions within a group in arrival order.
+int pf_plan(const int32_t *pair_expert, int n_pairs, int ne, const Workspace &L, void *ws, cudaStream_t st) {
+    k_plan<<<1, PLAN_THREADS, 0, st>>>(pair_expert, n_pairs, ne, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
+                                       at<int32_t>(ws, L.order), at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
+                                       at<int32_t>(ws, L.n_active), at<int>(ws, L.status), 4, at<int2>(ws, L.tiles),
+                                       at<int32_t>(ws, L.n_tiles), PF_N, false);
+    return launched();
+}
+
+// The prefill layer (n_tok > 64): the reference-order router (logits, selection, plan), Q8_0
+// of x in plan order, the grouped GEMMs, the slot-order combine.
+int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
+                int bias_stride, int n_tok, float *out, int32_t *ids, float *wts, void *ws, size_t ws_bytes,
+                cudaStream_t st) {
+    int rc;
+    if ((rc = pf_supported(w))) return rc;
+    const int ne = w->n_experts, used = w->used, pairs = n_tok * used, nb = w->n_embd / QK;
+    Workspace L(n_tok, w->n_embd, w->ff, ne, used);
+    int32_t *id = ids ? ids : at<int32_t>(ws, L.ids);
+    float *wt = wts ? wts : at<float>(ws, L.wts);
+    int32_t *pos_of = at<int32_t>(ws, L.pos_of);
+    // 1. router in the reference's order, selection, plan
+    if ((rc = rvc_moe_router(w, x_router, x_dtype, bias, bias_stride, n_tok, id, wt, nullptr, nullptr, nullptr, ws,
+                             ws_bytes, st)) ||
+        (rc = pf_plan(id, pairs, ne, L, ws, st)))
+        return rc;
+    // 2. Q8_0 of x, once per token, to its plan positions
+    uint8_t *xperm = at<uint8_t>(ws, L.xperm);
+    float2 *xso = at<float2>(ws, L.xd);
+    const int qblocks = (n_tok * ((nb + 7) / 8) + 7) / 8;  // one warp per 8 blocks of a token
+    if (x_dtype == RVC_BF16)
+        k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
+                                                      xso, (int)L.ppad);
+    else
+        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xso,
+                                                   (int)L.ppad);
+    if ((rc = launched())) return rc;
+    // 3. gate/up and down GEMMs
+    if ((rc = pf_gemms(w, L, ws, pairs, st))) return rc;
+    // 4. slot-order combine
+    k_pf_combine<<<n_tok, 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used, w->n_embd, n_tok,
+                                        out, nullptr, at<int>(ws, L.status));
+    return launched();
+}
+
+// Workspace of an expert-parallel call of up to max_pairs pairs: the prefill layout for
+// ceil(max_pairs / 8) tokens of 8 pairs (at least the prefill path's 65).
+int ep_tokens(int max_pairs) { return std::max(FD_MAX_TOK + 1, (max_pairs + 7) / 8); }
 
 // The decode layer for n_tok <= 64 tokens: routing from x_router (or the caller's ids/wts),
 // experts on x_expert, into out.
@@ -712,6 +734,67 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
 int rvc_workspace_reset(void *workspace, void *stream) {
     if (!workspace) return (int)cudaErrorInvalidValue;
     return (int)cudaMemsetAsync(workspace, 0, 256, S(stream));
+}
+
+// ------------------------------------------------------------------ expert parallelism
+size_t rvc_q8_record_bytes(int n_embd) { return n_embd > 0 && n_embd % QK == 0 ? (size_t)q8rec_bytes(n_embd / QK) : 0; }
+
+int rvc_quant_q8_rows(const void *x, int x_dtype, int n_rows, int n_embd, void *records, void *stream) {
+    if (!x || !records || n_rows < 0 || n_embd <= 0 || n_embd % QK || !aligned(x, 4) ||
+        (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
+        return (int)cudaErrorInvalidValue;
+    if (n_rows == 0) return 0;
+    const long long tasks = (long long)n_rows * (n_embd / QK);
+    const int blocks = (int)std::min<long long>(16 * num_sms(), (tasks + 7) / 8);
+    if (x_dtype == RVC_BF16)
+        k_quant_rows<uint16_t><<<blocks, 256, 0, S(stream)>>>((const uint16_t *)x, n_embd, n_rows, (uint8_t *)records);
+    else
+        k_quant_rows<float><<<blocks, 256, 0, S(stream)>>>((const float *)x, n_embd, n_rows, (uint8_t *)records);
+    return launched();
+}
+
+size_t rvc_ep_workspace_bytes(int max_pairs, int n_embd, int ff, int n_experts) {
+    if (max_pairs <= 0 || n_embd <= 0 || n_embd % QK || ff <= 0 || ff % QK || n_experts <= 0) return 0;
+    return Workspace(ep_tokens(max_pairs), n_embd, ff, n_experts, 8).total;
+}
+
+int rvc_ep_experts(const rvc_moe_weights *w, const void *records, int n_rows, const int32_t *row_start,
+                   const int32_t *pair_expert, const float *pair_w, int n_pairs, float *partial, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+    if (!dims_ok(w) || n_rows < 0 || n_pairs < 0 || !workspace || !aligned(workspace, 256) ||
+        (n_rows > 0 && (!records || !row_start || !partial || !aligned(records, 16) || !aligned(partial, 16))) ||
+        (n_pairs > 0 && (!pair_expert || !pair_w)))
+        return (int)cudaErrorInvalidValue;
+    int rc;
+    if ((rc = pf_supported(w))) return rc;
+    if (n_rows == 0) return 0;
+    const int nt = ep_tokens(n_pairs);
+    Workspace L(nt, w->n_embd, w->ff, w->n_experts, 8);
+    if (L.total > workspace_bytes) return RVC_ERR_WORKSPACE;
+    cudaStream_t st = S(stream);
+    const int nb = w->n_embd / QK;
+    if (n_pairs > 0) {
+        if ((rc = pf_plan(pair_expert, n_pairs, w->n_experts, L, workspace, st))) return rc;
+        const long long tasks = (long long)n_rows * nb;
+        k_ep_scatter<<<(int)std::min<long long>(16 * num_sms(), (tasks + 7) / 8), 256, 0, st>>>(
+            (const uint8_t *)records, nb, n_rows, row_start, at<int32_t>(workspace, L.pos_of),
+            at<uint8_t>(workspace, L.xperm), at<float2>(workspace, L.xd), (int)L.ppad);
+        if ((rc = launched()) || (rc = pf_gemms(w, L, workspace, n_pairs, st))) return rc;
+    }
+    k_pf_combine<<<n_rows, 256, 0, st>>>(at<float>(workspace, L.ybuf), at<int32_t>(workspace, L.pos_of), pair_expert,
+                                         pair_w, w->down_scale, 0, w->n_embd, n_rows, partial, row_start,
+                                         at<int>(workspace, L.status));
+    return launched();
+}
+
+int rvc_ep_reduce(const float *partial, const int32_t *src_start, const int32_t *src_row, int n_tok, int n_embd,
+                  float *out, void *stream) {
+    if (n_tok < 0 || n_embd <= 0 || n_embd % 4 || (n_tok > 0 && (!src_start || !out || !aligned(out, 16))) ||
+        (partial && !aligned(partial, 16)))
+        return (int)cudaErrorInvalidValue;
+    if (n_tok == 0) return 0;
+    k_ep_reduce<<<n_tok, 256, 0, S(stream)>>>(partial, src_start, src_row, n_embd, out);
+    return launched();
 }
 
 int rvc_status(void *workspace, void *stream) {

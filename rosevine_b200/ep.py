@@ -1,0 +1,223 @@
+"""Expert-parallel MoE layer: experts sharded 128/N per GPU, tokens exchanged by all-to-allv.
+
+The reference runs every expert on one device (runtime/src/hip_exec.rs:820-843); this module is
+the multi-GPU form of the same layer. Rank r of N holds experts [r E/N, (r + 1) E/N) and starts
+with its own shard of the tokens. One forward:
+
+  1. route     the rank's tokens with the full router (reference order: rvc_moe_router),
+  2. plan      per destination rank the tokens that selected at least one of its experts (each
+               token sent once per rank) and, per sent row, its slots there in slot order,
+  3. dispatch  row counts (all-to-all), Q8_0 records quantised once by the sender
+               (rvc_quant_q8_rows) and the slot metadata (all-to-allv over NCCL),
+  4. experts   the resident experts over the received rows (rvc_ep_experts): one partial sum
+               per row, over its slots in slot order,
+  5. combine   partials back to their owners (all-to-allv), summed per token in rank order
+               (rvc_ep_reduce).
+
+Each (token, expert) output is bit-identical to the single-device path; the owner adds the
+per-rank partials, so the f32 summation order differs from the reference's slot order and the
+layer output matches within the 1e-3 tolerance, not bitwise.
+
+The collectives are torch.distributed calls (NCCL on GPUs); the compute steps go through a
+backend object. `GpuBackend` (the product) calls the CUDA library; the tests substitute a
+CPU backend built on the oracle to check the exchange logic over gloo.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import rvcuda as rc
+from . import synth
+from .moe import _stream_handle
+
+
+@dataclass
+class EpStats:
+    """Device time of the last forward's exchanges, in ms (CUDA events; 0 on CPU)."""
+    dispatch_ms: float = 0.0
+    combine_ms: float = 0.0
+    rows_sent: int = 0
+    rows_received: int = 0
+
+
+class GpuBackend:
+    """The CUDA library on this rank's device: full router, resident experts."""
+
+    def __init__(self, w_router: np.ndarray, gate_up_local: np.ndarray, down_local: np.ndarray, n_local: int,
+                 max_tok: int, max_rows: int, down_scale_local=None, device: int | None = None,
+                 n_embd: int = synth.N_EMBD, ff: int = synth.FF, used: int = synth.USED):
+        rc.lib()  # fail loudly before touching the GPU if the extension is missing
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.device, self.n_embd, self.ff, self.used = dev, n_embd, ff, used
+        self.n_experts = w_router.shape[0]
+        self.router_dtype = rc.BF16 if w_router.dtype == np.uint16 else rc.F32
+        self.router_w = torch.from_numpy(np.ascontiguousarray(w_router).view(np.uint8)).to(dev)
+        self.down_scale = None if down_scale_local is None else torch.from_numpy(
+            np.ascontiguousarray(down_scale_local, dtype=np.float32)).to(dev)
+        self.packed = torch.empty(rc.packed_bytes(n_local, n_embd, ff), dtype=torch.uint8, device=dev)
+        gu = torch.from_numpy(np.ascontiguousarray(gate_up_local).reshape(-1)).to(dev)
+        dn = torch.from_numpy(np.ascontiguousarray(down_local).reshape(-1)).to(dev)
+        rc.pack_experts(gu, dn, n_local, n_embd, ff, self.packed, _stream_handle(None))
+        torch.cuda.current_stream().synchronize()
+        del gu, dn
+        # routing uses the full router (n_experts); the expert calls see only the resident experts
+        self.w_route = rc.weights_struct(n_embd, ff, self.n_experts, used, self.router_dtype, self.router_w,
+                                         self.packed, None)
+        self.w_local = rc.weights_struct(n_embd, ff, n_local, min(used, n_local), self.router_dtype, self.router_w,
+                                         self.packed, self.down_scale)
+        self.ws_route = torch.empty(rc.workspace_bytes(max_tok, n_embd, ff, self.n_experts, used), dtype=torch.uint8,
+                                    device=dev)
+        rc.workspace_reset(self.ws_route, _stream_handle(None))
+        self.max_pairs = max_rows * used
+        self.ws_ep = torch.empty(rc.ep_workspace_bytes(self.max_pairs, n_embd, ff, n_local), dtype=torch.uint8,
+                                 device=dev)
+        rc.workspace_reset(self.ws_ep, _stream_handle(None))
+        self.record_bytes = rc.q8_record_bytes(n_embd)
+
+    def route(self, x: torch.Tensor, bias: torch.Tensor | None = None):
+        """ids, wts [n, used]; bias: per-expert logit offsets [n_experts] or [n, n_experts]."""
+        n = x.shape[0]
+        ids = torch.empty((n, self.used), dtype=torch.int32, device=self.device)
+        wts = torch.empty((n, self.used), dtype=torch.float32, device=self.device)
+        stride = self.n_experts if bias is not None and bias.dim() == 2 else 0
+        rc.moe_router(self.w_route, x, _xdtype(x), n, self.ws_route, bias=bias, bias_stride=stride, ids=ids, wts=wts,
+                      stream=_stream_handle(None))
+        return ids, wts
+
+    def quant(self, x: torch.Tensor) -> torch.Tensor:
+        rec = torch.empty((x.shape[0], self.record_bytes), dtype=torch.uint8, device=self.device)
+        rc.quant_q8_rows(x, _xdtype(x), x.shape[0], self.n_embd, rec, _stream_handle(None))
+        return rec
+
+    def experts(self, rec, row_start, pair_expert, pair_w) -> torch.Tensor:
+        n_rows, n_pairs = rec.shape[0], pair_expert.shape[0]
+        if n_pairs > self.max_pairs:
+            raise ValueError(f"{n_pairs} pairs exceed the workspace's {self.max_pairs}")
+        partial = torch.empty((n_rows, self.n_embd), dtype=torch.float32, device=self.device)
+        rc.ep_experts(self.w_local, rec, n_rows, row_start, pair_expert, pair_w, n_pairs, partial, self.ws_ep,
+                      _stream_handle(None))
+        return partial
+
+    def reduce(self, partial, src_start, src_row, n_tok: int) -> torch.Tensor:
+        out = torch.empty((n_tok, self.n_embd), dtype=torch.float32, device=self.device)
+        rc.ep_reduce(partial, partial.shape[0], src_start, src_row, n_tok, self.n_embd, out, _stream_handle(None))
+        return out
+
+    def status(self) -> None:
+        rc.status(self.ws_route, _stream_handle(None))
+        rc.status(self.ws_ep, _stream_handle(None))
+
+
+def _xdtype(x: torch.Tensor) -> int:
+    if x.dtype == torch.bfloat16:
+        return rc.BF16
+    if x.dtype == torch.float32:
+        return rc.F32
+    raise TypeError("activations must be bf16 or f32")
+
+
+@dataclass
+class _Plan:
+    send_tok: torch.Tensor    # [S] int64: owner-local token of each sent row, grouped by destination rank
+    send_counts: list         # rows per destination rank
+    meta_e: torch.Tensor      # [S, used] int32: the row's experts at the destination (local ids), -1 if none
+    meta_w: torch.Tensor      # [S, used] f32: their routing weights
+
+
+def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, n_local: int) -> _Plan:
+    """Rows to send: token t goes once to every rank holding one of its experts; its slots there
+    keep the token's slot order (absent slots -1)."""
+    n, used = ids.shape
+    dest = (ids // n_local).to(torch.int64)                                  # [n, used]
+    hit = torch.zeros((n, world), dtype=torch.bool, device=ids.device)
+    hit.scatter_(1, dest, True)
+    # rows grouped by destination rank, tokens ascending within a rank
+    r_idx, t_idx = torch.nonzero(hit.t(), as_tuple=True)
+    counts = torch.bincount(r_idx, minlength=world)
+    sel = dest[t_idx] == r_idx[:, None]                                      # [S, used]
+    meta_e = torch.where(sel, (ids[t_idx] - (r_idx[:, None] * n_local).to(ids.dtype)), torch.full_like(ids[t_idx], -1))
+    meta_w = torch.where(sel, wts[t_idx], torch.zeros_like(wts[t_idx]))
+    return _Plan(t_idx, counts.tolist(), meta_e.to(torch.int32).contiguous(), meta_w.contiguous())
+
+
+def _csr(counts: torch.Tensor) -> torch.Tensor:
+    return torch.cat([torch.zeros(1, dtype=torch.int64, device=counts.device), torch.cumsum(counts, 0)]).to(torch.int32)
+
+
+class EpMoeLayer:
+    """One rank of the expert-parallel layer. `backend` does the compute on this rank's device;
+    `group` is the process group of the N ranks (rank r holds experts [r E/N, (r + 1) E/N))."""
+
+    def __init__(self, backend, rank: int, world: int, n_experts: int = synth.N_EXPERTS, group=None):
+        if n_experts % world:
+            raise ValueError("experts must divide evenly over the ranks")
+        self.be, self.rank, self.world, self.group = backend, rank, world, group
+        self.n_local = n_experts // world
+        self.stats = EpStats()
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's tokens x [n, n_embd] (bf16 or f32) -> their layer output [n, n_embd] f32.
+        bias: router logit offsets, [n_experts] or [n, n_experts] (the skewed-load configs)."""
+        be, world = self.be, self.world
+        dev = x.device
+        timed = dev.type == "cuda"
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timed else None
+        ids, wts = be.route(x, bias)
+        self.last_ids = ids
+        rec = be.quant(x)
+        p = plan_dispatch(ids, wts, world, self.n_local)
+        # 3. dispatch: counts, then records and slot metadata
+        send_counts = torch.tensor(p.send_counts, dtype=torch.int64, device=dev)
+        recv_counts = torch.empty_like(send_counts)
+        if timed:
+            ev[0].record()
+        self._a2a(recv_counts, send_counts, None, None)
+        rc_list = recv_counts.tolist()
+        n_recv = int(sum(rc_list))
+        send_rec = rec.index_select(0, p.send_tok)
+        recv_rec = torch.empty((n_recv, rec.shape[1]), dtype=rec.dtype, device=dev)
+        recv_e = torch.empty((n_recv, p.meta_e.shape[1]), dtype=torch.int32, device=dev)
+        recv_w = torch.empty((n_recv, p.meta_w.shape[1]), dtype=torch.float32, device=dev)
+        self._a2a(recv_rec, send_rec, rc_list, p.send_counts)
+        self._a2a(recv_e, p.meta_e, rc_list, p.send_counts)
+        self._a2a(recv_w, p.meta_w, rc_list, p.send_counts)
+        if timed:
+            ev[1].record()
+        # 4. resident experts: each row's slots in slot order
+        valid = recv_e >= 0
+        row_start = _csr(valid.sum(1))
+        pair_expert = recv_e[valid].contiguous()
+        pair_w = recv_w[valid].contiguous()
+        partial = be.experts(recv_rec, row_start, pair_expert, pair_w)
+        # 5. combine: partials back to their owners, summed per token in rank order
+        back = torch.empty((p.send_tok.shape[0], partial.shape[1]), dtype=partial.dtype, device=dev)
+        if timed:
+            ev[2].record()
+        self._a2a(back, partial, p.send_counts, rc_list)
+        if timed:
+            ev[3].record()
+        # rows of `back` are grouped by rank (ascending) and by token within a rank; a stable sort
+        # by token lists each token's ranks in ascending order
+        src_row = torch.sort(p.send_tok, stable=True).indices.to(torch.int32)
+        src_start = _csr(torch.bincount(p.send_tok, minlength=x.shape[0]))
+        out = be.reduce(back, src_start, src_row, x.shape[0])
+        if timed:
+            torch.cuda.synchronize(dev)
+            self.stats = EpStats(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]), int(p.send_tok.shape[0]),
+                                 n_recv)
+        else:
+            self.stats = EpStats(0.0, 0.0, int(p.send_tok.shape[0]), n_recv)
+        return out
+
+
+def local_experts(gate_up: np.ndarray, down: np.ndarray, rank: int, world: int):
+    """This rank's slices of the expert tensors (reference layout, one expert per leading index)."""
+    n = gate_up.shape[0] // world
+    return gate_up[rank * n:(rank + 1) * n], down[rank * n:(rank + 1) * n]

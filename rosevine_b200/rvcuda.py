@@ -31,7 +31,8 @@ EXPORTS = [
     "rvc_event_elapsed", "rvc_upload_async", "rvc_download_async", "rvc_event_record_on", "rvc_stream_sync",
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
-    "rvc_debug_mma_i8",
+    "rvc_debug_mma_i8", "rvc_q8_record_bytes", "rvc_quant_q8_rows", "rvc_ep_workspace_bytes", "rvc_ep_experts",
+    "rvc_ep_reduce",
 ]
 
 
@@ -97,6 +98,11 @@ def lib() -> ctypes.CDLL:
             "rvc_debug_block_sums": ([W, I, I, P, I, P, I, P, P], I),
             "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
             "rvc_debug_mma_i8": ([P, P, I, P, P, P], I),
+            "rvc_q8_record_bytes": ([I], Z),
+            "rvc_quant_q8_rows": ([P, I, I, I, P, P], I),
+            "rvc_ep_workspace_bytes": ([I, I, I, I], Z),
+            "rvc_ep_experts": ([W, P, I, P, P, P, I, P, P, Z, P], I),
+            "rvc_ep_reduce": ([P, P, P, I, I, P, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -295,3 +301,32 @@ def debug_mma_i8(a, b, n: int, d, status, stream: int | None = None) -> None:
     """d[128][n] = a[128][32] . b[n][32]^T through one tensor-core tile (int8 in, int32 out)."""
     check(lib().rvc_debug_mma_i8(_ptr(a, 128 * 32), _ptr(b, n * 32), n, _ptr(d, 128 * n * 4), _ptr(status, 4),
                                  stream))
+
+
+# -------------------------------------------------------------- expert parallelism
+def q8_record_bytes(n_embd: int) -> int:
+    return lib().rvc_q8_record_bytes(n_embd)
+
+
+def ep_workspace_bytes(max_pairs: int, n_embd: int, ff: int, n_experts: int) -> int:
+    return lib().rvc_ep_workspace_bytes(max_pairs, n_embd, ff, n_experts)
+
+
+def quant_q8_rows(x, x_dtype: int, n_rows: int, n_embd: int, records, stream: int | None = None) -> None:
+    check(lib().rvc_quant_q8_rows(_ptr(x, n_rows * n_embd * _xbytes(x_dtype)), x_dtype, n_rows, n_embd,
+                                  _ptr(records, n_rows * q8_record_bytes(n_embd)), stream))
+
+
+def ep_experts(w: MoeWeights, records, n_rows: int, row_start, pair_expert, pair_w, n_pairs: int, partial,
+               workspace, stream: int | None = None) -> None:
+    ws = view_of(workspace)
+    check(lib().rvc_ep_experts(ctypes.byref(w), _ptr(records, n_rows * q8_record_bytes(w.n_embd)), n_rows,
+                               _ptr(row_start, (n_rows + 1) * 4), _ptr(pair_expert, n_pairs * 4),
+                               _ptr(pair_w, n_pairs * 4), n_pairs, _ptr(partial, n_rows * w.n_embd * 4), ws.ptr,
+                               ws.nbytes, stream))
+
+
+def ep_reduce(partial, n_partial: int, src_start, src_row, n_tok: int, n_embd: int, out,
+              stream: int | None = None) -> None:
+    check(lib().rvc_ep_reduce(_ptr(partial, n_partial * n_embd * 4), _ptr(src_start, (n_tok + 1) * 4),
+                              _ptr(src_row, n_partial * 4), n_tok, n_embd, _ptr(out, n_tok * n_embd * 4), stream))
