@@ -64,9 +64,12 @@ class GpuBackend:
         rc.pack_experts(gu, dn, n_local, n_embd, ff, self.packed, _stream_handle(None))
         torch.cuda.current_stream().synchronize()
         del gu, dn
-        # routing uses the full router (n_experts); the expert calls see only the resident experts
-        self.w_route = rc.weights_struct(n_embd, ff, self.n_experts, used, self.router_dtype, self.router_w,
-                                         self.packed, None)
+        # routing uses the full router (n_experts); rvc_moe_router reads only the router rows, so
+        # its weights struct points at the resident experts' planes without covering all experts
+        self.w_route = rc.MoeWeights(n_embd, ff, self.n_experts, used, self.router_dtype,
+                                     rc.view_of(self.router_w).need(self.n_experts * n_embd * (2 if self.router_dtype
+                                                                                                == rc.BF16 else 4)),
+                                     self.packed.data_ptr(), None)
         self.w_local = rc.weights_struct(n_embd, ff, n_local, min(used, n_local), self.router_dtype, self.router_w,
                                          self.packed, self.down_scale)
         self.ws_route = torch.empty(rc.workspace_bytes(max_tok, n_embd, ff, self.n_experts, used), dtype=torch.uint8,
