@@ -1,24 +1,29 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 MoE layer (driver contract: one JSON line on rank 0).
 
-Workload at N=1: the batched-decode sweep of one MoE layer,
-B in {1, 2, 4, 8, 16, 32, 64} tokens, seeded synthetic bf16 inputs and Q4_0 experts of the
-target's shapes (2816 / 704 / 128 experts / top-8). One step = one layer call at every B
-(127 tokens). The L2 (126 MB) is flushed before every timed layer call by writing a 256 MB
-buffer outside the timed events, so expert weights always stream from HBM.
+Metric (BASELINE): MoE layer us/token at B=1 (HBM GB/s) and prefill tokens/s at 1/2/4/8 GPUs.
 
-- value: tokens/s over the sweep, device time (CUDA events on the launching stream);
-- decode: per-B us/layer and achieved HBM GB/s (algorithmic bytes: distinct experts x
-  3,345,408 B + router + activations), the headline us/token at B=1;
-- roofline: the expert GEMV phase (rvc_moe_experts) timed alone against the measured HBM peak;
-- e2e: the same sweep through the C ABI from pinned host buffers (H2D of x, the layer, D2H
-  of the output, all inside the timed region);
-- cpu_baseline: the oracle's port of the reference CPU-experts Q8_0 path (AVX2, persistent
-  pool, all host cores), on a bounded sample of the same sweep.
+- value: prefill tokens/s of one MoE layer over PREFILL_TOK = 16384 tokens (configs[3]: bf16
+  N(0,1) RMS-normalised rows, the random router's natural, near-uniform routing, Q4_0 experts of
+  the target's shapes 2816 / 704 / 128 experts / top-8). At N = 1 the tokens go through the
+  single-device layer (rvc_moe_forward); at N > 1 (torchrun) each rank holds 128/N experts and
+  16384/N tokens and the layer runs expert-parallel (rosevine_b200.ep: NCCL all-to-allv
+  dispatch/combine). Total work is fixed (strong scaling); device time by CUDA events on the
+  launching stream, max over ranks. The inputs (92 MB of x, 428 MB of experts, 1.5 GB of
+  intermediates) exceed the 126 MB L2, so no flush is needed between steps.
+- prefill: per-step ms, int8 TOPS against the int8 dense peak (2 x the measured bf16 peak), and
+  at N > 1 the exposed all-to-all time (dispatch and combine, CUDA events).
+- decode (N = 1): the batched-decode sweep of configs[1], B in {1, 2, 4, 8, 16, 32, 64}, L2
+  flushed (256 MB write) before every timed call: per-B us/layer, achieved HBM GB/s
+  (algorithmic bytes: distinct experts x 3,345,408 B + router + activations), the headline
+  us/token at B = 1, and its roofline against the measured HBM peak.
+- roofline: the decode layer (the HBM-bound hot path the north star sets a 70% target for).
+- e2e: the prefill through the public API from pinned host buffers (H2D of x, the layer, D2H of
+  the output inside the timed region).
+- cpu_baseline (N = 1): the oracle port of the reference CPU-experts Q8_0 path (AVX2, all host
+  cores) on a bounded sample of the prefill workload.
 
-`--impl reference` times only that CPU path (the reference arm). With N>1 GPUs (torchrun) every
-rank runs the sweep as an independent replica (decode at B <= 64 is not sharded), timing is the
-max over ranks and value is the whole-job tokens/s.
+`--impl reference` times that CPU path alone on the prefill workload (rank 0 only).
 """
 from __future__ import annotations
 
@@ -37,8 +42,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "MoE layer µs/token @B=1 (HBM GB/s) and prefill tokens/s @1/2/4/8 B200"
 SWEEP = [1, 2, 4, 8, 16, 32, 64]
+PREFILL_TOK = 16384
 EXPERT_BYTES = 3_345_408
 ROUTER_BYTES = 128 * 2816 * 2
+OPS_PER_TOKEN = 2 * 8 * (1408 * 2816 + 2816 * 704)  # int8 MACs x 2 of the 8 experts' gate/up and down
+DTYPE = "int8xq4 (Q8_0 x Q4_0, f32 accumulate)"
+DATA = "synthetic (seeded; BASELINE distributions)"
 
 
 def algorithmic_bytes(n_tok: int, distinct: int) -> int:
@@ -50,8 +59,8 @@ def measured_peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "int8_tops": 2 * d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "int8_tops": 2 * 1590.0, "source": "fallback"}
 
 
 # ------------------------------------------------------------------- clocks
@@ -78,12 +87,12 @@ class ClockSampler:
         self.path = os.path.join("/tmp", f"rvc_clocks_{os.getpid()}.csv")
 
     def start(self):
-        """Start sampling every 20 ms and wait (up to 5 s) until the first sample is written,
+        """Start sampling every 100 ms and wait (up to 5 s) until the first sample is written,
         so that the timed region that follows is covered from its start."""
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -125,36 +134,42 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_sweep(weights, inputs, budget_s: float, threads: int | None = None) -> dict:
-    """The oracle port of the reference CPU-experts Q8_0 path, timed per B on host cores."""
+def cpu_prefill(budget_s: float, seed: int, threads: int | None = None) -> dict:
+    """The oracle port of the reference CPU-experts Q8_0 path on host cores, over consecutive
+    256-token slices of the prefill workload for about budget_s seconds."""
     from oracle import oracle as O
     O.build()
+    weights, x = prefill_inputs(seed, 0, 1)
     pool = O.Pool(threads)
-    per_b = {}
     try:
-        for b in SWEEP:  # warm-up: page the weights in once
-            O.moe_layer(pool, inputs[b], inputs[b], weights["w_router"], weights["gate_up"], weights["down"])
-        per_b_budget = budget_s / len(SWEEP)
-        for b in SWEEP:
-            xs = inputs[b]
-            ts = []
-            t_end = time.perf_counter() + per_b_budget
-            while time.perf_counter() < t_end or len(ts) < 3:
-                t0 = time.perf_counter()
-                O.moe_layer(pool, xs, xs, weights["w_router"], weights["gate_up"], weights["down"])
-                ts.append(time.perf_counter() - t0)
-            per_b[b] = statistics.median(ts)
+        O.moe_layer(pool, x[:64], x[:64], weights["w_router"], weights["gate_up"], weights["down"])  # page in
+        done, t_cpu, i = 0, 0.0, 0
+        while t_cpu < budget_s or done == 0:
+            s = x[(i * 256) % PREFILL_TOK:(i * 256) % PREFILL_TOK + 256]
+            t0 = time.perf_counter()
+            O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"])
+            t_cpu += time.perf_counter() - t0
+            done += s.shape[0]
+            i += 1
         n = pool.threads
     finally:
         pool.close()
-    step = sum(per_b.values())
-    return {"value": sum(SWEEP) / step, "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": f"median over >=3 calls per B of the B in {SWEEP} sweep, ~{budget_s:.0f} s of CPU work; "
-                      f"oracle/rv_oracle.c AVX2 int8 routine, persistent pool",
-            "b1_us_per_token": per_b[1] * 1e6, "per_b_ms": {str(b): per_b[b] * 1e3 for b in SWEEP}}
+    return {"value": done / t_cpu, "unit": "tokens/s", "cores": n, "kind": "port",
+            "sample": f"{done} of the {PREFILL_TOK} prefill tokens in 256-token calls, ~{t_cpu:.0f} s of CPU work; "
+                      f"oracle/rv_oracle.c AVX2 int8 routine, persistent pool of {n} threads"}
 
 
 # ------------------------------------------------------------------- inputs
+def prefill_inputs(seed: int, rank: int, world: int):
+    """Weights (all experts) and this rank's shard of the prefill tokens."""
+    from rosevine_b200 import synth
+    gu, dn = synth.experts(seed + 2)
+    weights = {"gate_up": gu, "down": dn, "w_router": synth.router(seed + 1)}
+    x = synth.tokens(PREFILL_TOK, seed + 77)
+    n = PREFILL_TOK // world
+    return weights, x[rank * n:(rank + 1) * n]
+
+
 def make_inputs(seed: int = 0):
     from rosevine_b200 import synth
     gu, dn = synth.experts(seed + 2)
@@ -167,16 +182,13 @@ def distinct_experts(ids: np.ndarray) -> int:
     return int(np.unique(ids).size)
 
 
-# ---------------------------------------------------------------- GPU arm
-def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
+# ---------------------------------------------------------------- decode sweep (N = 1)
+def run_decode(args, local_rank: int, peaks: dict) -> dict:
     import torch
-    import torch.distributed as dist
-    from rosevine_b200 import rvcuda as rc
     from rosevine_b200.moe import MoeLayer, to_device_x
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    weights, inputs = make_inputs(args.seed + rank)
+    weights, inputs = make_inputs(args.seed)
     layer = MoeLayer(weights["w_router"], weights["gate_up"], weights["down"], max_tok=max(SWEEP), device=local_rank)
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
@@ -185,13 +197,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     outs = {b: torch.empty((b, 2816), dtype=torch.float32, device=dev) for b in SWEEP}
     ids = {b: torch.empty((b, 8), dtype=torch.int32, device=dev) for b in SWEEP}
     wts = {b: torch.empty((b, 8), dtype=torch.float32, device=dev) for b in SWEEP}
-    # pinned host buffers for the e2e path
-    hx = {b: torch.from_numpy(inputs[b].view(np.int16)).pin_memory() for b in SWEEP}
-    ho = {b: torch.empty((b, 2816), dtype=torch.float32).pin_memory() for b in SWEEP}
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in SWEEP]
-
-    # One CUDA graph per B holding the layer call (the C ABI call captured as-is: K0 on the
-    # library's side lane, K1, gate/up, down+combine). Warm-up outside capture first.
+    # one CUDA graph per B holding the layer call (warm-up outside capture first)
     graphs, graphs_exp = {}, {}
     for b in SWEEP:
         layer.forward(xs[b], out=outs[b], ids=ids[b], wts=wts[b], stream=sh)
@@ -208,7 +215,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         graphs_exp[b] = g2
     torch.cuda.synchronize()
 
-    def step_graph(timed: bool, which=graphs):
+    def step(which, timed: bool):
         for i, b in enumerate(SWEEP):
             flush.zero_()
             if timed:
@@ -217,149 +224,211 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
             if timed:
                 ev[i][1].record(stream)
 
-    def step_stream(timed: bool):
-        for i, b in enumerate(SWEEP):
-            flush.zero_()
-            if timed:
-                ev[i][0].record(stream)
-            layer.forward(xs[b], out=outs[b], ids=ids[b], wts=wts[b], stream=sh)
-            if timed:
-                ev[i][1].record(stream)
-
-    def step_e2e(timed: bool):
-        for i, b in enumerate(SWEEP):
-            flush.zero_()
-            if timed:
-                ev[i][0].record(stream)
-            rc.check(rc.lib().rvc_upload_async(xs[b].data_ptr(), hx[b].data_ptr(), hx[b].numel() * 2, sh))
-            layer.forward(xs[b], out=outs[b], ids=ids[b], wts=wts[b], stream=sh)
-            rc.check(rc.lib().rvc_download_async(ho[b].data_ptr(), outs[b].data_ptr(), ho[b].numel() * 4, sh))
-            if timed:
-                ev[i][1].record(stream)
-
-    def timed_loop(fn, steps, warmup):
+    def timed_loop(which, steps, warmup):
         for _ in range(warmup):
-            fn(False)
+            step(which, False)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         per_b = {b: 0.0 for b in SWEEP}
         for _ in range(steps):
-            fn(True)
+            step(which, True)
             torch.cuda.synchronize()
             for i, b in enumerate(SWEEP):
                 per_b[b] += ev[i][0].elapsed_time(ev[i][1])
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         return {b: per_b[b] / steps for b in SWEEP}  # ms per call
 
-    clocks = ClockSampler(gpu_smi_id(local_rank))
-    clocks.start()
-    per_b = timed_loop(step_graph, args.steps, args.warmup)
-    clk = clocks.stop()
+    steps = max(10, args.decode_steps)
+    per_b = timed_loop(graphs, steps, args.warmup)
+    phase = timed_loop(graphs_exp, steps, args.warmup)
     layer.status(stream=sh)
-    per_b_stream = timed_loop(step_stream, args.steps, args.warmup)
-    per_b_e2e = timed_loop(step_e2e, max(1, args.steps), max(1, args.warmup))
-    phase = timed_loop(lambda t: step_graph(t, graphs_exp), args.steps, args.warmup)
-    layer.status(stream=sh)
-
     distinct = {b: distinct_experts(ids[b].cpu().numpy()) for b in SWEEP}
-    step_ms = sum(per_b.values())
-    e2e_ms = sum(per_b_e2e.values())
-    if world > 1:
-        t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, e2e_ms = float(t[0]), float(t[1])
-    if rank != 0:
-        return None
-    peaks = measured_peaks()
-    tokens = sum(SWEEP)
-    decode = []
+    rows = []
     for b in SWEEP:
         byt = algorithmic_bytes(b, distinct[b])
-        decode.append({"B": b, "us_per_layer": per_b[b] * 1e3, "distinct_experts": distinct[b],
-                       "algorithmic_bytes": byt, "hbm_gbs": byt / (per_b[b] * 1e-3) / 1e9,
-                       "frac_of_hbm": byt / (per_b[b] * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                       "us_per_layer_no_graph": per_b_stream[b] * 1e3,
-                       "expert_phase_us": phase[b] * 1e3, "e2e_us": per_b_e2e[b] * 1e3})
-    # roofline of the whole decode layer over the sweep (algorithmic bytes and device time
-    # summed over B), and of the expert GEMV phase alone
+        rows.append({"B": b, "us_per_layer": per_b[b] * 1e3, "distinct_experts": distinct[b], "algorithmic_bytes": byt,
+                     "hbm_gbs": byt / (per_b[b] * 1e-3) / 1e9, "frac_of_hbm": byt / (per_b[b] * 1e-3) / 1e9 /
+                     peaks["hbm_gbs"], "expert_phase_us": phase[b] * 1e3})
     lay_bytes = sum(algorithmic_bytes(b, distinct[b]) for b in SWEEP)
-    achieved = lay_bytes / (step_ms * 1e-3) / 1e9
-    ph_bytes = sum(distinct[b] * EXPERT_BYTES for b in SWEEP)
-    ph_gbs = ph_bytes / (sum(phase.values()) * 1e-3) / 1e9
-    h2d = sum(b * 2816 * 2 for b in SWEEP)
-    d2h = sum(b * 2816 * 4 for b in SWEEP)
+    sweep_ms = sum(per_b.values())
+    achieved = lay_bytes / (sweep_ms * 1e-3) / 1e9
+    ph_gbs = sum(distinct[b] * EXPERT_BYTES for b in SWEEP) / (sum(phase.values()) * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_fd_route, k_fd_gate, k_fd_down), "
+                                           "algorithmic bytes and device time summed over the B sweep",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "peak_source": peaks["source"], "b1_frac": rows[0]["frac_of_hbm"],
+                "expert_phase_gbs": ph_gbs, "expert_phase_frac": ph_gbs / peaks["hbm_gbs"], "traffic": None}
+    return {"workload": "configs[1]: batched decode sweep B in {1,2,4,8,16,32,64}, L2 flushed before every call",
+            "steps": steps, "b1_us_per_token": per_b[1] * 1e3, "b1_hbm_gbs": rows[0]["hbm_gbs"],
+            "sweep_tokens_per_s": sum(SWEEP) / (sweep_ms * 1e-3), "per_b": rows, "roofline": roofline,
+            "gpu_launches_per_call": 3}
+
+
+# ---------------------------------------------------------------- prefill (all N)
+def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> dict:
+    import torch
+    import torch.distributed as dist
+    from rosevine_b200.moe import MoeLayer, to_device_x
+
+    dev = torch.device("cuda", local_rank)
+    weights, xs = prefill_inputs(args.seed, rank, world)
+    n = xs.shape[0]
+    x = to_device_x(xs, dev)
+    hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
+    ho = torch.empty((n, 2816), dtype=torch.float32).pin_memory()
+    if world == 1:
+        layer = MoeLayer(weights["w_router"], weights["gate_up"], weights["down"], max_tok=n, device=local_rank)
+        out = torch.empty((n, 2816), dtype=torch.float32, device=dev)
+
+        def fwd():
+            return layer.forward(x, out=out)
+        launches = 7  # k_router_chains, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_ms, k_pf_combine
+        check = layer.status
+    else:
+        from rosevine_b200.ep import EpMoeLayer, GpuBackend, local_experts
+        gl, dl = local_experts(weights["gate_up"], weights["down"], rank, world)
+        be = GpuBackend(weights["w_router"], gl, dl, 128 // world, max_tok=n, max_rows=PREFILL_TOK, device=local_rank)
+        layer = EpMoeLayer(be, rank, world)
+
+        def fwd():
+            return layer.forward(x)
+        # k_router_chains, k_select, k_quant_rows, k_plan, k_ep_scatter, 2 x k_pf_gemm_ms, k_pf_combine,
+        # k_ep_reduce (NCCL's own kernels not counted)
+        launches = 9
+        check = be.status
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    phases = {}
+
+    def loop(steps, e2e: bool):
+        tot, disp, comb = 0.0, 0.0, 0.0
+        phases.clear()
+        for _ in range(steps):
+            ev0.record(stream)
+            if e2e:
+                x.copy_(hx.view(torch.bfloat16), non_blocking=True)
+            o = fwd()
+            if e2e:
+                ho.copy_(o, non_blocking=True)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            tot += ev0.elapsed_time(ev1)
+            if world > 1:
+                disp += layer.stats.dispatch_ms
+                comb += layer.stats.combine_ms
+                for k, v in layer.stats.phases_ms.items():
+                    phases[k] = phases.get(k, 0.0) + v / steps
+        return tot / steps, disp / steps, comb / steps
+
+    for _ in range(args.warmup):
+        fwd()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(gpu_smi_id(local_rank))
+    clocks.start()
+    step_ms, disp_ms, comb_ms = loop(args.steps, False)
+    clk = clocks.stop()
+    phases_main = dict(phases)
+    if world > 1:
+        dist.barrier()
+    e2e_ms, _, _ = loop(max(3, args.steps // 2), True)
+    check()
+    t = torch.tensor([step_ms, e2e_ms, disp_ms, comb_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms, disp_ms, comb_ms = (float(v) for v in t)
+    tops = OPS_PER_TOKEN * PREFILL_TOK / world / (step_ms * 1e-3) / 1e12
+    return {"step_ms": step_ms, "e2e_ms": e2e_ms, "tokens_per_s": PREFILL_TOK / (step_ms * 1e-3),
+            "e2e_tokens_per_s": PREFILL_TOK / (e2e_ms * 1e-3), "int8_tops_per_gpu": tops,
+            "int8_frac_per_gpu": tops / peaks["int8_tops"], "exposed_all_to_all_ms": disp_ms + comb_ms,
+            "dispatch_ms": disp_ms, "combine_ms": comb_ms, "launches": launches, "clocks": clk,
+            "rank0_phases_ms": phases_main or None,
+            "h2d_bytes_per_step": PREFILL_TOK * 2816 * 2, "d2h_bytes_per_step": PREFILL_TOK * 2816 * 4}
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    torch.cuda.set_device(local_rank)
+    peaks = measured_peaks()
+    pf = run_prefill(args, rank, world, local_rank, peaks)
+    dec = run_decode(args, local_rank, peaks) if world == 1 and not args.no_decode else None
+    if rank != 0:
+        return None
     res = {
-        "metric": METRIC, "value": world * tokens / (step_ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4 (Q8_0 x Q4_0, f32 accumulate)",
-        "data": "synthetic (seeded; BASELINE distributions)",
-        "config": {"workload": "configs[1]: batched decode sweep B in {1,2,4,8,16,32,64}, one MoE layer "
-                               "(2816/704, 128 experts, top-8, Q4_0 experts, bf16 x)",
-                   "tokens_per_step": tokens, "l2": "flushed (256 MB write) before every timed layer call",
-                   "parallelism": "replicas" if world > 1 else "single GPU"},
-        "decode": {"b1_us_per_token": per_b[1] * 1e3, "b1_hbm_gbs": decode[0]["hbm_gbs"], "per_b": decode},
-        "roofline": {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_fd_route, k_fd_gate, k_fd_down), "
-                                                "algorithmic bytes and device time summed over the sweep",
-                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                     "expert_phase_gbs": ph_gbs, "expert_phase_frac": ph_gbs / peaks["hbm_gbs"],
+        "metric": METRIC, "value": pf["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": pf["step_ms"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": DTYPE, "data": DATA,
+        "config": {"workload": f"configs[3] at N={world}: prefill of {PREFILL_TOK} tokens through one MoE layer "
+                               f"(2816/704, 128 experts, top-8, Q4_0 experts, bf16 x), "
+                               + ("single device" if world == 1 else f"expert-parallel, {128 // world} experts "
+                                  f"and {PREFILL_TOK // world} tokens per GPU, NCCL all-to-allv"),
+                   "tokens_per_step": PREFILL_TOK, "l2": "inputs and intermediates larger than the 126 MB L2",
+                   "parallelism": "single GPU" if world == 1 else f"ep{world}"},
+        "prefill": {k: v for k, v in pf.items() if k != "clocks"},
+        "roofline": {"bound": "tensor", "kernel": "prefill layer (router, plan, quantise, grouped GEMMs "
+                                                  "k_pf_gemm_ms, combine), int8 MACs of the experts x 2",
+                     "achieved": pf["int8_tops_per_gpu"], "peak": peaks["int8_tops"], "unit": "TOP/s",
+                     "frac": pf["int8_frac_per_gpu"], "peak_source": peaks["source"] + " (2 x bf16 dense)",
                      "traffic": None},
-        "e2e": {"value": world * tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": 3 * len(SWEEP) * args.steps,  # k_fd_route, k_fd_gate, k_fd_down per layer call
-        "clocks": clk,
+        "e2e": {"value": pf["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": pf["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": pf["d2h_bytes_per_step"]},
+        "gpu_launches": pf["launches"] * args.steps * world,
+        "clocks": pf["clocks"],
     }
+    if dec is not None:
+        res["decode"] = dec
     if world == 1 and not args.no_cpu:
-        res["cpu_baseline"] = cpu_sweep(weights, inputs, args.cpu_budget)
+        res["cpu_baseline"] = cpu_prefill(args.cpu_budget, args.seed)
     return res
 
 
 def run_reference(args, rank: int) -> dict | None:
+    """The reference arm: the oracle port of the reference CPU-experts Q8_0 path on the host's
+    cores, each step a 256-token slice of the same prefill workload (rank 0 only)."""
     if rank != 0:
         return None
-    weights, inputs = make_inputs(args.seed)
     from oracle import oracle as O
     O.build()
+    weights, x = prefill_inputs(args.seed, 0, 1)
     pool = O.Pool(None)
-    for b in SWEEP:
-        O.moe_layer(pool, inputs[b], inputs[b], weights["w_router"], weights["gate_up"], weights["down"])
-    for _ in range(args.warmup):
-        for b in SWEEP[:3]:
-            O.moe_layer(pool, inputs[b], inputs[b], weights["w_router"], weights["gate_up"], weights["down"])
-    step_times = []
-    for _ in range(args.steps):
+    sl = 256
+    O.moe_layer(pool, x[:64], x[:64], weights["w_router"], weights["gate_up"], weights["down"])
+    for i in range(args.warmup):
+        s = x[i * sl:(i + 1) * sl]
+        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"])
+    steps = max(1, min(args.steps, 8))  # bounded: a few minutes of host work at most
+    ts = []
+    for i in range(steps):
+        s = x[(i * sl) % PREFILL_TOK:(i * sl) % PREFILL_TOK + sl]
         t0 = time.perf_counter()
-        for b in SWEEP:
-            O.moe_layer(pool, inputs[b], inputs[b], weights["w_router"], weights["gate_up"], weights["down"])
-        step_times.append(time.perf_counter() - t0)
+        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"])
+        ts.append(time.perf_counter() - t0)
     threads = pool.threads
     pool.close()
-    step = statistics.median(step_times)
-    v = sum(SWEEP) / step
-    return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8xq4 (Q8_0 x Q4_0, f32 accumulate)",
-            "data": "synthetic (seeded; BASELINE distributions)", "impl": "reference",
-            "config": {"workload": "configs[1]: batched decode sweep B in {1,2,4,8,16,32,64} on the reference's "
-                                   "CPU-experts Q8_0 path (oracle port: Rust toolchain absent)",
-                       "tokens_per_step": sum(SWEEP), "parallelism": "host threads"},
+    step = statistics.median(ts)
+    v = sl / step
+    return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE, "data": DATA, "impl": "reference",
+            "config": {"workload": f"configs[3] prefill workload ({PREFILL_TOK} tokens) on the reference's CPU-experts "
+                                   f"Q8_0 path (oracle port: the Rust toolchain is absent), {sl}-token slices",
+                       "tokens_per_step": sl, "parallelism": "host threads"},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"{args.steps} full sweeps, median step"},
+                             "sample": f"{steps} slices of {sl} tokens of the prefill workload, median"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--decode-steps", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -373,6 +442,7 @@ def main():
             import datetime
             import torch
             import torch.distributed as dist
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", local_rank))

@@ -42,6 +42,7 @@ class EpStats:
     combine_ms: float = 0.0
     rows_sent: int = 0
     rows_received: int = 0
+    phases_ms: dict | None = None  # device time of each phase of the last forward
 
 
 class GpuBackend:
@@ -170,53 +171,60 @@ class EpMoeLayer:
         bias: router logit offsets, [n_experts] or [n, n_experts] (the skewed-load configs)."""
         be, world = self.be, self.world
         dev = x.device
-        timed = dev.type == "cuda"
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timed else None
+        marks = []
+
+        def mark(name):  # device timestamps between the phases (CUDA only)
+            if dev.type == "cuda":
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                marks.append((name, e))
+
+        mark("start")
         ids, wts = be.route(x, bias)
         self.last_ids = ids
+        mark("route")
         rec = be.quant(x)
+        mark("quantise")
         p = plan_dispatch(ids, wts, world, self.n_local)
         # 3. dispatch: counts, then records and slot metadata
         send_counts = torch.tensor(p.send_counts, dtype=torch.int64, device=dev)
         recv_counts = torch.empty_like(send_counts)
-        if timed:
-            ev[0].record()
+        send_rec = rec.index_select(0, p.send_tok)
+        mark("plan")
         self._a2a(recv_counts, send_counts, None, None)
         rc_list = recv_counts.tolist()
         n_recv = int(sum(rc_list))
-        send_rec = rec.index_select(0, p.send_tok)
         recv_rec = torch.empty((n_recv, rec.shape[1]), dtype=rec.dtype, device=dev)
         recv_e = torch.empty((n_recv, p.meta_e.shape[1]), dtype=torch.int32, device=dev)
         recv_w = torch.empty((n_recv, p.meta_w.shape[1]), dtype=torch.float32, device=dev)
         self._a2a(recv_rec, send_rec, rc_list, p.send_counts)
         self._a2a(recv_e, p.meta_e, rc_list, p.send_counts)
         self._a2a(recv_w, p.meta_w, rc_list, p.send_counts)
-        if timed:
-            ev[1].record()
+        mark("dispatch")
         # 4. resident experts: each row's slots in slot order
         valid = recv_e >= 0
         row_start = _csr(valid.sum(1))
         pair_expert = recv_e[valid].contiguous()
         pair_w = recv_w[valid].contiguous()
+        mark("pairs")
         partial = be.experts(recv_rec, row_start, pair_expert, pair_w)
-        # 5. combine: partials back to their owners, summed per token in rank order
         back = torch.empty((p.send_tok.shape[0], partial.shape[1]), dtype=partial.dtype, device=dev)
-        if timed:
-            ev[2].record()
+        mark("experts")
+        # 5. combine: partials back to their owners, summed per token in rank order
         self._a2a(back, partial, p.send_counts, rc_list)
-        if timed:
-            ev[3].record()
+        mark("combine")
         # rows of `back` are grouped by rank (ascending) and by token within a rank; a stable sort
         # by token lists each token's ranks in ascending order
         src_row = torch.sort(p.send_tok, stable=True).indices.to(torch.int32)
         src_start = _csr(torch.bincount(p.send_tok, minlength=x.shape[0]))
         out = be.reduce(back, src_start, src_row, x.shape[0])
-        if timed:
+        mark("reduce")
+        st = EpStats(rows_sent=int(p.send_tok.shape[0]), rows_received=n_recv)
+        if marks:
             torch.cuda.synchronize(dev)
-            self.stats = EpStats(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]), int(p.send_tok.shape[0]),
-                                 n_recv)
-        else:
-            self.stats = EpStats(0.0, 0.0, int(p.send_tok.shape[0]), n_recv)
+            st.phases_ms = {n1: e0.elapsed_time(e1) for (_, e0), (n1, e1) in zip(marks, marks[1:])}
+            st.dispatch_ms, st.combine_ms = st.phases_ms["dispatch"], st.phases_ms["combine"]
+        self.stats = st
         return out
 
 
