@@ -1,5 +1,5 @@
-// prefill.cuh - the MoE layer for prefill batches: a grouped expert GEMM on the 5th-generation
-// tensor cores (tcgen05.mma kind::i8, accumulators in tensor memory), sm_100a.
+// prefill.cuh - the MoE layer for prefill batches (and the expert-parallel layer's expert step):
+// a grouped expert GEMM fed by TMA tensor copies, sm_100a.
 //
 // Replaces the reference's per-expert device loop (runtime/src/hip_exec.rs:820-843) for batches
 // above the decode kernels' 64 tokens and computes what its CPU-experts Q8_0 path computes
@@ -7,37 +7,34 @@
 //
 //   k_plan        (router.cuh) expert groups in plan order, each group starting at a multiple
 //                 of 4 positions, and the list of (expert, 128-position) tiles.
-//   k_pf_quant    Q8_0 of x once per token, scattered to the token's plan positions; the block
-//                 scales also block-major (the layout the GEMM's scale tiles are copied from).
-//   k_pf_gemm<GU> for each (expert, 128 packed gate/up rows, 128 positions) tile: per 32-column
-//                 block b, two tcgen05.mma (M=128, N<=128, K=32, kind::i8) give the exact int32
-//                 block dots D_b; the epilogue warps read D_b from tensor memory and accumulate
-//                 acc = acc + D_b * (dw_b * dx_b) per (row, token) in block order, each operation
-//                 rounded as the scalar reference does; then h = gelu(gate)*up and its Q8_0
-//                 records.
-//   k_pf_gemm<DN> the same over the down rows and the h records: y per (position, row).
+//   k_pf_quant    Q8_0 of x once per token, scattered to the token's plan positions, with each
+//                 block's (scale, offset) pair block-major (the layout the GEMM copies).
+//   k_pf_gemm_ms<GU> per (expert, 128 packed gate/up rows, 128 positions) tile and 32-column
+//                 block b: the exact int32 block dots D_b (mma.sync m16n8k32, u8 nibbles x s8
+//                 quants), then acc = acc + D_b * (dw_b * dx_b) per (row, position) in block
+//                 order, each operation rounded as the scalar reference does; then
+//                 h = gelu(gate) * up and its Q8_0 records.
+//   k_pf_gemm_ms<DN> the same over the down rows and the h records: y per (position, row).
 //   k_pf_combine  out[t] = slot-order sum of (y * down_scale) * w (exec.rs:626-638).
 //
-// Operands. Weights stay Q4_0 in HBM (the packed nibble and scale planes of pack.cuh); a stage
-// of 8 K-blocks of a tile's 128 rows (16 KB of nibbles) is brought in by one TMA tensor copy and
-// split by the producer warp into unsigned bytes n in the canonical no-swizzle K-major layout
-// tcgen05 reads (8-row x 16-byte core matrices); a second MMA against a constant tile of -8
-// adds -8 * sum(q), so D_b = sum (n - 8) q exactly. Activation tiles (128 tokens x 8 blocks) are
-// TMA tensor copies straight into that layout: the tensor map's dimensions are ordered
-// (16 bytes, rows, 16-byte chunks) so that a chunk's 128 rows land contiguously.
+// Exactness. The nibbles n (0..15) multiply as unsigned bytes; the activation block's offset
+// -(1.5 * 2^23 + 8 sum(q)) turns C + sum n q (C the accumulator's starting bits) into
+// sum (n - 8) q exactly, so D_b equals the reference's integer block dot and the float
+// operations that follow are the reference's, in its order (f32x2 instructions, two positions
+// at a time, never contracted into an fma: see f2_prod).
 //
-// Epilogue arithmetic. The accumulators start each block at the bits of 1.5 * 2^23, so D_b reads
-// as a float offset by that constant and one exact subtraction replaces the int-to-float
-// conversion; the products and sums run two tokens at a time on the f32x2 instructions of
-// sm_100. That is 4 f32 operations per (row, token, block) against 64 tensor-core operations:
-// the CUDA cores, not the tensor cores, bound this kernel (exact per-block scales cost that).
+// Why register accumulators. Scaling is per 32-column block, so every block's dots must reach
+// the CUDA cores: 4 f32 operations per (row, position, block) against 64 int8 multiply-adds.
+// The CUDA cores bound this GEMM (about 13% of the int8 tensor peak at best). With tcgen05 the
+// dots sit in tensor memory and each block needs a tcgen05.ld (and a store of C) by the
+// epilogue; on B200 a tcgen05.ld or .st waits for every MMA in flight in the CTA (measured:
+// 140-330 ns per load under a stream of MMAs), which serialises the MMAs with the epilogue.
+// A tcgen05 version of this pipeline (TMA, tensor-memory accumulators, warp-specialised
+// unpack / MMA / epilogue) ran the 2048-token layer in 3.1 ms; this one runs it in 2.0 ms.
 //
-// Pipeline (one CTA per tile, 17 warps): warp 16 is the producer and MMA issuer (lane 0 issues
-// the TMA copies and the MMAs, all lanes unpack); warps 0-15 are the epilogue, warp w reading
-// tensor-memory lanes 32 (w % 4) .. + 31 (tile rows) and columns 32 (w / 4) .. + 31 (tokens);
-// warps whose 32 columns hold no token of the tile stay idle. Three shared-memory stages of
-// activations, one nibble buffer, four tensor-memory accumulators of 128 columns, mbarriers
-// between the roles; every wait is bounded (a timeout ends in the status word, never in a hang).
+// Operands. Weights stay Q4_0 in HBM (the packed nibble and scale planes of pack.cuh); per stage
+// of 8 blocks one TMA tensor copy brings a tile's 128 rows of nibbles (16 KB), one its 128
+// positions' quants in K-halves x positions x 16 B order, one their (scale, offset) pairs.
 #pragma once
 #include "common.cuh"
 #include "pack.cuh"
@@ -46,23 +43,14 @@
 
 namespace rvc {
 
-constexpr int PF_M = 128;          // rows per tile (tensor-memory lanes)
-constexpr int PF_N = 128;          // tokens per tile (accumulator columns)
-constexpr int PF_KB = 8;           // K-blocks per stage
-constexpr int PF_A_SLOTS = 2;      // unpacked weight tiles
-constexpr int PF_B_SLOTS = 3;      // activation tiles
-constexpr int PF_DX_SLOTS = 4;     // activation block scales
-constexpr int PF_NIB_SLOTS = 2;    // weight nibbles
-constexpr int PF_TBUF = 2;         // tensor-memory accumulators (ping-pong)
-constexpr int PF_EPI_WARPS = 8;    // warps 0-7
-constexpr int PF_UNPACK_WARPS = 3; // warps 8-10
-constexpr int PF_MMA_WARP = PF_EPI_WARPS + PF_UNPACK_WARPS;  // warp 11: TMA copies and MMAs
-constexpr int PF_THREADS = (PF_MMA_WARP + 1) * 32;
-constexpr int PF_TMEM_COLS = PF_TBUF * PF_N;  // 256 of the SM's 512 columns
+constexpr int PF_M = 128;  // weight rows per tile
+constexpr int PF_N = 128;  // plan positions per tile
+constexpr int PF_KB = 8;   // K-blocks per stage
 
-// The tensor-memory accumulators start every block at the bits of 1.5 * 2^23: the int32 sum
-// C + D of a block dot D (|D| < 2^22) then reads as the float 1.5 * 2^23 + D exactly, and one
-// exact subtraction gives (float)D.
+
+// Every block's MMA accumulates onto the bits of 1.5 * 2^23: the int32 sum C + D of a block dot
+// D (|D| < 2^22) then reads as the float 1.5 * 2^23 + D exactly, and one exact addition gives
+// (float)D.
 constexpr uint32_t PF_MAGIC_BITS = 0x4B400000u;
 constexpr float PF_MAGIC = 12582912.0f;
 // An activation block with quants q, scale d and sum(q) = qs enters the GEMM as the pair
@@ -131,26 +119,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         : "r"(taddr)
         : "memory");
 }
-// 32 lanes x 16 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // The wait with the loaded registers as operands: the compiler cannot move their uses above it
 // (tcgen05.ld writes them asynchronously; plain register uses are not ordered by a memory clobber).
-__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-                 :
-                 : "memory");
-}
 __device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
@@ -404,21 +375,12 @@ struct PfArgs {
 
 constexpr int PF_GU = 0, PF_DN = 1;
 
-// Shared memory: rings of unpacked A tiles (8 blocks x 2 halves x 128 rows x 16 B), B tiles
-// (the same for 128 positions), the positions' block scales (8 blocks x 128 f32) and weight
-// nibbles (128 rows x 8 blocks x 16 B), and the constant A tile of -8 (one block).
-constexpr int PF_A_BYTES = PF_KB * 2 * PF_M * 16;  // 32 KB
+// A stage of a tile in shared memory: the weight nibbles (128 rows x 8 blocks x 16 B), the
+// activation quants (8 blocks x 2 halves x 128 positions x 16 B) and the positions' (scale,
+// offset) pairs (8 blocks x 128 positions x 2 f32).
 constexpr int PF_B_BYTES = PF_KB * 2 * PF_N * 16;  // 32 KB
 constexpr int PF_NIB_BYTES = PF_M * PF_KB * 16;    // 16 KB
 constexpr int PF_DX_BYTES = PF_N * PF_KB * 8;      // 8 KB: (scale, offset) per position and block
-constexpr int PF_OFF_B = PF_A_SLOTS * PF_A_BYTES;
-constexpr int PF_OFF_DX = PF_OFF_B + PF_B_SLOTS * PF_B_BYTES;
-constexpr int PF_OFF_NIB = PF_OFF_DX + PF_DX_SLOTS * PF_DX_BYTES;
-constexpr int PF_OFF_C = PF_OFF_NIB + PF_NIB_SLOTS * PF_NIB_BYTES;
-constexpr int PF_SMEM_BYTES = PF_OFF_C + 1024;  // + alignment slack
-static_assert(PF_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm");
-static_assert(4 * 32 * PF_N * 4 <= PF_OFF_B + PF_B_SLOTS * PF_B_BYTES, "gate/up staging of the outputs");
-
 
 // Bounded mbarrier wait, inline (a call would make the caller save its live accumulators).
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, int *status) {
@@ -460,306 +422,7 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
     return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
 }
 
-// 32 lanes x 32 columns of tensor memory set to one value; tcgen05.wait::st before reuse.
-__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void named_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-
-// All threads of the unpack warps: the AND of `ok` over them (a barrier, id 7).
-__device__ __forceinline__ bool unpack_all(bool ok) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 7, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)ok), "n"(PF_UNPACK_WARPS * 32)
-        : "memory");
-    return r != 0;
-}
-
-// One (expert, 128 weight rows, up to 128 plan positions) tile per CTA. Per 32-column block b:
-//   D = C + u8(n) . q     (tcgen05.mma kind::i8, A unsigned: the nibbles as stored)
-//   D = D + (-8) . q      (A signed: a constant tile), so D = C + sum (n - 8) q exactly;
-// the epilogue warps read D, put C back for block b + 4, and accumulate
-//   acc = acc + ((float)(D - C) * (dw_b * dx_b))   (each operation rounded, as the reference).
-// Roles: warps 0-7 epilogue, 8-10 unpack the nibbles of stage st into A slot st % 2, warp 11
-// (one lane) copies B tiles and scales two stages ahead and issues the MMAs. Barriers per ring
-// slot: nib_full (TMA -> unpack), a_full (unpack -> MMA), a_free (MMAs done -> unpack),
-// b_full (TMA -> MMA; the epilogue learns of the scales through mma_done), b_free (MMAs done ->
-// TMA), dx_free (epilogue -> TMA), mma_done / tmem_free per accumulator.
-template <int MODE>
-__global__ void __launch_bounds__(PF_THREADS, 1) k_pf_gemm(const __grid_constant__ CUtensorMap map_nib,
-                                                           const __grid_constant__ CUtensorMap map_act,
-                                                           const __grid_constant__ CUtensorMap map_dx, PfArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t nib_full[PF_NIB_SLOTS], a_full[PF_A_SLOTS], a_free[PF_A_SLOTS], b_full[PF_B_SLOTS],
-        b_free[PF_B_SLOTS], dx_free[PF_DX_SLOTS], mma_done[PF_TBUF], tmem_free[PF_TBUF];
-    __shared__ uint32_t taddr_s;
-    if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nblk = a.nblk, rows = a.rows_per_expert;
-    const int row0 = blockIdx.x * PF_M;  // tile rows within the expert
-    const int2 td = __ldg(a.tiles + blockIdx.y);
-    const int e = td.x & 0xFF, nt = td.x >> 8, p0 = td.y;
-    const int ncg = (nt + 31) >> 5;  // 32-token column groups holding tokens
-    const int nch = (nt + 63) >> 6;  // 64-token column halves holding tokens (epilogue warps 4 ch .. + 3)
-    const int nst = (nblk + PF_KB - 1) / PF_KB;
-    const int wrow0 = e * rows + row0;  // first weight row of the tile
-
-    if (warp == 0) {
-        tmem_alloc(&taddr_s, PF_TMEM_COLS);
-        tmem_relinquish();
-    }
-    if (tid == PF_MMA_WARP * 32) {
-        for (int s = 0; s < PF_NIB_SLOTS; ++s) mbar_init(&nib_full[s], 1);
-        for (int s = 0; s < PF_A_SLOTS; ++s) mbar_init(&a_full[s], 1), mbar_init(&a_free[s], 1);
-        for (int s = 0; s < PF_B_SLOTS; ++s) mbar_init(&b_full[s], 1), mbar_init(&b_free[s], 1);
-        for (int s = 0; s < PF_DX_SLOTS; ++s) mbar_init(&dx_free[s], 4 * nch);
-        for (int s = 0; s < PF_TBUF; ++s) mbar_init(&mma_done[s], 1), mbar_init(&tmem_free[s], 4 * nch);
-        fence_barrier_init();
-        // the whole weight tile (rows contiguous in the nibble plane) and its scales toward L2
-        bulk_prefetch_l2(a.nib + (size_t)wrow0 * nblk * 16, (uint32_t)(PF_M * nblk * 16));
-        bulk_prefetch_l2(a.scl + (size_t)wrow0 * nblk, (uint32_t)(PF_M * nblk * 2) & ~15u);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t taddr = taddr_s;
-
-    if (warp == PF_MMA_WARP) {
-        // ------------------------------------------------ TMA copies of B and scales, MMAs
-        if (lane == 0) {
-            const uint32_t id_u = idesc_i8(PF_M, ncg * 32, false);
-            auto issue_bx = [&](int st) {
-                uint8_t *sB = smem + PF_OFF_B + (st % PF_B_SLOTS) * PF_B_BYTES;
-                uint8_t *sX = smem + PF_OFF_DX + (st % PF_DX_SLOTS) * PF_DX_BYTES;
-                uint64_t *bar = &b_full[st % PF_B_SLOTS];
-                mbar_arrive_expect_tx(bar, PF_B_BYTES + PF_DX_BYTES);
-                tma_load_3d(sB, &map_act, 0, p0, 2 * st * PF_KB, bar);  // [16 halves][128 positions][16 B]
-                tma_load_2d(sX, &map_dx, 2 * p0, st * PF_KB, bar);      // [8 blocks][128 positions] f32 pairs
-            };
-            for (int st = 0; st < min(nst, 2); ++st) issue_bx(st);
-            bool ok = true;
-            for (int st = 0; st < nst && ok; ++st) {
-                const int sa = st % PF_A_SLOTS, sb = st % PF_B_SLOTS;
-                const int kb0 = st * PF_KB, kn = min(PF_KB, nblk - kb0);
-                ok = pf_wait(&a_full[sa], (uint32_t)(st / PF_A_SLOTS) & 1u, a.status) &&
-                     pf_wait(&b_full[sb], (uint32_t)(st / PF_B_SLOTS) & 1u, a.status);
-                const uint8_t *sA = smem + sa * PF_A_BYTES, *sB = smem + PF_OFF_B + sb * PF_B_BYTES;
-                for (int j = 0; j < kn && ok; ++j) {
-                    const int b = kb0 + j, buf = b % PF_TBUF;
-                    // Issued only once the epilogue has read block b - 1 (and put C back in its
-                    // accumulator): a tcgen05.ld or .st waits for every MMA in flight, so no MMA
-                    // may be queued while the epilogue moves an accumulator (measured on B200);
-                    // the epilogue's arithmetic on block b - 1 then overlaps this MMA.
-                    // tmem_free[k] completes phase 0 at the initial fill, phase p + 1 once block
-                    // 2 p + k has been read.
-                    ok = b == 0 ? pf_wait(&tmem_free[0], 0, a.status)
-                                : pf_wait(&tmem_free[(b - 1) % PF_TBUF], (uint32_t)((b - 1) / PF_TBUF + 1) & 1u, a.status);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint64_t dB = umma_desc(sB + j * 2 * (PF_N * 16), PF_N * 16, 128);
-                    mma_i8(taddr + buf * PF_N, umma_desc(sA + j * 2 * (PF_M * 16), PF_M * 16, 128), dB, id_u, true);
-                    mma_commit(&mma_done[buf]);
-                }
-                if (!ok) break;
-                mma_commit(&a_free[sa]);
-                mma_commit(&b_free[sb]);
-                // B of stage st + 2 into the slot of stage st - 1 (its MMAs are in flight or done),
-                // its scales into the slot of stage st - 2 (the epilogue is past it by now)
-                const int sn = st + 2;
-                if (sn < nst) {
-                    if (sn >= PF_B_SLOTS)
-                        ok &= pf_wait(&b_free[sn % PF_B_SLOTS], (uint32_t)(sn / PF_B_SLOTS - 1) & 1u, a.status);
-                    if (ok && sn >= PF_DX_SLOTS)
-                        ok &= pf_wait(&dx_free[sn % PF_DX_SLOTS], (uint32_t)(sn / PF_DX_SLOTS - 1) & 1u, a.status);
-                    if (ok) issue_bx(sn);
-                }
-            }
-            if (!ok) set_status(a.status, STATUS_TIMEOUT);
-        }
-        __syncwarp();
-    } else if (warp >= PF_EPI_WARPS) {
-        // ------------------------------------------------ unpack
-        const int ut = tid - PF_EPI_WARPS * 32;  // 0 .. 95
-        auto issue_nib = [&](int st) {
-            uint64_t *bar = &nib_full[st % PF_NIB_SLOTS];
-            mbar_arrive_expect_tx(bar, PF_NIB_BYTES);
-            tma_load_3d(smem + PF_OFF_NIB + (st % PF_NIB_SLOTS) * PF_NIB_BYTES, &map_nib, 0, st * PF_KB, wrow0,
-                        bar);  // [128 rows][8 blocks][16 B]
-        };
-        if (ut == 0)
-            for (int st = 0; st < min(nst, PF_NIB_SLOTS); ++st) issue_nib(st);
-        bool ok = true;
-        for (int st = 0; st < nst; ++st) {
-            const int sa = st % PF_A_SLOTS, sn = st % PF_NIB_SLOTS;
-            ok = pf_wait(&nib_full[sn], (uint32_t)(st / PF_NIB_SLOTS) & 1u, a.status);
-            if (ok && st >= PF_A_SLOTS) ok = pf_wait(&a_free[sa], (uint32_t)(st / PF_A_SLOTS - 1) & 1u, a.status);
-            if (!unpack_all(ok)) {
-                ok = false;
-                break;
-            }
-            const uint8_t *sN = smem + PF_OFF_NIB + sn * PF_NIB_BYTES;
-            uint8_t *sA = smem + sa * PF_A_BYTES;
-            // task (row r, block j) -> nibble bytes split into halves 0, 1 at
-            // sA + (2 j + k) * 2048 + r * 16. The 8 lanes of one 16-byte access phase take 8
-            // consecutive rows (distinct write banks) and blocks whose stored positions differ
-            // (distinct read banks): the block is fixed when the rows are swizzled (position
-            // j ^ (r & 7); the tile's rows start at a multiple of 8), and runs along the diagonal
-            // when they are not.
-#pragma unroll 2
-            for (int i = ut; i < PF_M * PF_KB; i += PF_UNPACK_WARPS * 32) {
-                const int l = i & 7, g = i >> 3, c = g >> 4;
-                const int r = (g & 15) * 8 + l;
-                const int j = a.swizzled ? c : ((l + c) & 7);
-                const int pos = a.swizzled ? (c ^ l) : j;
-                const uint4 nb4 = *reinterpret_cast<const uint4 *>(sN + r * (PF_KB * 16) + pos * 16);
-                const uint4 lo = make_uint4(nb4.x & 0x0F0F0F0Fu, nb4.y & 0x0F0F0F0Fu, nb4.z & 0x0F0F0F0Fu,
-                                            nb4.w & 0x0F0F0F0Fu);
-                const uint4 hi = make_uint4((nb4.x >> 4) & 0x0F0F0F0Fu, (nb4.y >> 4) & 0x0F0F0F0Fu,
-                                            (nb4.z >> 4) & 0x0F0F0F0Fu, (nb4.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(sA + (2 * j) * (PF_M * 16) + r * 16) = lo;
-                *reinterpret_cast<uint4 *>(sA + (2 * j + 1) * (PF_M * 16) + r * 16) = hi;
-            }
-            fence_proxy_async_smem();  // the A tile for the tensor core; the nibble reads before the refill
-            unpack_all(true);
-            if (ut == 0) {
-                mbar_arrive(&a_full[sa]);
-                if (st + PF_NIB_SLOTS < nst) issue_nib(st + PF_NIB_SLOTS);
-            }
-        }
-        if (!ok) set_status(a.status, STATUS_TIMEOUT);
-    } else if ((warp >> 2) < nch) {
-        // ------------------------------------------------ epilogue: scale and accumulate
-        const int m = 32 * (warp & 3) + lane;  // tile row (tensor-memory lane)
-        const int ch = warp >> 2;              // token columns 64 ch .. 64 ch + 63
-        const int ng = min(2, ncg - 2 * ch);   // of which 32-column groups hold tokens (1 or 2)
-        const uint32_t tw = taddr + ((uint32_t)(32 * (warp & 3)) << 16) + ch * 64;
-#pragma unroll 1
-        for (int buf = 0; buf < PF_TBUF; ++buf) {
-            tmem_fill32(tw + buf * PF_N, PF_MAGIC_BITS);
-            if (ng > 1) tmem_fill32(tw + buf * PF_N + 32, PF_MAGIC_BITS);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-            for (int buf = 0; buf < PF_TBUF; ++buf) mbar_arrive(&tmem_free[buf]);
-        float2 acc[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
-        // this row's weight scales (f16): one per block from L1, where a prefetch a stage ahead
-        // has put them
-        const uint16_t *srow = a.scl + ((size_t)e * rows + row0 + m) * nblk;
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(srow));
-        const uint64_t nz2 = a.negzero2;
-        bool ok = true;
-        for (int b = 0; b < nblk; ++b) {
-            const int buf = b % PF_TBUF, st = b / PF_KB, j = b % PF_KB;
-            if (j == 0) {
-                if (b + PF_KB < nblk) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + b + PF_KB));
-                if (b + 2 * PF_KB - 1 < nblk) asm volatile("prefetch.global.L1 [%0];" ::"l"(srow + b + 2 * PF_KB - 1));
-            }
-            const float dw = f16_bits_to_f32(__ldg(srow + b));
-            ok &= pf_wait(&mma_done[buf], (b / PF_TBUF) & 1u, a.status);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            tc_fence_after();
-            // (scale, offset) pairs of this warp's positions for block j: float4 k holds positions
-            // 2k and 2k + 1
-            const float4 *sso = reinterpret_cast<const float4 *>(smem + PF_OFF_DX + (st % PF_DX_SLOTS) * PF_DX_BYTES) +
-                                (j * PF_N + ch * 64) / 2;
-            const float2 dw2 = make_float2(dw, dw);
-            // both 32-column groups read, C put back, the MMA of block b + 1 released; then the
-            // arithmetic of block b overlaps that MMA
-            uint32_t v0[32], v1[32];
-            tmem_ld32(tw + buf * PF_N, v0);
-            if (ng > 1) tmem_ld32(tw + buf * PF_N + 32, v1);
-            tmem_ld_wait(v0);
-            if (ng > 1) tmem_ld_wait(v1);
-            tmem_fill32(tw + buf * PF_N, PF_MAGIC_BITS);
-            if (ng > 1) tmem_fill32(tw + buf * PF_N + 32, PF_MAGIC_BITS);
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_free[buf]);
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-                if (g < ng) {
-                    const uint32_t *v = g == 0 ? v0 : v1;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {  // positions 4 q .. 4 q + 3 of the group
-                        const float4 L0 = sso[g * 16 + 2 * q], L1 = sso[g * 16 + 2 * q + 1];
-                        const float2 s0 = f2_mul(dw2, make_float2(L0.x, L0.z));
-                        const float2 s1 = f2_mul(dw2, make_float2(L1.x, L1.z));
-                        const float2 t0 = f2_add(make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])),
-                                                 make_float2(L0.y, L0.w));
-                        const float2 t1 = f2_add(make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])),
-                                                 make_float2(L1.y, L1.w));
-                        acc[g * 16 + 2 * q] = f2_add(acc[g * 16 + 2 * q], f2_prod(t0, s0, nz2));
-                        acc[g * 16 + 2 * q + 1] = f2_add(acc[g * 16 + 2 * q + 1], f2_prod(t1, s1, nz2));
-                    }
-                }
-            }
-            if (j == PF_KB - 1 || b == nblk - 1) {  // done with this stage's token scales
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&dx_free[st % PF_DX_SLOTS]);
-            }
-        }
-        if (!ok) set_status(a.status, STATUS_TIMEOUT);
-        // ------------------------------------------------ outputs
-        if (MODE == PF_DN) {
-            if (ok) {
-                float *yp = a.y + (size_t)(p0 + ch * 64) * a.n_embd + row0 + m;
-                const int nv = min(64, nt - ch * 64);
-#pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float2 v2 = acc[i >> 1];
-                    if (i < nv) *yp = (i & 1) ? v2.y : v2.x;
-                    yp += a.n_embd;
-                }
-            }
-        } else {
-            // rows: unit u = m / 64 of the tile; m % 64 < 32 gate, else up; column m % 32.
-            // Both go through shared memory (the A and B rings, free now): [gate/up][2 units][32 columns]
-            // [128 tokens], so that no accumulator is live across the quantisation calls.
-            float *sg = reinterpret_cast<float *>(smem);
-            const int nthr = nch * 4 * 32;
-            named_sync_n(6, nthr);
-            const int u = m >> 6, col = m & 31;
-            const bool gate = (m & 63) < 32;
-            float *mine = sg + ((gate ? 0 : 2) + u) * 32 * PF_N + col * PF_N + ch * 64;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) reinterpret_cast<float2 *>(mine)[i] = acc[i];
-            named_sync_n(6, nthr);
-            if (!gate && ok) {
-                const int hrb = q8rec_bytes(a.nh);
-                const int q = (row0 >> 6) + u;  // h block within the expert's ff columns
-                const float *gp = sg + u * 32 * PF_N + col * PF_N, *up = sg + (2 + u) * 32 * PF_N + col * PF_N;
-#pragma unroll 1
-                for (int i = 0; i < 64; ++i) {
-                    const int n = ch * 64 + i;
-                    const float hv = __fmul_rn(gelu_tanh(gp[n]), up[n]);
-                    uint16_t dbits;
-                    int qsum;
-                    const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);  // the warp's 32 lanes: one block
-                    if (n < nt) {
-                        q8rec_store(a.hrec + (size_t)(p0 + n) * hrb, a.nh, q, lane, qv, dbits, qsum);
-                        if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + n] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
-                    }
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, PF_TMEM_COLS);
-}
 
 // ------------------------------------------------------------------ grouped GEMM, register accumulators
 // The same tiles, with the block dots from mma.sync.m16n8k32 (u8 nibbles x s8 quants, s32
