@@ -1,37 +1,37 @@
-// decode_fused.cuh - the decode MoE layer (n_tok <= 64) as one persistent kernel (sm_100a).
+// decode_fused.cuh - the decode MoE layer (n_tok <= 64) in three kernels (sm_100a).
 //
 // Replaces, for decode batches, the reference's MoE branch of HipSession::layer
 // (runtime/src/hip_exec.rs:786-843: router GEMV, logits download, host select_experts and
 // MoePlan, four uploads, per-expert q4_mm / geglu_split / q4_mm, moe_combine) and computes
 // what the CPU-experts Q8_0 path computes (runtime/src/exec.rs:493-517, 541-557, 572-640).
 //
-// One CTA per SM (cooperative launch, so all CTAs are resident), 512 threads. Decode is a
-// latency problem: every phase spreads its work over whole CTAs so that no single warp runs a
-// long serial instruction stream. Phases are separated by a grid-wide barrier (two words in
-// the workspace, bounded spins):
+// Three kernels, one CTA per SM each, 512 threads. Decode is a latency problem: every phase
+// spreads its work over whole CTAs so that no single warp runs a long serial instruction
+// stream, and the kernel boundaries replace grid-wide barriers where the next phase needs all of
+// the previous one's results (an SM also starts a kernel with its first 64 KB of code at hand,
+// so three compact kernels run faster than one long persistent one):
 //
-//  1. router: items of (expert, up to 4 tokens) spread over the CTAs; within an item warp g
-//     takes the g-th 256 columns, forming f64 dots (exact products of bf16/f32 operands) and
-//     the rigorous bound on the reference's sequential f32 chain (router_fast.cuh). Spare warps
-//     write the Q8_0 records of x.                                              -- barrier --
-//  2. selection: a group of 128 threads per token ranks the experts in two levels (within
-//     each warp, then among the warps' candidates), certifies that the fast logits' order is
-//     the reference's and forms the softmax / top-k / renormalised weights with the reference's
-//     arithmetic on those logits rounded to f32. Tokens that cannot be certified get the exact
-//     sequential chains (one per CTA, all CTAs in parallel, rows staged by bulk copies) and an
-//     exact selection on them, behind one more barrier. With up to 4 tokens every CTA selects
-//     all tokens itself; beyond that CTA t selects token t and a barrier publishes the result.
-//  3. plan: every CTA builds the stable (expert, pair) plan of MoePlan::new in shared memory.
-//  4. gate/up: the (expert, 32-column) units of all active experts are split evenly over the
-//     CTAs. Weight rows stream through a ring of shared-memory slots filled by 1-D TMA bulk
-//     copies (the gate and the up half of a unit in two slots, computed at the same time by
-//     the two halves of the CTA); token records are double-buffered beside it;
-//     h = gelu(gate)*up is quantised to Q8_0 records. As slots free up, the ring is refilled
-//     with this CTA's down-projection tiles, so those weights are in flight before the barrier
-//     that makes h complete.                                                    -- barrier --
-//  5. down + combine: each CTA owns a range of output rows for every pair, computes
-//     y = W_down[rows] . h for all pairs from its prefetched tiles and combines the pairs of
-//     each token in slot order.
+//  k_fd_route (cooperative launch, so all CTAs are resident)
+//   1. router: items of (expert, up to 4 tokens) spread over the CTAs; within an item warp g
+//      takes the g-th 256 columns, forming f64 dots (exact products of bf16/f32 operands) and
+//      the rigorous bound on the reference's sequential f32 chain (router_fast.cuh). Spare warps
+//      write the Q8_0 records of x.                                   -- grid barrier --
+//   2. selection: a group of 128 threads per token ranks the experts in two levels (within
+//      each warp, then among the warps' candidates), certifies that the fast logits' order is
+//      the reference's and forms the softmax / top-k / renormalised weights with the
+//      reference's arithmetic on those logits rounded to f32; CTA t selects token t.
+//  k_fd_gate
+//   3. tokens that could not be certified get the exact sequential chains and an exact
+//      selection (rare: a few percent of tokens); every CTA builds the stable (expert, pair)
+//      plan of MoePlan::new in shared memory.
+//   4. gate/up: the (expert, 32-column) units of all active experts are split evenly over the
+//      CTAs. Weight rows stream through a ring of shared-memory slots filled by 1-D TMA bulk
+//      copies; token records sit beside them; h = gelu(gate)*up is quantised to Q8_0 records.
+//      The CTAs also pull this call's down-projection tiles toward L2.
+//  k_fd_down
+//   5. down + combine: each CTA owns a range of output rows for every pair, computes
+//      y = W_down[rows] . h for all pairs from tiles streamed through its ring and combines the
+//      pairs of each token in slot order.
 //
 // Every expert dot product runs in the reference's scalar order (expert_kernel.rs:147-161):
 // int32 block sums, acc = acc + sumi * (dw * dx) with each operation rounded separately.
