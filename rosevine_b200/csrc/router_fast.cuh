@@ -235,6 +235,95 @@ __global__ void __launch_bounds__(128) k_router_chains(RouteArgs a, int tpc) {
     RVC_MARK(0, 3);
 }
 
+// ------------------------------------------------------------------ K0, batches
+// The same exact chains for batches of 32 tokens and more: a tile of C4_E experts x C4_T tokens
+// per CTA of 128 threads, each thread running 4 independent chains (2 experts x 2 tokens) so
+// that the FMA latency of one chain hides behind the other three; the tile's rows stream in
+// chunks of C4_CH columns through two shared-memory buffers (1-D TMA bulk copies, one per row
+// and chunk). Every chain is still the reference's sequential order over all columns.
+constexpr int C4_E = 16, C4_T = 32, C4_CH = 352, C4_THREADS = 128;
+
+template <typename T>
+__host__ __device__ constexpr int c4_row_bytes() {
+    return C4_CH * (int)sizeof(T) + 16;  // padded: rows of one column start in different banks
+}
+template <typename XT, typename WT>
+__host__ __device__ constexpr int c4_buf_bytes() {
+    return C4_E * c4_row_bytes<WT>() + C4_T * c4_row_bytes<XT>();
+}
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(C4_THREADS) k_router_chains4(RouteArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[2];
+    const int e0 = blockIdx.x * C4_E, t0 = blockIdx.y * C4_T;
+    const int nw = min(C4_E, a.n_experts - e0), nx = min(C4_T, a.n_tok - t0);
+    const int tid = threadIdx.x, n = a.n_embd, nch = n / C4_CH;
+    constexpr int wrb = c4_row_bytes<WT>(), xrb = c4_row_bytes<XT>(), bb = c4_buf_bytes<XT, WT>();
+    const WT *w = static_cast<const WT *>(a.w);
+    const XT *x = static_cast<const XT *>(a.x);
+    if (tid == 0) {
+        mbar_init(&full[0], nw + nx);  // one arrival per staged row
+        mbar_init(&full[1], nw + nx);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int c) {  // thread r < nw + nx: row r's chunk c (router rows, then x rows)
+        if (tid >= nw + nx) return;
+        uint8_t *base = smem + (c & 1) * bb;
+        const bool isw = tid < nw;
+        const int r = isw ? tid : tid - nw;
+        const uint32_t bytes = (uint32_t)C4_CH * (isw ? sizeof(WT) : sizeof(XT));
+        uint8_t *dst = isw ? base + r * wrb : base + C4_E * wrb + r * xrb;
+        const uint8_t *src = isw ? reinterpret_cast<const uint8_t *>(w + (size_t)(e0 + r) * n + (size_t)c * C4_CH)
+                                 : reinterpret_cast<const uint8_t *>(x + (size_t)(t0 + r) * n + (size_t)c * C4_CH);
+        mbar_arrive_expect_tx(&full[c & 1], bytes);
+        bulk_g2s(dst, src, bytes, &full[c & 1]);
+    };
+    issue(0);
+    if (nch > 1) issue(1);
+    const int ep = tid >> 4, tp = tid & 15;  // experts e0 + 2 ep (+1), tokens t0 + 2 tp (+1)
+    float s00 = -0.0f, s01 = -0.0f, s10 = -0.0f, s11 = -0.0f;
+    for (int c = 0; c < nch; ++c) {
+        const int b = c & 1;
+        const bool ok = fd_mbar_wait(&full[b], (uint32_t)(c >> 1) & 1u, a.status);
+        if (__syncthreads_or(!ok)) return;
+        const uint8_t *base = smem + b * bb;
+        const WT *w0 = reinterpret_cast<const WT *>(base + (2 * ep) * wrb), *w1 = reinterpret_cast<const WT *>(base + (2 * ep + 1) * wrb);
+        const XT *x0 = reinterpret_cast<const XT *>(base + C4_E * wrb + (2 * tp) * xrb);
+        const XT *x1 = reinterpret_cast<const XT *>(base + C4_E * wrb + (2 * tp + 1) * xrb);
+#pragma unroll 2
+        for (int k = 0; k < C4_CH; k += 8) {
+            float wa[8], wb[8], xa[8], xb[8];
+            lds8<WT>(w0 + k, wa);
+            lds8<WT>(w1 + k, wb);
+            lds8<XT>(x0 + k, xa);
+            lds8<XT>(x1 + k, xb);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                s00 = chain_step<XT, WT>(s00, wa[j], xa[j]);
+                s01 = chain_step<XT, WT>(s01, wa[j], xb[j]);
+                s10 = chain_step<XT, WT>(s10, wb[j], xa[j]);
+                s11 = chain_step<XT, WT>(s11, wb[j], xb[j]);
+            }
+        }
+        __syncthreads();  // every thread is done with buffer b
+        if (c + 2 < nch) issue(c + 2);
+    }
+    const float sv[2][2] = {{s00, s01}, {s10, s11}};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int el = 2 * ep + i, tl = 2 * tp + j;
+            if (el < nw && tl < nx) {
+                float v = sv[i][j];
+                if (a.bias) v = __fadd_rn(v, __ldg(a.bias + (size_t)(t0 + tl) * a.bias_stride + e0 + el));
+                a.lexact[(size_t)(t0 + tl) * a.n_experts + e0 + el] = v;
+            }
+        }
+}
+
 // Exact chain of one (token, expert) logit with the router row streamed from global memory
 // (L2) through a double-buffered register window of 64 elements, and x from shared memory.
 template <typename WT>

@@ -169,6 +169,14 @@ int chains_tpc(int n_tok) {
 // K0: exact-order router chains -> lexact; with done_cnt set, the last CTA also selects ids/wts.
 template <typename XT, typename WT>
 int launch_chains_t(RouteArgs a, cudaStream_t st) {
+    if (a.n_tok >= C4_T && a.n_embd % C4_CH == 0 && !a.done_cnt) {  // batches: 4 chains per thread
+        const size_t smem = 2 * (size_t)c4_buf_bytes<XT, WT>();
+        int rc = set_smem_attr(k_router_chains4<XT, WT>, 20 + 2 * ((int)sizeof(XT) / 4) + (int)sizeof(WT) / 4);
+        if (rc) return rc;
+        dim3 grid((a.n_experts + C4_E - 1) / C4_E, (a.n_tok + C4_T - 1) / C4_T);
+        k_router_chains4<XT, WT><<<grid, C4_THREADS, smem, st>>>(a);
+        return launched();
+    }
     const int tpc = chains_tpc<XT>(a.n_tok);
     const size_t smem = (size_t)C0_EPC * c0_row_bytes<WT>(a.n_embd) + (size_t)tpc * c0_row_bytes<XT>(a.n_embd);
     int rc = set_smem_attr(k_router_chains<XT, WT>, 2 + 2 * (int)sizeof(XT) / 2 + (int)sizeof(WT) / 4);
