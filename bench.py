@@ -285,7 +285,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
     else:
         from rosevine_b200.ep import EpMoeLayer, GpuBackend, local_experts
         gl, dl = local_experts(weights["gate_up"], weights["down"], rank, world)
-        be = GpuBackend(weights["w_router"], gl, dl, 128 // world, max_tok=n, max_rows=PREFILL_TOK, device=local_rank)
+        be = GpuBackend(weights["w_router"], gl, dl, 128 // world, max_tok=n, max_rows=PREFILL_TOK, world=world,
+                        device=local_rank)
         layer = EpMoeLayer(be, rank, world)
 
         def fwd():

@@ -120,36 +120,45 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
 
 /* Zero the workspace's status word (call once after allocating a workspace). */
 /* ---------------------------------------------------------------- expert parallelism
- * No reference counterpart: the reference runs every expert on one device. A rank routes its
- * own tokens (rvc_moe_router), quantises the rows it sends (rvc_quant_q8_rows), runs its
- * resident experts on the rows it receives (rvc_ep_experts) and sums the partial outputs
+ * No reference counterpart: the reference runs every expert on one device. Rank r of N holds
+ * experts [r n_local, (r + 1) n_local). A rank routes its own tokens (rvc_moe_router), quantises
+ * them once (rvc_quant_q8_rows), packs one row per (token, destination rank) (rvc_ep_pack), runs
+ * its resident experts on the rows it receives (rvc_ep_experts) and sums the partial outputs
  * returned for its tokens (rvc_ep_reduce); the exchanges between these calls are the caller's
- * (NCCL all-to-allv). */
+ * (NCCL all-to-allv of rvc_ep_row_bytes-byte rows, and of n_embd f32 partials back). */
 
 /* Bytes of one Q8_0 row record of this backend: per 32-element block 32 int8 quants, then all
  * blocks' f32 scales, then all blocks' int32 quant sums (n_embd / 32 * 40 bytes). */
 size_t rvc_q8_record_bytes(int n_embd);
 
+/* Bytes of one sent row: a record, then `used` int32 local expert ids (-1: the slot's expert is on
+ * another rank) and `used` f32 routing weights, in the token's slot order. */
+size_t rvc_ep_row_bytes(int n_embd, int used);
+
 /* Q8_0 records (quantised as the reference quantises activations) of x [n_rows][n_embd]. */
 int rvc_quant_q8_rows(const void *x, int x_dtype, int n_rows, int n_embd, void *records, void *stream);
 
-/* Workspace for rvc_ep_experts calls of up to max_pairs (row, expert) pairs. */
-size_t rvc_ep_workspace_bytes(int max_pairs, int n_embd, int ff, int n_experts);
+/* Rows to send, grouped by destination rank (rank order; rows within a group in arrival order):
+ * a token goes once to every rank holding one of its experts. counts [2 * world] int32: on
+ * return counts[r] = rows for rank r (counts[world ..] is scratch); send holds up to
+ * n_tok * world rows; owner_map [n_tok][world] = the row of (token, rank) in send, or -1. */
+int rvc_ep_pack(const int32_t *ids, const float *wts, const void *records, int n_tok, int used, int n_embd,
+                int n_local, int world, int32_t *counts, void *send, int32_t *owner_map, int *status, void *stream);
 
-/* The resident experts (w: this rank's n_experts, ids local) over n_rows received records.
- * Row r's pairs are row_start[r] .. row_start[r + 1] - 1 (at most 16, in the token's slot
- * order), with expert pair_expert[p] and routing weight pair_w[p]. partial[r] [n_embd] f32 =
- * slot-order sum over the row's pairs of (y * down_scale[e]) * w, y the expert output of the
- * reference's CPU-experts Q8_0 path; the block dots are exact and each pair's y is bit-identical
- * to that path's. */
-int rvc_ep_experts(const rvc_moe_weights *w, const void *records, int n_rows, const int32_t *row_start,
-                   const int32_t *pair_expert, const float *pair_w, int n_pairs, float *partial, void *workspace,
+/* Workspace for rvc_ep_experts calls of up to max_rows received rows. */
+size_t rvc_ep_workspace_bytes(int max_rows, int used, int n_embd, int ff, int n_experts);
+
+/* The resident experts (w: this rank's n_experts, ids local) over n_rows received rows.
+ * partial[r] [n_embd] f32 = slot-order sum over the row's occupied slots of (y * down_scale[e])
+ * * w, y the expert output of the reference's CPU-experts Q8_0 path (block dots exact, each
+ * (row, expert) y bit-identical to that path's). */
+int rvc_ep_experts(const rvc_moe_weights *w, const void *rows, int n_rows, int used, float *partial, void *workspace,
                    size_t workspace_bytes, void *stream);
 
-/* out[t] = partial[src_row[k0]] + partial[src_row[k0 + 1]] + ... (f32, in that order) over
- * k in src_start[t] .. src_start[t + 1] - 1; a token with no entry gets zeros. */
-int rvc_ep_reduce(const float *partial, const int32_t *src_start, const int32_t *src_row, int n_tok, int n_embd,
-                  float *out, void *stream);
+/* out[t] = the partials back[owner_map[t][r]] over the ranks r with owner_map[t][r] >= 0, added in
+ * rank order (f32); a token sent nowhere gets zeros. */
+int rvc_ep_reduce(const float *back, const int32_t *owner_map, int n_tok, int world, int n_embd, float *out,
+                  void *stream);
 
 int rvc_workspace_reset(void *workspace, void *stream);
 

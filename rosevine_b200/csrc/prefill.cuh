@@ -242,37 +242,35 @@ __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int 
 
 // ------------------------------------------------------------------ combine
 // out[t][r] = slot-order sum over j of (y[pos_of[p_j]][r] * down_scale[e_j]) * w_j (exec.rs:626-638)
-// over the pairs p_j of token (or received row) t: t used .. + used - 1, or with row_start
-// row_start[t] .. row_start[t + 1] - 1 (at most MAX_USED); one CTA per token, four rows per
-// thread and step.
+// over the occupied slots p_j = t used + j of token (or received row) t; one CTA per token, four
+// rows per thread and step.
 __global__ void __launch_bounds__(256) k_pf_combine(const float *__restrict__ y, const int32_t *__restrict__ pos_of,
                                                     const int32_t *__restrict__ ids, const float *__restrict__ wts,
                                                     const float *__restrict__ down_scale, int used, int n_embd,
-                                                    int n_tok, float *__restrict__ out,
-                                                    const int32_t *__restrict__ row_start, int *status) {
+                                                    int n_tok, float *__restrict__ out, int *status) {
     __shared__ const float4 *s_row[MAX_USED];
     __shared__ float s_ds[MAX_USED], s_w[MAX_USED];
+    __shared__ int s_n;
     const int t = blockIdx.x;
-    const int pb = row_start ? __ldg(row_start + t) : t * used;
-    if (row_start) {
-        used = __ldg(row_start + t + 1) - pb;
-        if (used < 0 || used > MAX_USED) {
-            if (threadIdx.x == 0) set_status(status, STATUS_BAD_INDEX);
-            used = 0;
+    if (threadIdx.x == 0) {  // the token's occupied slots, in slot order (-1: a slot whose expert is elsewhere)
+        int n = 0;
+        for (int j = 0; j < used; ++j) {
+            const int p = t * used + j, e = __ldg(ids + p);
+            if (e < 0) continue;
+            s_row[n] = reinterpret_cast<const float4 *>(y + (size_t)__ldg(pos_of + p) * n_embd);
+            s_ds[n] = down_scale ? __ldg(down_scale + e) : 1.0f;
+            s_w[n] = __ldg(wts + p);
+            ++n;
         }
-    }
-    if (threadIdx.x < used) {
-        const int p = pb + threadIdx.x;
-        s_row[threadIdx.x] = reinterpret_cast<const float4 *>(y + (size_t)__ldg(pos_of + p) * n_embd);
-        s_ds[threadIdx.x] = down_scale ? __ldg(down_scale + __ldg(ids + p)) : 1.0f;
-        s_w[threadIdx.x] = __ldg(wts + p);
+        s_n = n;
     }
     __syncthreads();
+    const int n = s_n;
     float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)t * n_embd);
     const bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int r = threadIdx.x; r < n_embd / 4; r += blockDim.x) {
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);  // a row with no pair (never from the router) reads 0
-        for (int j = 0; j < used; ++j) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);  // a token with no slot here reads 0
+        for (int j = 0; j < n; ++j) {
             const float4 v = __ldg(s_row[j] + r);
             const float ds = s_ds[j], w = s_w[j];
             const float4 c = make_float4(__fmul_rn(__fmul_rn(v.x, ds), w), __fmul_rn(__fmul_rn(v.y, ds), w),
@@ -308,23 +306,102 @@ __global__ void __launch_bounds__(256) k_quant_rows(const XT *__restrict__ x, in
     }
 }
 
-// Received records to plan positions: warp task (row r, block b) copies the block into the
-// records of the row's pairs row_start[r] .. row_start[r + 1] - 1, with its (scale, offset) pair.
-__global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ rec, int nb, int n_rows,
-                                                    const int32_t *__restrict__ row_start,
+constexpr int EP_MAX_RANKS = 32;  // ranks of an expert-parallel group (a token's ranks form a 32-bit mask)
+
+// Sent rows: a token's Q8_0 record followed by its slots at the destination rank, `used` int32
+// local expert ids (-1: the slot's expert is elsewhere) and `used` f32 routing weights.
+__host__ __device__ constexpr int ep_row_bytes(int nb, int used) { return q8rec_bytes(nb) + used * 8; }
+
+// Rows per destination rank: rank r holds experts [r n_local, (r + 1) n_local); a token goes once
+// to every rank holding one of its experts.
+__global__ void __launch_bounds__(256) k_ep_count(const int32_t *__restrict__ ids, int n_tok, int used, int n_local,
+                                                  int world, int32_t *__restrict__ counts, int *status) {
+    __shared__ int s_cnt[EP_MAX_RANKS];
+    for (int r = threadIdx.x; r < world; r += blockDim.x) s_cnt[r] = 0;
+    __syncthreads();
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n_tok) {
+        unsigned hit = 0;
+        for (int j = 0; j < used; ++j) {
+            const int e = __ldg(ids + (size_t)t * used + j), r = e / n_local;
+            if (e < 0 || r >= world) {
+                set_status(status, STATUS_BAD_INDEX);
+                continue;
+            }
+            hit |= 1u << r;
+        }
+        for (unsigned h = hit; h; h &= h - 1) atomicAdd(&s_cnt[__ffs(h) - 1], 1);
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < world; r += blockDim.x)
+        if (s_cnt[r]) atomicAdd(counts + r, s_cnt[r]);
+}
+
+// Packing: warp w takes token w; for each rank it goes to (ascending), lane 0 takes a row in the
+// rank's group (groups in rank order, rows within a group in arrival order), the warp copies the
+// record and writes the slot metadata, and owner_map[t][r] gets the row (-1 for the ranks it
+// does not go to).
+__global__ void __launch_bounds__(256) k_ep_pack(const int32_t *__restrict__ ids, const float *__restrict__ wts,
+                                                 const uint8_t *__restrict__ rec, int nb, int n_tok, int used,
+                                                 int n_local, int world, const int32_t *__restrict__ counts,
+                                                 int32_t *__restrict__ cursor, uint8_t *__restrict__ send,
+                                                 int32_t *__restrict__ owner_map) {
+    const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= n_tok) return;
+    const int xrb = q8rec_bytes(nb), rb = ep_row_bytes(nb, used);
+    const int e = lane < used ? __ldg(ids + (size_t)t * used + lane) : -1;
+    const float wv = lane < used ? __ldg(wts + (size_t)t * used + lane) : 0.0f;
+    const int my_r = e >= 0 ? e / n_local : -1;
+    int base = 0;
+    for (int r = 0; r < world; ++r) {
+        const unsigned m = __ballot_sync(0xffffffffu, my_r == r);
+        int row = -1;
+        if (m) {
+            if (lane == 0) row = base + atomicAdd(cursor + r, 1);
+            row = __shfl_sync(0xffffffffu, row, 0);
+            uint8_t *dst = send + (size_t)row * rb;
+            const uint4 *src = reinterpret_cast<const uint4 *>(rec + (size_t)t * xrb);
+            for (int i = lane; i < xrb / 16; i += 32) reinterpret_cast<uint4 *>(dst)[i] = __ldg(src + i);
+            if (lane < used) {
+                reinterpret_cast<int32_t *>(dst + xrb)[lane] = my_r == r ? e - r * n_local : -1;
+                reinterpret_cast<float *>(dst + xrb + used * 4)[lane] = my_r == r ? wv : 0.0f;
+            }
+        }
+        if (lane == 0) owner_map[(size_t)t * world + r] = row;
+        base += __ldg(counts + r);
+    }
+}
+
+// The slot metadata of received rows into contiguous per-(row, slot) arrays for the plan.
+__global__ void __launch_bounds__(256) k_ep_meta(const uint8_t *__restrict__ rows, int nb, int n_rows, int used,
+                                                 int32_t *__restrict__ slot_e, float *__restrict__ slot_w) {
+    const int xrb = q8rec_bytes(nb), rb = ep_row_bytes(nb, used);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows * used; i += gridDim.x * blockDim.x) {
+        const int r = i / used, j = i - r * used;
+        const uint8_t *m = rows + (size_t)r * rb + xrb;
+        slot_e[i] = reinterpret_cast<const int32_t *>(m)[j];
+        slot_w[i] = reinterpret_cast<const float *>(m + used * 4)[j];
+    }
+}
+
+// Received rows to plan positions: warp task (row r, block b) copies the block into the records
+// of the row's occupied slots' plan positions, with its (scale, offset) pair.
+__global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ rows, int nb, int n_rows, int used,
+                                                    const int32_t *__restrict__ slot_e,
                                                     const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
                                                     float2 *__restrict__ xso, int ppad) {
-    const int xrb = q8rec_bytes(nb);
+    const int xrb = q8rec_bytes(nb), rb = ep_row_bytes(nb, used);
     const int lane = threadIdx.x & 31;
     const long long total = (long long)n_rows * nb;
     for (long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += (long long)gridDim.x * 8) {
         const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
-        const uint8_t *src = rec + (size_t)r * xrb;
+        const uint8_t *src = rows + (size_t)r * rb;
         const uint8_t q = src[b * 32 + lane];
         const float d = reinterpret_cast<const float *>(src + nb * 32)[b];
         const int qs = reinterpret_cast<const int *>(src + nb * 36)[b];
-        const int p1 = __ldg(row_start + r + 1);
-        for (int p = __ldg(row_start + r); p < p1; ++p) {
+        for (int j = 0; j < used; ++j) {
+            const int p = r * used + j;
+            if (__ldg(slot_e + p) < 0) continue;
             const int k = __ldg(pos_of + p);
             uint8_t *dst = xperm + (size_t)k * xrb;
             dst[b * 32 + lane] = q;
@@ -337,20 +414,24 @@ __global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ 
     }
 }
 
-// Owner-side sum of the partials returned for its tokens: out[t] = partial[src_row[k0]] +
-// partial[src_row[k0 + 1]] + ... over k in src_start[t] .. src_start[t + 1] - 1 (rank order).
-__global__ void __launch_bounds__(256) k_ep_reduce(const float *__restrict__ partial, const int32_t *__restrict__ src_start,
-                                                   const int32_t *__restrict__ src_row, int n_embd,
-                                                   float *__restrict__ out) {
+// Owner-side sum of the partials returned for its tokens: out[t] = the partials
+// back[owner_map[t][r]] over the ranks r it was sent to, added in rank order.
+__global__ void __launch_bounds__(256) k_ep_reduce(const float *__restrict__ back, const int32_t *__restrict__ owner_map,
+                                                   int world, int n_embd, float *__restrict__ out) {
+    __shared__ int s_row[EP_MAX_RANKS];
     const int t = blockIdx.x;
-    const int k0 = __ldg(src_start + t), k1 = __ldg(src_start + t + 1);
-    for (int r = threadIdx.x; r < n_embd / 4; r += blockDim.x) {
+    if (threadIdx.x < world) s_row[threadIdx.x] = __ldg(owner_map + (size_t)t * world + threadIdx.x);
+    __syncthreads();
+    for (int r4 = threadIdx.x; r4 < n_embd / 4; r4 += blockDim.x) {
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = k0; k < k1; ++k) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(partial + (size_t)__ldg(src_row + k) * n_embd) + r);
-            o = k == k0 ? v : make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
+        bool first = true;
+        for (int r = 0; r < world; ++r) {
+            if (s_row[r] < 0) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(back + (size_t)s_row[r] * n_embd) + r4);
+            o = first ? v : make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
+            first = false;
         }
-        reinterpret_cast<float4 *>(out + (size_t)t * n_embd)[r] = o;
+        reinterpret_cast<float4 *>(out + (size_t)t * n_embd)[r4] = o;
     }
 }
 

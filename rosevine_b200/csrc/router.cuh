@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
                                                        int32_t *__restrict__ active, int32_t *__restrict__ n_active,
                                                        int *status, int align = 1, int2 *__restrict__ tiles = nullptr,
                                                        int32_t *__restrict__ n_tiles = nullptr, int tile_rows = 128,
-                                                       bool stable = true) {
+                                                       bool stable = true, bool skip_neg = false) {
     __shared__ int s_count[MAX_EXPERTS];
     __shared__ int s_base[MAX_EXPERTS];
     __shared__ int s_warp[32][MAX_EXPERTS];  // per-warp counts within a chunk
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_plan(const int32_t *__restrict
     for (int p = tid; p < n_pairs; p += PLAN_THREADS) {
         int e = ids[p];
         if (e < 0 || e >= n_experts) {
-            set_status(status, STATUS_BAD_INDEX);
+            if (!(skip_neg && e == -1)) set_status(status, STATUS_BAD_INDEX);  // -1: an empty slot
             continue;
         }
         atomicAdd(&s_count[e], 1);

@@ -490,13 +490,14 @@ int pf_supported(const rvc_moe_weights *w) {
     return tensor_map_encode();
 }
 
-// Plan of n_pairs (pair -> expert ids) into expert groups starting at multiples of 4
-// positions, with the tile list; positions within a group in arrival order.
-int pf_plan(const int32_t *pair_expert, int n_pairs, int ne, const Workspace &L, void *ws, cudaStream_t st) {
+// Plan of n_pairs (pair -> expert ids; -1 skipped when skip_empty) into expert groups starting
+// at multiples of 4 positions, with the tile list; positions within a group in arrival order.
+int pf_plan(const int32_t *pair_expert, int n_pairs, int ne, const Workspace &L, void *ws, cudaStream_t st,
+            bool skip_empty = false) {
     k_plan<<<1, PLAN_THREADS, 0, st>>>(pair_expert, n_pairs, ne, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                                        at<int32_t>(ws, L.order), at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
                                        at<int32_t>(ws, L.n_active), at<int>(ws, L.status), 4, at<int2>(ws, L.tiles),
-                                       at<int32_t>(ws, L.n_tiles), PF_N, false);
+                                       at<int32_t>(ws, L.n_tiles), PF_N, false, skip_empty);
     return launched();
 }
 
@@ -532,12 +533,12 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     if ((rc = pf_gemms(w, L, ws, pairs, st))) return rc;
     // 4. slot-order combine
     k_pf_combine<<<n_tok, 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used, w->n_embd, n_tok,
-                                        out, nullptr, at<int>(ws, L.status));
+                                        out, at<int>(ws, L.status));
     return launched();
 }
 
-// Workspace of an expert-parallel call of up to max_pairs pairs: the prefill layout for
-// ceil(max_pairs / 8) tokens of 8 pairs (at least the prefill path's 65).
+// Workspace of an expert-parallel call of up to max_pairs (row, slot) pairs: the prefill layout
+// for ceil(max_pairs / 8) tokens of 8 pairs (at least the prefill path's 65).
 int ep_tokens(int max_pairs) { return std::max(FD_MAX_TOK + 1, (max_pairs + 7) / 8); }
 
 // The decode layer for n_tok <= 64 tokens: routing from x_router (or the caller's ids/wts),
@@ -747,6 +748,10 @@ int rvc_workspace_reset(void *workspace, void *stream) {
 // ------------------------------------------------------------------ expert parallelism
 size_t rvc_q8_record_bytes(int n_embd) { return n_embd > 0 && n_embd % QK == 0 ? (size_t)q8rec_bytes(n_embd / QK) : 0; }
 
+size_t rvc_ep_row_bytes(int n_embd, int used) {
+    return n_embd > 0 && n_embd % QK == 0 && used > 0 && used <= MAX_USED ? (size_t)ep_row_bytes(n_embd / QK, used) : 0;
+}
+
 int rvc_quant_q8_rows(const void *x, int x_dtype, int n_rows, int n_embd, void *records, void *stream) {
     if (!x || !records || n_rows < 0 || n_embd <= 0 || n_embd % QK || !aligned(x, 4) ||
         (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
@@ -761,47 +766,66 @@ int rvc_quant_q8_rows(const void *x, int x_dtype, int n_rows, int n_embd, void *
     return launched();
 }
 
-size_t rvc_ep_workspace_bytes(int max_pairs, int n_embd, int ff, int n_experts) {
-    if (max_pairs <= 0 || n_embd <= 0 || n_embd % QK || ff <= 0 || ff % QK || n_experts <= 0) return 0;
-    return Workspace(ep_tokens(max_pairs), n_embd, ff, n_experts, 8).total;
+int rvc_ep_pack(const int32_t *ids, const float *wts, const void *records, int n_tok, int used, int n_embd,
+                int n_local, int world, int32_t *counts, void *send, int32_t *owner_map, int *status, void *stream) {
+    if (n_tok < 0 || used <= 0 || used > MAX_USED || n_embd <= 0 || n_embd % QK || n_local <= 0 || world <= 0 ||
+        world > EP_MAX_RANKS || !counts || !status || (n_tok > 0 && (!ids || !wts || !records || !send || !owner_map)) ||
+        (records && !aligned(records, 16)) || (send && !aligned(send, 16)))
+        return (int)cudaErrorInvalidValue;
+    cudaStream_t st = S(stream);
+    cudaError_t e = cudaMemsetAsync(counts, 0, 2 * (size_t)world * sizeof(int32_t), st);  // counts, cursors
+    if (e != cudaSuccess) return (int)e;
+    if (n_tok == 0) return 0;
+    k_ep_count<<<(n_tok + 255) / 256, 256, 0, st>>>(ids, n_tok, used, n_local, world, counts, status);
+    int rc = launched();
+    if (rc) return rc;
+    k_ep_pack<<<(n_tok + 7) / 8, 256, 0, st>>>(ids, wts, (const uint8_t *)records, n_embd / QK, n_tok, used, n_local,
+                                               world, counts, counts + world, (uint8_t *)send, owner_map);
+    return launched();
 }
 
-int rvc_ep_experts(const rvc_moe_weights *w, const void *records, int n_rows, const int32_t *row_start,
-                   const int32_t *pair_expert, const float *pair_w, int n_pairs, float *partial, void *workspace,
+size_t rvc_ep_workspace_bytes(int max_rows, int used, int n_embd, int ff, int n_experts) {
+    if (max_rows <= 0 || used <= 0 || used > MAX_USED || n_embd <= 0 || n_embd % QK || ff <= 0 || ff % QK ||
+        n_experts <= 0)
+        return 0;
+    return Workspace(ep_tokens(max_rows * used), n_embd, ff, n_experts, 8).total;
+}
+
+int rvc_ep_experts(const rvc_moe_weights *w, const void *rows, int n_rows, int used, float *partial, void *workspace,
                    size_t workspace_bytes, void *stream) {
-    if (!dims_ok(w) || n_rows < 0 || n_pairs < 0 || !workspace || !aligned(workspace, 256) ||
-        (n_rows > 0 && (!records || !row_start || !partial || !aligned(records, 16) || !aligned(partial, 16))) ||
-        (n_pairs > 0 && (!pair_expert || !pair_w)))
+    if (!dims_ok(w) || n_rows < 0 || used <= 0 || used > MAX_USED || !workspace || !aligned(workspace, 256) ||
+        (n_rows > 0 && (!rows || !partial || !aligned(rows, 16) || !aligned(partial, 16))))
         return (int)cudaErrorInvalidValue;
     int rc;
     if ((rc = pf_supported(w))) return rc;
     if (n_rows == 0) return 0;
-    const int nt = ep_tokens(n_pairs);
-    Workspace L(nt, w->n_embd, w->ff, w->n_experts, 8);
+    const int n_pairs = n_rows * used;
+    Workspace L(ep_tokens(n_pairs), w->n_embd, w->ff, w->n_experts, 8);
     if (L.total > workspace_bytes) return RVC_ERR_WORKSPACE;
     cudaStream_t st = S(stream);
     const int nb = w->n_embd / QK;
-    if (n_pairs > 0) {
-        if ((rc = pf_plan(pair_expert, n_pairs, w->n_experts, L, workspace, st))) return rc;
-        const long long tasks = (long long)n_rows * nb;
-        k_ep_scatter<<<(int)std::min<long long>(16 * num_sms(), (tasks + 7) / 8), 256, 0, st>>>(
-            (const uint8_t *)records, nb, n_rows, row_start, at<int32_t>(workspace, L.pos_of),
-            at<uint8_t>(workspace, L.xperm), at<float2>(workspace, L.xd), (int)L.ppad);
-        if ((rc = launched()) || (rc = pf_gemms(w, L, workspace, n_pairs, st))) return rc;
-    }
-    k_pf_combine<<<n_rows, 256, 0, st>>>(at<float>(workspace, L.ybuf), at<int32_t>(workspace, L.pos_of), pair_expert,
-                                         pair_w, w->down_scale, 0, w->n_embd, n_rows, partial, row_start,
-                                         at<int>(workspace, L.status));
+    int32_t *slot_e = at<int32_t>(workspace, L.ids);
+    float *slot_w = at<float>(workspace, L.wts);
+    k_ep_meta<<<std::min(4 * num_sms(), (n_pairs + 255) / 256), 256, 0, st>>>((const uint8_t *)rows, nb, n_rows, used,
+                                                                              slot_e, slot_w);
+    if ((rc = launched()) || (rc = pf_plan(slot_e, n_pairs, w->n_experts, L, workspace, st, true))) return rc;
+    const long long tasks = (long long)n_rows * nb;
+    k_ep_scatter<<<(int)std::min<long long>(16 * num_sms(), (tasks + 7) / 8), 256, 0, st>>>(
+        (const uint8_t *)rows, nb, n_rows, used, slot_e, at<int32_t>(workspace, L.pos_of), at<uint8_t>(workspace, L.xperm),
+        at<float2>(workspace, L.xd), (int)L.ppad);
+    if ((rc = launched()) || (rc = pf_gemms(w, L, workspace, n_pairs, st))) return rc;
+    k_pf_combine<<<n_rows, 256, 0, st>>>(at<float>(workspace, L.ybuf), at<int32_t>(workspace, L.pos_of), slot_e, slot_w,
+                                         w->down_scale, used, w->n_embd, n_rows, partial, at<int>(workspace, L.status));
     return launched();
 }
 
-int rvc_ep_reduce(const float *partial, const int32_t *src_start, const int32_t *src_row, int n_tok, int n_embd,
-                  float *out, void *stream) {
-    if (n_tok < 0 || n_embd <= 0 || n_embd % 4 || (n_tok > 0 && (!src_start || !out || !aligned(out, 16))) ||
-        (partial && !aligned(partial, 16)))
+int rvc_ep_reduce(const float *back, const int32_t *owner_map, int n_tok, int world, int n_embd, float *out,
+                  void *stream) {
+    if (n_tok < 0 || world <= 0 || world > EP_MAX_RANKS || n_embd <= 0 || n_embd % 4 ||
+        (n_tok > 0 && (!owner_map || !out || !aligned(out, 16))) || (back && !aligned(back, 16)))
         return (int)cudaErrorInvalidValue;
     if (n_tok == 0) return 0;
-    k_ep_reduce<<<n_tok, 256, 0, S(stream)>>>(partial, src_start, src_row, n_embd, out);
+    k_ep_reduce<<<n_tok, 256, 0, S(stream)>>>(back, owner_map, world, n_embd, out);
     return launched();
 }
 

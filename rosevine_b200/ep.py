@@ -5,10 +5,10 @@ the multi-GPU form of the same layer. Rank r of N holds experts [r E/N, (r + 1) 
 with its own shard of the tokens. One forward:
 
   1. route     the rank's tokens with the full router (reference order: rvc_moe_router),
-  2. plan      per destination rank the tokens that selected at least one of its experts (each
-               token sent once per rank) and, per sent row, its slots there in slot order,
-  3. dispatch  row counts (all-to-all), Q8_0 records quantised once by the sender
-               (rvc_quant_q8_rows) and the slot metadata (all-to-allv over NCCL),
+  2. pack      the Q8_0 records, quantised once (rvc_quant_q8_rows), into one row per (token,
+               destination rank holding one of its experts), each row carrying the token's
+               slots there in slot order (rvc_ep_pack),
+  3. dispatch  row counts (all-to-all), then the rows (one all-to-allv over NCCL),
   4. experts   the resident experts over the received rows (rvc_ep_experts): one partial sum
                per row, over its slots in slot order,
   5. combine   partials back to their owners (all-to-allv), summed per token in rank order
@@ -49,11 +49,11 @@ class GpuBackend:
     """The CUDA library on this rank's device: full router, resident experts."""
 
     def __init__(self, w_router: np.ndarray, gate_up_local: np.ndarray, down_local: np.ndarray, n_local: int,
-                 max_tok: int, max_rows: int, down_scale_local=None, device: int | None = None,
+                 max_tok: int, max_rows: int, world: int, down_scale_local=None, device: int | None = None,
                  n_embd: int = synth.N_EMBD, ff: int = synth.FF, used: int = synth.USED):
         rc.lib()  # fail loudly before touching the GPU if the extension is missing
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
-        self.device, self.n_embd, self.ff, self.used = dev, n_embd, ff, used
+        self.device, self.n_embd, self.ff, self.used, self.world = dev, n_embd, ff, used, world
         self.n_experts = w_router.shape[0]
         self.router_dtype = rc.BF16 if w_router.dtype == np.uint16 else rc.F32
         self.router_w = torch.from_numpy(np.ascontiguousarray(w_router).view(np.uint8)).to(dev)
@@ -73,14 +73,20 @@ class GpuBackend:
                                      self.packed.data_ptr(), None)
         self.w_local = rc.weights_struct(n_embd, ff, n_local, min(used, n_local), self.router_dtype, self.router_w,
                                          self.packed, self.down_scale)
+        self.n_local, self.max_tok, self.max_rows = n_local, max_tok, max_rows
         self.ws_route = torch.empty(rc.workspace_bytes(max_tok, n_embd, ff, self.n_experts, used), dtype=torch.uint8,
                                     device=dev)
         rc.workspace_reset(self.ws_route, _stream_handle(None))
-        self.max_pairs = max_rows * used
-        self.ws_ep = torch.empty(rc.ep_workspace_bytes(self.max_pairs, n_embd, ff, n_local), dtype=torch.uint8,
+        self.ws_ep = torch.empty(rc.ep_workspace_bytes(max_rows, used, n_embd, ff, n_local), dtype=torch.uint8,
                                  device=dev)
         rc.workspace_reset(self.ws_ep, _stream_handle(None))
-        self.record_bytes = rc.q8_record_bytes(n_embd)
+        self.row_bytes = rc.ep_row_bytes(n_embd, used)
+        # per-forward buffers, allocated once
+        self.rec = torch.empty((max_tok, rc.q8_record_bytes(n_embd)), dtype=torch.uint8, device=dev)
+        self.send = torch.empty((max_tok * world, self.row_bytes), dtype=torch.uint8, device=dev)
+        self.counts = torch.empty(2 * world, dtype=torch.int32, device=dev)
+        self.owner = torch.empty((max_tok, world), dtype=torch.int32, device=dev)
+        self.status_ws = self.ws_ep  # the pack kernel reports bad ids in the EP workspace's status word
 
     def route(self, x: torch.Tensor, bias: torch.Tensor | None = None):
         """ids, wts [n, used]; bias: per-expert logit offsets [n_experts] or [n, n_experts]."""
@@ -92,23 +98,30 @@ class GpuBackend:
                       stream=_stream_handle(None))
         return ids, wts
 
-    def quant(self, x: torch.Tensor) -> torch.Tensor:
-        rec = torch.empty((x.shape[0], self.record_bytes), dtype=torch.uint8, device=self.device)
-        rc.quant_q8_rows(x, _xdtype(x), x.shape[0], self.n_embd, rec, _stream_handle(None))
-        return rec
+    def pack(self, x: torch.Tensor, ids, wts):
+        """Rows to send grouped by destination rank, their counts (host list) and the owner map."""
+        n = x.shape[0]
+        if n > self.max_tok:
+            raise ValueError(f"{n} tokens exceed the layer's {self.max_tok}")
+        sh = _stream_handle(None)
+        rc.quant_q8_rows(x, _xdtype(x), n, self.n_embd, self.rec, sh)
+        rc.ep_pack(ids, wts, self.rec, n, self.used, self.n_embd, self.n_local, self.world, self.counts, self.send,
+                   self.owner, self.status_ws, sh)
+        counts = self.counts[:self.world].tolist()
+        return self.send[:sum(counts)], counts, self.owner[:n]
 
-    def experts(self, rec, row_start, pair_expert, pair_w) -> torch.Tensor:
-        n_rows, n_pairs = rec.shape[0], pair_expert.shape[0]
-        if n_pairs > self.max_pairs:
-            raise ValueError(f"{n_pairs} pairs exceed the workspace's {self.max_pairs}")
+    def experts(self, rows) -> torch.Tensor:
+        n_rows = rows.shape[0]
+        if n_rows > self.max_rows:
+            raise ValueError(f"{n_rows} rows exceed the workspace's {self.max_rows}")
         partial = torch.empty((n_rows, self.n_embd), dtype=torch.float32, device=self.device)
-        rc.ep_experts(self.w_local, rec, n_rows, row_start, pair_expert, pair_w, n_pairs, partial, self.ws_ep,
-                      _stream_handle(None))
+        rc.ep_experts(self.w_local, rows, n_rows, self.used, partial, self.ws_ep, _stream_handle(None))
         return partial
 
-    def reduce(self, partial, src_start, src_row, n_tok: int) -> torch.Tensor:
+    def reduce(self, back, owner_map, n_tok: int) -> torch.Tensor:
         out = torch.empty((n_tok, self.n_embd), dtype=torch.float32, device=self.device)
-        rc.ep_reduce(partial, partial.shape[0], src_start, src_row, n_tok, self.n_embd, out, _stream_handle(None))
+        rc.ep_reduce(back if back.shape[0] else None, back.shape[0], owner_map, n_tok, self.world, self.n_embd, out,
+                     _stream_handle(None))
         return out
 
     def status(self) -> None:
@@ -148,8 +161,19 @@ def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, n_local: int
     return _Plan(t_idx, counts.tolist(), meta_e.to(torch.int32).contiguous(), meta_w.contiguous())
 
 
-def _csr(counts: torch.Tensor) -> torch.Tensor:
-    return torch.cat([torch.zeros(1, dtype=torch.int64, device=counts.device), torch.cumsum(counts, 0)]).to(torch.int32)
+def pack_host(rec: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, world: int, n_local: int):
+    """rvc_ep_pack's rows with torch operations (any device): per sent row the record bytes, then
+    the slot metadata (int32 local expert ids, -1 when elsewhere; f32 weights). Returns the rows
+    grouped by destination rank, the counts per rank and the owner map [n, world] (row or -1);
+    used by backends without the CUDA library (the CPU tests)."""
+    p = plan_dispatch(ids, wts, world, n_local)
+    meta = torch.cat([p.meta_e.view(torch.uint8).reshape(p.meta_e.shape[0], -1),
+                      p.meta_w.view(torch.uint8).reshape(p.meta_w.shape[0], -1)], dim=1)
+    rows = torch.cat([rec.index_select(0, p.send_tok), meta], dim=1)
+    owner = torch.full((ids.shape[0], world), -1, dtype=torch.int32, device=ids.device)
+    r_idx = torch.repeat_interleave(torch.arange(world, device=ids.device), torch.tensor(p.send_counts, device=ids.device))
+    owner[p.send_tok, r_idx] = torch.arange(p.send_tok.shape[0], dtype=torch.int32, device=ids.device)
+    return rows, p.send_counts, owner
 
 
 class EpMoeLayer:
@@ -169,7 +193,7 @@ class EpMoeLayer:
     def forward(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's tokens x [n, n_embd] (bf16 or f32) -> their layer output [n, n_embd] f32.
         bias: router logit offsets, [n_experts] or [n, n_experts] (the skewed-load configs)."""
-        be, world = self.be, self.world
+        be = self.be
         dev = x.device
         marks = []
 
@@ -183,43 +207,24 @@ class EpMoeLayer:
         ids, wts = be.route(x, bias)
         self.last_ids = ids
         mark("route")
-        rec = be.quant(x)
-        mark("quantise")
-        p = plan_dispatch(ids, wts, world, self.n_local)
-        # 3. dispatch: counts, then records and slot metadata
-        send_counts = torch.tensor(p.send_counts, dtype=torch.int64, device=dev)
-        recv_counts = torch.empty_like(send_counts)
-        send_rec = rec.index_select(0, p.send_tok)
-        mark("plan")
-        self._a2a(recv_counts, send_counts, None, None)
-        rc_list = recv_counts.tolist()
-        n_recv = int(sum(rc_list))
-        recv_rec = torch.empty((n_recv, rec.shape[1]), dtype=rec.dtype, device=dev)
-        recv_e = torch.empty((n_recv, p.meta_e.shape[1]), dtype=torch.int32, device=dev)
-        recv_w = torch.empty((n_recv, p.meta_w.shape[1]), dtype=torch.float32, device=dev)
-        self._a2a(recv_rec, send_rec, rc_list, p.send_counts)
-        self._a2a(recv_e, p.meta_e, rc_list, p.send_counts)
-        self._a2a(recv_w, p.meta_w, rc_list, p.send_counts)
+        send, send_counts, owner_map = be.pack(x, ids, wts)
+        mark("pack")
+        # dispatch: row counts, then the rows (records with their slot metadata)
+        sc = torch.tensor(send_counts, dtype=torch.int64, device=dev)
+        rcnt = torch.empty_like(sc)
+        self._a2a(rcnt, sc, None, None)
+        recv_counts = rcnt.tolist()
+        recv = torch.empty((int(sum(recv_counts)), send.shape[1]), dtype=send.dtype, device=dev)
+        self._a2a(recv, send, recv_counts, send_counts)
         mark("dispatch")
-        # 4. resident experts: each row's slots in slot order
-        valid = recv_e >= 0
-        row_start = _csr(valid.sum(1))
-        pair_expert = recv_e[valid].contiguous()
-        pair_w = recv_w[valid].contiguous()
-        mark("pairs")
-        partial = be.experts(recv_rec, row_start, pair_expert, pair_w)
-        back = torch.empty((p.send_tok.shape[0], partial.shape[1]), dtype=partial.dtype, device=dev)
+        partial = be.experts(recv)
+        back = torch.empty((send.shape[0], partial.shape[1]), dtype=partial.dtype, device=dev)
         mark("experts")
-        # 5. combine: partials back to their owners, summed per token in rank order
-        self._a2a(back, partial, p.send_counts, rc_list)
+        self._a2a(back, partial, send_counts, recv_counts)  # partials back to their owners
         mark("combine")
-        # rows of `back` are grouped by rank (ascending) and by token within a rank; a stable sort
-        # by token lists each token's ranks in ascending order
-        src_row = torch.sort(p.send_tok, stable=True).indices.to(torch.int32)
-        src_start = _csr(torch.bincount(p.send_tok, minlength=x.shape[0]))
-        out = be.reduce(back, src_start, src_row, x.shape[0])
+        out = be.reduce(back, owner_map, x.shape[0])
         mark("reduce")
-        st = EpStats(rows_sent=int(p.send_tok.shape[0]), rows_received=n_recv)
+        st = EpStats(rows_sent=int(send.shape[0]), rows_received=int(recv.shape[0]))
         if marks:
             torch.cuda.synchronize(dev)
             st.phases_ms = {n1: e0.elapsed_time(e1) for (_, e0), (n1, e1) in zip(marks, marks[1:])}

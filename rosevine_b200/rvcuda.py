@@ -31,8 +31,8 @@ EXPORTS = [
     "rvc_event_elapsed", "rvc_upload_async", "rvc_download_async", "rvc_event_record_on", "rvc_stream_sync",
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
-    "rvc_debug_mma_i8", "rvc_q8_record_bytes", "rvc_quant_q8_rows", "rvc_ep_workspace_bytes", "rvc_ep_experts",
-    "rvc_ep_reduce",
+    "rvc_debug_mma_i8", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
+    "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce",
 ]
 
 
@@ -99,10 +99,12 @@ def lib() -> ctypes.CDLL:
             "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
             "rvc_debug_mma_i8": ([P, P, I, P, P, P], I),
             "rvc_q8_record_bytes": ([I], Z),
+            "rvc_ep_row_bytes": ([I, I], Z),
             "rvc_quant_q8_rows": ([P, I, I, I, P, P], I),
-            "rvc_ep_workspace_bytes": ([I, I, I, I], Z),
-            "rvc_ep_experts": ([W, P, I, P, P, P, I, P, P, Z, P], I),
-            "rvc_ep_reduce": ([P, P, P, I, I, P, P], I),
+            "rvc_ep_pack": ([P, P, P, I, I, I, I, I, P, P, P, P, P], I),
+            "rvc_ep_workspace_bytes": ([I, I, I, I, I], Z),
+            "rvc_ep_experts": ([W, P, I, I, P, P, Z, P], I),
+            "rvc_ep_reduce": ([P, P, I, I, I, P, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -308,8 +310,12 @@ def q8_record_bytes(n_embd: int) -> int:
     return lib().rvc_q8_record_bytes(n_embd)
 
 
-def ep_workspace_bytes(max_pairs: int, n_embd: int, ff: int, n_experts: int) -> int:
-    return lib().rvc_ep_workspace_bytes(max_pairs, n_embd, ff, n_experts)
+def ep_row_bytes(n_embd: int, used: int) -> int:
+    return lib().rvc_ep_row_bytes(n_embd, used)
+
+
+def ep_workspace_bytes(max_rows: int, used: int, n_embd: int, ff: int, n_experts: int) -> int:
+    return lib().rvc_ep_workspace_bytes(max_rows, used, n_embd, ff, n_experts)
 
 
 def quant_q8_rows(x, x_dtype: int, n_rows: int, n_embd: int, records, stream: int | None = None) -> None:
@@ -317,16 +323,22 @@ def quant_q8_rows(x, x_dtype: int, n_rows: int, n_embd: int, records, stream: in
                                   _ptr(records, n_rows * q8_record_bytes(n_embd)), stream))
 
 
-def ep_experts(w: MoeWeights, records, n_rows: int, row_start, pair_expert, pair_w, n_pairs: int, partial,
-               workspace, stream: int | None = None) -> None:
+def ep_pack(ids, wts, records, n_tok: int, used: int, n_embd: int, n_local: int, world: int, counts, send,
+            owner_map, status, stream: int | None = None) -> None:
+    rb = ep_row_bytes(n_embd, used)
+    check(lib().rvc_ep_pack(_ptr(ids, n_tok * used * 4), _ptr(wts, n_tok * used * 4),
+                            _ptr(records, n_tok * q8_record_bytes(n_embd)), n_tok, used, n_embd, n_local, world,
+                            _ptr(counts, 2 * world * 4), _ptr(send, n_tok * world * rb),
+                            _ptr(owner_map, n_tok * world * 4), _ptr(status, 4), stream))
+
+
+def ep_experts(w: MoeWeights, rows, n_rows: int, used: int, partial, workspace, stream: int | None = None) -> None:
     ws = view_of(workspace)
-    check(lib().rvc_ep_experts(ctypes.byref(w), _ptr(records, n_rows * q8_record_bytes(w.n_embd)), n_rows,
-                               _ptr(row_start, (n_rows + 1) * 4), _ptr(pair_expert, n_pairs * 4),
-                               _ptr(pair_w, n_pairs * 4), n_pairs, _ptr(partial, n_rows * w.n_embd * 4), ws.ptr,
-                               ws.nbytes, stream))
+    check(lib().rvc_ep_experts(ctypes.byref(w), _ptr(rows, n_rows * ep_row_bytes(w.n_embd, used)), n_rows, used,
+                               _ptr(partial, n_rows * w.n_embd * 4), ws.ptr, ws.nbytes, stream))
 
 
-def ep_reduce(partial, n_partial: int, src_start, src_row, n_tok: int, n_embd: int, out,
+def ep_reduce(back, n_back: int, owner_map, n_tok: int, world: int, n_embd: int, out,
               stream: int | None = None) -> None:
-    check(lib().rvc_ep_reduce(_ptr(partial, n_partial * n_embd * 4), _ptr(src_start, (n_tok + 1) * 4),
-                              _ptr(src_row, n_partial * 4), n_tok, n_embd, _ptr(out, n_tok * n_embd * 4), stream))
+    check(lib().rvc_ep_reduce(_ptr(back, n_back * n_embd * 4), _ptr(owner_map, n_tok * world * 4), n_tok, world,
+                              n_embd, _ptr(out, n_tok * n_embd * 4), stream))

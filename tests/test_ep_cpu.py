@@ -18,18 +18,20 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from rosevine_b200 import synth
-from rosevine_b200.ep import EpMoeLayer, plan_dispatch
+from rosevine_b200.ep import EpMoeLayer, pack_host, plan_dispatch
 
 N_TOK = 24
 EP_RTOL = 1e-3
 
 
 class OracleBackend:
-    """Compute on the host through the oracle: rows travel as their raw bf16 bits."""
+    """Compute on the host through the oracle: a sent row is the token's raw bf16 bits followed by
+    its slot metadata (pack_host, the same row layout rvc_ep_pack writes after a Q8_0 record)."""
 
-    def __init__(self, oracle, pool, w_router, gate_up, down, rank, n_local):
+    def __init__(self, oracle, pool, w_router, gate_up, down, rank, world, n_local):
         self.O, self.pool, self.wr, self.gu, self.dn = oracle, pool, w_router, gate_up, down
-        self.base = rank * n_local
+        self.base, self.world, self.n_local = rank * n_local, world, n_local
+        self.xb = synth.N_EMBD * 2
 
     def route(self, x, bias=None):
         b = None if bias is None else bias.numpy()
@@ -38,29 +40,33 @@ class OracleBackend:
         ids, w, _ = self.O.select_experts(lg, synth.USED)
         return torch.from_numpy(ids), torch.from_numpy(w)
 
-    def quant(self, x):
-        return x.contiguous().view(torch.uint8).reshape(x.shape[0], -1).clone()
+    def pack(self, x, ids, wts):
+        rec = x.contiguous().view(torch.uint8).reshape(x.shape[0], -1)
+        return pack_host(rec, ids, wts, self.world, self.n_local)
 
-    def experts(self, rec, row_start, pair_expert, pair_w):
-        x = rec.numpy().view(np.uint16).reshape(rec.shape[0], -1)
-        rs = row_start.numpy()
+    def experts(self, rows):
+        used = synth.USED
+        r = rows.numpy()
+        x = np.ascontiguousarray(r[:, :self.xb]).view(np.uint16)
+        e = np.ascontiguousarray(r[:, self.xb:self.xb + 4 * used]).view(np.int32)
+        w = np.ascontiguousarray(r[:, self.xb + 4 * used:self.xb + 8 * used]).view(np.float32)
         out = np.zeros((x.shape[0], synth.N_EMBD), np.float32)
-        for r in range(x.shape[0]):
-            p0, p1 = rs[r], rs[r + 1]
-            if p1 > p0:
-                ids = (pair_expert[p0:p1].numpy() + self.base)[None, :]
-                out[r] = self.O.experts_q8(self.pool, x[r:r + 1], self.gu, self.dn, None, ids,
-                                           pair_w[p0:p1].numpy()[None, :])[0]
+        for i in range(x.shape[0]):
+            k = e[i] >= 0
+            if k.any():
+                out[i] = self.O.experts_q8(self.pool, x[i:i + 1], self.gu, self.dn, None,
+                                           (e[i][k] + self.base)[None, :], w[i][k][None, :])[0]
         return torch.from_numpy(out)
 
-    def reduce(self, partial, src_start, src_row, n_tok):
-        out = torch.zeros((n_tok, partial.shape[1]), dtype=torch.float32)
-        s, rows = src_start.numpy(), src_row.numpy()
+    def reduce(self, back, owner_map, n_tok):
+        out = torch.zeros((n_tok, back.shape[1] if back.dim() == 2 else synth.N_EMBD), dtype=torch.float32)
+        om = owner_map.numpy()
         for t in range(n_tok):
             acc = None
-            for k in range(s[t], s[t + 1]):
-                v = partial[rows[k]]
-                acc = v.clone() if acc is None else acc + v
+            for r in range(om.shape[1]):
+                if om[t, r] >= 0:
+                    v = back[om[t, r]]
+                    acc = v.clone() if acc is None else acc + v
             if acc is not None:
                 out[t] = acc
         return out
@@ -78,7 +84,7 @@ def _rank(rank, world, port, tmp, hot):
         x = synth.tokens(N_TOK, 5)
         n = N_TOK // world
         mine = torch.from_numpy(x[rank * n:(rank + 1) * n].view(np.int16))
-        be = OracleBackend(O, pool, wr, gu, dn, rank, synth.N_EXPERTS // world)
+        be = OracleBackend(O, pool, wr, gu, dn, rank, world, synth.N_EXPERTS // world)
         layer = EpMoeLayer(be, rank, world)
         bias = None
         if hot:  # 90% of the tokens pick experts 0..7, all on rank 0
@@ -133,3 +139,15 @@ def test_plan_dispatch_dedups_and_keeps_slot_order():
     assert p.meta_e[1].tolist() == [-1, -1, 2, 3]
     assert p.meta_e[4].tolist() == [0, 1, -1, -1]
     assert p.meta_w[0].tolist() == pytest.approx([0.4, 0.0, 0.2, 0.0])
+
+
+def test_pack_host_rows_and_owner_map():
+    ids = torch.tensor([[0, 5, 1, 9], [12, 13, 2, 3]], dtype=torch.int32)
+    wts = torch.tensor([[0.4, 0.3, 0.2, 0.1], [0.25, 0.25, 0.25, 0.25]])
+    rec = torch.arange(2 * 16, dtype=torch.uint8).reshape(2, 16)
+    rows, counts, owner = pack_host(rec, ids, wts, world=4, n_local=4)
+    assert counts == [2, 1, 1, 1]
+    assert rows.shape == (5, 16 + 4 * 8)
+    assert owner.tolist() == [[0, 2, 3, -1], [1, -1, -1, 4]]
+    assert torch.equal(rows[1, :16], rec[1])
+    assert rows[1, 16:32].view(torch.int32).tolist() == [-1, -1, 2, 3]

@@ -51,7 +51,7 @@ def _rank(rank, world, port, tmp, n_tok, hot):
         x = synth.tokens(n_tok, 9)
         n = n_tok // world
         gl, dl = local_experts(gu, dn, rank, world)
-        be = GpuBackend(wr, gl, dl, synth.N_EXPERTS // world, max_tok=n, max_rows=n_tok)
+        be = GpuBackend(wr, gl, dl, synth.N_EXPERTS // world, max_tok=n, max_rows=n_tok, world=world)
         layer = EpMoeLayer(be, rank, world)
         b = _bias(n_tok, hot)
         bias = None if b is None else torch.from_numpy(b[rank * n:(rank + 1) * n].copy()).cuda()
