@@ -280,7 +280,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
 
         def fwd():
             return layer.forward(x, out=out)
-        launches = 7  # k_router_chains, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_ms, k_pf_combine
+        launches = 7  # k_router_chains4, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_ms, k_pf_combine
         check = layer.status
     else:
         from rosevine_b200.ep import EpMoeLayer, GpuBackend, local_experts
@@ -291,9 +291,9 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
 
         def fwd():
             return layer.forward(x)
-        # k_router_chains, k_select, k_quant_rows, k_plan, k_ep_scatter, 2 x k_pf_gemm_ms, k_pf_combine,
-        # k_ep_reduce (NCCL's own kernels not counted)
-        launches = 9
+        # k_router_chains4, k_select, k_quant_rows, k_ep_count, k_ep_pack, k_ep_meta, k_plan, k_ep_scatter,
+        # 2 x k_pf_gemm_ms, k_pf_combine, k_ep_reduce (NCCL's and torch's own kernels not counted)
+        launches = 12
         check = be.status
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
