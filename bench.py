@@ -325,10 +325,13 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(gpu_smi_id(local_rank))
-    clocks.start()
+    # one sampler per node (local rank 0, its own GPU): several nvidia-smi processes polling at
+    # once slow the expert-parallel step's host synchronisations
+    clocks = ClockSampler(gpu_smi_id(local_rank)) if local_rank == 0 else None
+    if clocks:
+        clocks.start()
     step_ms, disp_ms, comb_ms = loop(args.steps, False)
-    clk = clocks.stop()
+    clk = clocks.stop() if clocks else None
     phases_main = dict(phases)
     if world > 1:
         dist.barrier()
