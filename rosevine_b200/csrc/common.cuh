@@ -167,8 +167,7 @@ __device__ __forceinline__ void q8rec_store(uint8_t *rec, int nblk, int b, int l
 // straight-line code that runs once per call. The decode kernels keep their hot paths in the
 // first 64 KB: out-of-line device functions are laid out after the kernel body in the order of
 // their mangled names, so hot helpers carry names of 10 to 19 characters ("fd_..."), which
-// sort first, and rare-path helpers names of fewer than 10 ("x..."), which sort last
-// (tests/test_code_layout.py checks the result).
+// sort first, and rare-path helpers names of fewer than 10 ("x..."), which sort last.
 __device__ __noinline__ float fd_exp_f32(float x) { return (float)exp((double)x); }
 __device__ __noinline__ float fd_tanh_f32(float x) { return (float)tanh((double)x); }
 
