@@ -2,7 +2,7 @@
 // a grouped expert GEMM fed by TMA tensor copies, sm_100a.
 //
 // Replaces the reference's per-expert device loop (runtime/src/hip_exec.rs:820-843) for batches
-// above the decode kernels' 64 tokens and computes what its CPU-experts Q8_0 path computes
+// of more than 16 tokens and computes what its CPU-experts Q8_0 path computes
 // (runtime/src/exec.rs:572-640, expert_pool.rs:282-355, expert_kernel.rs:147-161):
 //
 //   k_plan        (router.cuh) expert groups in plan order, each group starting at a multiple
