@@ -11,6 +11,10 @@
 // the previous one's results (an SM also starts a kernel with its first 64 KB of code at hand,
 // so three compact kernels run faster than one long persistent one):
 //
+// k_fd_gate and k_fd_down are launched as programmatic dependents of the kernel before them: their
+// CTAs start on SMs the previous kernel's CTAs leave and wait for its completion (griddep_wait)
+// before reading what it wrote, which takes most of the launch gap out of each boundary.
+//
 //  k_fd_route (cooperative launch, so all CTAs are resident)
 //   1. router: items of (expert, up to 4 tokens) spread over the CTAs; within an item warp g
 //      takes the g-th 256 columns, forming f64 dots (exact products of bf16/f32 operands) and
@@ -118,6 +122,17 @@ struct FdScratch {
     FdSelGroup g[FD_GROUPS];
 };
 static_assert(sizeof(FdScratch) <= FD_SCRATCH, "phase scratch exceeds its share of the ring");
+
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched as a programmatic dependent (cudaLaunchAttributeProgrammaticStreamSerialization)
+// may start before the kernel ahead of it in the stream has finished; griddep_wait blocks until
+// that kernel has completed and its memory operations are visible. griddep_launch_dependents lets
+// the next such kernel launch early (its CTAs still need free SM resources to start). Both are
+// no-ops in a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // ---------------------------------------------------------------- grid barrier
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
@@ -397,28 +412,66 @@ __device__ __noinline__ bool xchains(const XT *x, const WT *w, const float *bias
 }
 
 // --------------------------------------------------------------- gate / up rows
-// One warp: the 32 packed rows of one ring slot (lane L: row L) against up to two tokens' x
-// records, blocks in order (expert_kernel.rs:147-161). The packed nibble plane stores block b
-// of row R at position b ^ (R & 7) (pack.cuh), so the 32 lanes' 16-byte reads of one block
-// index fall in distinct bank groups. A small rolled loop: this code runs few times per call,
-// and its instruction footprint matters more than its unrolled speed.
+// The 32 packed rows of one ring slot (lane L: row L) against up to two tokens' x records, for
+// small batches (k_fd_gate<..., false>). The packed nibble plane stores block b of row R at
+// position b ^ (R & 7) (pack.cuh), so the 32 lanes' 16-byte reads of one block index fall in
+// distinct bank groups. A task's nb blocks are split into FD_SEG contiguous ranges, one warp
+// each (warp w: range w % FD_SEG of task w / FD_SEG), so that a CTA runs 16 warps where one
+// warp per task would run a long serial chain. Each warp forms its range's products
+// sumi * (dw * dx) in registers; then, in FD_SEG rounds separated by CTA barriers, the warp of
+// range r adds its products in block order onto the running sums the warp of range r - 1 left in
+// `hand`, so every row's sum is the reference's (expert_kernel.rs:147-161). Every thread of the
+// CTA calls it (the barriers); `active` is false for warps without a task.
+constexpr int FD_SEG = 4;
 template <int NB8>
-__device__ __noinline__ float2 fd_gu_rows(const uint8_t *slot, const uint8_t *rec0, const uint8_t *rec1, bool two) {
-    constexpr int nb = NB8 * 8;
-    const int lane = threadIdx.x & 31, sw = lane & 7;
+__device__ __noinline__ void fd_gu_split(const uint8_t *slot, const uint8_t *rec0, const uint8_t *rec1, bool two,
+                                         bool active, float *hand, float *dst) {
+    constexpr int nb = NB8 * 8, SL = nb / FD_SEG;
+    static_assert(nb % FD_SEG == 0, "block ranges must split evenly");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, seg = warp % FD_SEG, sw = lane & 7;
     const uint8_t *nrow = slot + (size_t)lane * nb * 16;
     const uint16_t *srow = reinterpret_cast<const uint16_t *>(slot + FD_ROWS * nb * 16) + lane * nb;
     const Q8Rec xa{rec0, nb}, xb{rec1, nb};
-    float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 4
-    for (int b = 0; b < nb; ++b) {
-        const uint4 nib = *reinterpret_cast<const uint4 *>(nrow + (b ^ sw) * 16);
-        const float dw = f16_bits_to_f32(srow[b]);
-        a0 = __fadd_rn(a0, __fmul_rn((float)q4q8_sumi(nib, xa.qa(b), xa.qb(b), xa.s(b)), __fmul_rn(dw, xa.d(b))));
-        if (two)
-            a1 = __fadd_rn(a1, __fmul_rn((float)q4q8_sumi(nib, xb.qa(b), xb.qb(b), xb.s(b)), __fmul_rn(dw, xb.d(b))));
+    float p0[SL], p1[SL];
+    if (active && two) {
+#pragma unroll
+        for (int k = 0; k < SL; ++k) {
+            const int b = seg * SL + k;
+            const uint4 nib = *reinterpret_cast<const uint4 *>(nrow + (b ^ sw) * 16);
+            const float dw = f16_bits_to_f32(srow[b]);
+            p0[k] = __fmul_rn((float)q4q8_sumi(nib, xa.qa(b), xa.qb(b), xa.s(b)), __fmul_rn(dw, xa.d(b)));
+            p1[k] = __fmul_rn((float)q4q8_sumi(nib, xb.qa(b), xb.qb(b), xb.s(b)), __fmul_rn(dw, xb.d(b)));
+        }
+    } else if (active) {
+#pragma unroll
+        for (int k = 0; k < SL; ++k) {
+            const int b = seg * SL + k;
+            const uint4 nib = *reinterpret_cast<const uint4 *>(nrow + (b ^ sw) * 16);
+            const float dw = f16_bits_to_f32(srow[b]);
+            p0[k] = __fmul_rn((float)q4q8_sumi(nib, xa.qa(b), xa.qb(b), xa.s(b)), __fmul_rn(dw, xa.d(b)));
+            p1[k] = 0.0f;
+        }
     }
-    return make_float2(a0, a1);
+    float *h = hand + (warp / FD_SEG) * 64;
+#pragma unroll 1
+    for (int r = 0; r < FD_SEG; ++r) {
+        if (active && seg == r) {
+            float a0 = r ? h[lane] : 0.0f, a1 = r ? h[32 + lane] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < SL; ++k) a0 = __fadd_rn(a0, p0[k]);
+            if (two) {
+#pragma unroll
+                for (int k = 0; k < SL; ++k) a1 = __fadd_rn(a1, p1[k]);
+            }
+            if (r + 1 < FD_SEG) {
+                h[lane] = a0, h[32 + lane] = a1;
+            } else {
+                dst[lane] = a0;
+                if (two) dst[64 + lane] = a1;
+            }
+        }
+        __syncthreads();
+    }
 }
 
 // The same rows for batches (k_fd_gate<..., true>): warp w computes row (w & 7) * 4 + lane / 8
@@ -706,6 +759,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_route(FdArgs a) {
         fence_barrier_init();
     }
     __syncthreads();
+    griddep_launch_dependents();  // k_fd_gate may take SMs as this kernel's CTAs leave
     // this CTA's k-th router item into buffer k & 1: part 0 the router row (and the arrive),
     // part 1 + tt the x row of token tt
     auto issue_item = [&](int k, int part) {
@@ -768,6 +822,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     __shared__ int s_ftok[FD_MAX_TOK];
     __shared__ int s_nflag, s_n_act, s_bad;
     __shared__ FdCtx C;
+    __shared__ float s_hand[FD_WARPS / FD_SEG][2][32];  // fd_gu_split's running sums
     RVC_MARK(4, 2);
     const FdLayout &L = a.L;
     constexpr int nb = NB8 * 8;
@@ -800,6 +855,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     }
     __syncthreads();
 
+    // k_fd_route's results are complete and visible past this point; k_fd_down may launch
+    griddep_wait();
+    griddep_launch_dependents();
     // ------------------------------------------------------------ routing
     // the ids and weights k_fd_route published (or the caller's); tokens whose order it could
     // not certify go through the reference's exact chains here, over all CTAs
@@ -807,12 +865,15 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     if (route) {
 #pragma unroll 1
         for (int i = tid; i < pairs; i += FD_THREADS) p_ids[i] = __ldcg(a.sel_ids + i), p_wts[i] = __ldcg(a.sel_wts + i);
-        if (tid == 0) {
-            int n = 0;
-#pragma unroll 1
-            for (int t = 0; t < T; ++t)
-                if (__ldcg(a.sel_flag + t)) s_ftok[n++] = t;
-            s_nflag = n;
+        if (warp == FD_WARPS - 1) {  // the flagged tokens in ascending order, from two ballots (T <= 64)
+            static_assert(FD_MAX_TOK <= 64, "two ballots cover the flags");
+            const bool f0 = lane < T && __ldcg(a.sel_flag + lane) != 0;
+            const bool f1 = lane + 32 < T && __ldcg(a.sel_flag + lane + 32) != 0;
+            const unsigned b0 = __ballot_sync(0xffffffffu, f0), b1 = __ballot_sync(0xffffffffu, f1);
+            const unsigned below = (1u << lane) - 1u;
+            if (f0) s_ftok[__popc(b0 & below)] = lane;
+            if (f1) s_ftok[__popc(b0) + __popc(b1 & below)] = lane + 32;
+            if (lane == 0) s_nflag = __popc(b0) + __popc(b1);
         }
         __syncthreads();
         if (s_nflag > 0 &&
@@ -988,7 +1049,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                     }
                 }
             } else {
-            // tasks (w, half, token pair): unit w of the wave has nt_w tokens in this chunk
+            // tasks (w, half, token pair): unit w of the wave has nt_w tokens in this chunk; each
+            // task split over FD_SEG warps (fd_gu_split)
             int ntask = 0;
 #pragma unroll 1
             for (int w = 0; w < nw; ++w) {
@@ -997,27 +1059,31 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                 ntask += 2 * ((nt + 1) / 2);
             }
 #pragma unroll 1
-            for (int task = warp; task < ntask; task += FD_WARPS) {
-                int w = 0, k = task, nt = 0, e = 0;
+            for (int t0 = 0; t0 < ntask; t0 += FD_WARPS / FD_SEG) {  // uniform: fd_gu_split syncs the CTA
+                const int task = t0 + warp / FD_SEG;
+                const bool active = task < ntask;
+                const uint8_t *slot = ring, *r0p = recs, *r1p = recs;
+                bool two = false;
+                float *dst = sgu;
+                if (active) {
+                    int w = 0, k = task, nt = 0, e = 0;
 #pragma unroll 1
-                for (;; ++w) {
-                    e = p_act[(C.g0 + u0 + w) / nbh];
-                    nt = resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
-                    const int n = 2 * ((nt + 1) / 2);
-                    if (k < n) break;
-                    k -= n;
+                    for (;; ++w) {
+                        e = p_act[(C.g0 + u0 + w) / nbh];
+                        nt = resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
+                        const int n = 2 * ((nt + 1) / 2);
+                        if (k < n) break;
+                        k -= n;
+                    }
+                    const int half = k & 1, i = (k >> 1) * 2;  // tokens i, i + 1 of the chunk
+                    two = i + 1 < nt;
+                    const int pa = p_off[e] + m * AX + i;
+                    r0p = resident ? recs + (size_t)(p_order[pa] / used) * xrb : recs + (size_t)i * xrb;
+                    r1p = !two ? r0p : (resident ? recs + (size_t)(p_order[pa + 1] / used) * xrb : r0p + xrb);
+                    slot = ring + (size_t)((2 * (u0 + w) + half) % L.nslot) * L.slot_bytes;
+                    dst = sgu + ((size_t)(w * AX + i) * 2 + half) * 32;
                 }
-                const int half = k & 1, i = (k >> 1) * 2;  // tokens i, i + 1 of the chunk
-                const bool two = i + 1 < nt;
-                const int pa = p_off[e] + m * AX + i;
-                const uint8_t *r0p = resident ? recs + (size_t)(p_order[pa] / used) * xrb : recs + (size_t)i * xrb;
-                const uint8_t *r1p =
-                    !two ? r0p : (resident ? recs + (size_t)(p_order[pa + 1] / used) * xrb : r0p + xrb);
-                const uint8_t *slot = ring + (size_t)((2 * (u0 + w) + half) % L.nslot) * L.slot_bytes;
-                const float2 acc = fd_gu_rows<NB8>(slot, r0p, r1p, two);
-                float *dst = sgu + ((size_t)(w * AX + i) * 2 + half) * 32 + lane;
-                dst[0] = acc.x;
-                if (two) dst[64] = acc.y;
+                fd_gu_split<NB8>(slot, r0p, r1p, two, active, &s_hand[0][0][0], dst);
             }
             }
             __syncthreads();
@@ -1074,6 +1140,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
     __shared__ uint64_t full[FD_MAX_SLOTS], actb[2];
     __shared__ FdCtx C;
     RVC_MARK(4, 6);
+    griddep_wait();  // k_fd_gate's plan and h records are complete and visible past this point
     const FdLayout &L = a.L;
     const int tid = threadIdx.x;
     const int G = gridDim.x, c = blockIdx.x;

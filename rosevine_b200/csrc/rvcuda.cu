@@ -354,7 +354,8 @@ int fd_smem_max(K kernel, size_t *out) {
 }
 
 // The three decode kernels on `st`, each on one CTA per SM: k_fd_route and k_fd_gate cooperative
-// (all CTAs resident, for their grid barriers), k_fd_down plain.
+// (all CTAs resident, for their grid barriers), k_fd_down plain; the last two as programmatic
+// dependents of the kernel before them.
 template <typename XT, typename WT, int NB8>
 int launch_fd_n(FdArgs &a, cudaStream_t st) {
     auto kr = k_fd_route<XT, WT, NB8>;
@@ -381,13 +382,25 @@ int launch_fd_n(FdArgs &a, cudaStream_t st) {
     cfg.numAttrs = 1;
     cfg.dynamicSmemBytes = a.L.r_bytes;
     if ((rc = (int)cudaLaunchKernelEx(&cfg, kr, a))) return rc;
+    // k_fd_gate and k_fd_down as programmatic dependents: each is launched while its predecessor
+    // runs, its CTAs take SMs as the predecessor's CTAs leave, and it waits (griddepcontrol.wait)
+    // for the predecessor's completion before reading what that wrote
+    cudaLaunchAttribute dep[2];
+    dep[0] = attr[0];
+    dep[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    dep[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = dep;
+    cfg.numAttrs = 2;
     cfg.dynamicSmemBytes = a.L.bytes;
     if (a.n_tok <= a.L.act_x)  // every x record fits one buffer: the small-batch gate/up kernel
         rc = (int)cudaLaunchKernelEx(&cfg, kg, a);
     else
         rc = (int)cudaLaunchKernelEx(&cfg, k_fd_gate<XT, WT, NB8, true>, a);
     if (rc) return rc;
-    k_fd_down<<<G, FD_THREADS, a.L.d_bytes, st>>>(a);
+    cfg.attrs = dep + 1;  // k_fd_down: not cooperative
+    cfg.numAttrs = 1;
+    cfg.dynamicSmemBytes = a.L.d_bytes;
+    if ((rc = (int)cudaLaunchKernelEx(&cfg, k_fd_down, a))) return rc;
     return launched();
 }
 
