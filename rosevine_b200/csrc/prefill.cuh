@@ -58,6 +58,16 @@ constexpr float PF_MAGIC = 12582912.0f;
 // leaves sum (n - 8) q exactly (all values integers below 2^24).
 __device__ __forceinline__ float2 pf_scale_offset(float d, int qs) { return make_float2(d, -(PF_MAGIC + 8.0f * (float)qs)); }
 
+// The (scale, offset) plane of activation blocks (x: xso, h: hso) is block-major, 2 * ppad f32
+// per block, each position pair (2k, 2k + 1) stored as [scale 2k, scale 2k + 1, offset 2k,
+// offset 2k + 1]: the GEMM then loads a pair's two scales and its two offsets as ready f32x2
+// operands (one 16-byte load, no register shuffling). ppad is even.
+__device__ __forceinline__ void pf_store_so(float2 *plane, int ppad, int b, int k, float2 so) {
+    float *p = reinterpret_cast<float *>(plane) + (size_t)b * 2 * ppad + 4 * (k >> 1) + (k & 1);
+    p[0] = so.x;
+    p[2] = so.y;
+}
+
 // ------------------------------------------------------------------ tcgen05 primitives
 __device__ __forceinline__ void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {  // one full warp
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
@@ -234,7 +244,7 @@ __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int 
         for (int j = 0; j < used; ++j) {
             const int k = __shfl_sync(0xffffffffu, my_pos, j);
             q8rec_store(xperm + (size_t)k * xrb, nb, b, lane, q, dbits, qsum);
-            if (lane == 0) xso[(size_t)b * ppad + k] = so;
+            if (lane == 0) pf_store_so(xso, ppad, b, k, so);
         }
         v = vn;
     }
@@ -408,7 +418,7 @@ __global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ 
             if (lane == 0) {
                 reinterpret_cast<float *>(dst + nb * 32)[b] = d;
                 reinterpret_cast<int *>(dst + nb * 36)[b] = qs;
-                xso[(size_t)b * ppad + k] = pf_scale_offset(d, qs);
+                pf_store_so(xso, ppad, b, k, pf_scale_offset(d, qs));
             }
         }
     }
@@ -494,6 +504,29 @@ __device__ __forceinline__ float2 f2_prod(float2 a, float2 b, uint64_t negzero2)
           "l"(((uint64_t)__float_as_uint(b.y) << 32) | __float_as_uint(b.x)), "l"(negzero2));
     return make_float2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
 }
+// The same on f32x2 values kept packed in 64-bit registers (low half: the first lane), which
+// the GEMM's inner loop uses so that no operand needs repacking.
+__device__ __forceinline__ uint64_t f2x_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2x_prod(uint64_t a, uint64_t b, uint64_t negzero2) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(negzero2));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2x_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) {
+    const uint64_t u = __float_as_uint(v);
+    return (u << 32) | u;
+}
+__device__ __forceinline__ float f2x_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2x_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
     uint64_t r;
     asm("add.rn.f32x2 %0, %1, %2;"
@@ -523,7 +556,7 @@ constexpr int PM_STAGES = 3;
 constexpr int PM_OFF_B = PF_NIB_BYTES;
 constexpr int PM_OFF_SO = PM_OFF_B + PF_B_BYTES;
 constexpr int PM_STAGE_BYTES = PM_OFF_SO + PF_DX_BYTES;  // 56 KB
-constexpr int PM_DW_WARP = 2 * PF_KB * 32;               // f32 per warp: [2 stages][8 blocks][32 rows]
+constexpr int PM_DW_WARP = 2 * PF_KB * 32;  // f32 per warp: [2 stages][8 blocks][8 g][4: row 16 i + 8 h + g]
 constexpr int PM_OFF_DW = PM_STAGES * PM_STAGE_BYTES;
 constexpr int PM_SMEM_BYTES = PM_OFF_DW + PM_WARPS * PM_DW_WARP * 4 + 1024;
 constexpr int PM_H_PITCH = 33;  // gate/up staging [unit][gate|up][position][33]
@@ -539,12 +572,26 @@ __device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 
+// The same MMA with the accumulator fragment returned as two f32x2-ready 64-bit values: rows g and
+// g + 8, each (position 2 tq, position 2 tq + 1) in (low, high) halves.
+__device__ __forceinline__ void mma_u8s8_x2(uint64_t (&d)[2], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1, uint32_t c) {
+    asm("{\n\t.reg .b32 r0, r1, r2, r3;\n\t"
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {r0, r1, r2, r3}, {%2, %3, %4, %5}, {%6, %7}, "
+        "{%8, %8, %8, %8};\n\t"
+        "mov.b64 %0, {r0, r1};\n\tmov.b64 %1, {r2, r3};\n\t}"
+        : "=l"(d[0]), "=l"(d[1])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_constant__ CUtensorMap map_nib,
                                                               const __grid_constant__ CUtensorMap map_act,
                                                               const __grid_constant__ CUtensorMap map_so, PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base, by an offset from the shared array itself (pointer arithmetic keeps
+    // the compiler's knowledge that these are shared addresses: 32-bit LDS, not generic loads)
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     __shared__ uint64_t full[PM_STAGES], empty[PM_STAGES];
     if ((int)blockIdx.y >= __ldg(a.n_tiles)) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -576,7 +623,8 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
     const int g = lane >> 2, tq = lane & 3;
     const int nj = min(4, (nt - 32 * wc + 7) >> 3);  // 8-position fragments holding tokens
     // the warp's weight scales: lane l loads row 32 wr + l's 8 scales of a stage one stage ahead
-    // (four f16 pairs) and stores them as f32 in the warp's own slice [2][8 blocks][32 rows]
+    // (four f16 pairs) and stores them as f32 in the warp's own slice [2][8 blocks][8][4], where
+    // row l = 16 i + 8 h + g sits at [g][2 i + h]: one 16-byte load gives a lane its four rows
     const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + (size_t)(wrow0 + 32 * wr + lane) * nblk);
     float *const sdw = reinterpret_cast<float *>(smem + PM_OFF_DW) + warp * PM_DW_WARP;
     uint32_t wn[4];
@@ -585,7 +633,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         for (int k = 0; k < 4; ++k) wn[k] = st * PF_KB + 2 * k < nblk ? __ldg(srow + (st * PF_KB) / 2 + k) : 0u;
     };
     auto st_dw = [&](int st) {
-        float *d = sdw + (st & 1) * (PF_KB * 32) + lane;
+        float *d = sdw + (st & 1) * (PF_KB * 32) + (lane & 7) * 4 + (lane >> 4) * 2 + ((lane >> 3) & 1);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             d[(2 * k) * 32] = f16_bits_to_f32((uint16_t)(wn[k] & 0xFFFFu));
@@ -595,11 +643,12 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
     ld_dw(0);
     st_dw(0);
     __syncwarp();
-    float2 acc[2][4][2];  // [row fragment][position fragment][rows g, g + 8]: positions 2 tq, 2 tq + 1
+    // [row fragment][position fragment][rows g, g + 8], f32x2 of positions 2 tq, 2 tq + 1 (low, high)
+    uint64_t acc[2][4][2];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) acc[i][jj][0] = acc[i][jj][1] = make_float2(0.0f, 0.0f);
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj][0] = acc[i][jj][1] = 0ull;
     const uint64_t nz2 = a.negzero2;
     bool ok = true;
     for (int st = 0; st < nst && ok; ++st) {
@@ -609,15 +658,12 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok) {
             const uint8_t *sN = smem + s * PM_STAGE_BYTES, *sB = sN + PM_OFF_B;
-            const float4 *sSO = reinterpret_cast<const float4 *>(sN + PM_OFF_SO);
-            const float *dwp = sdw + (st & 1) * (PF_KB * 32) + g;
+            const ulonglong2 *sSO = reinterpret_cast<const ulonglong2 *>(sN + PM_OFF_SO);
+            const float4 *dwp = reinterpret_cast<const float4 *>(sdw + (st & 1) * (PF_KB * 32)) + g;
             const int kn = min(PF_KB, nblk - st * PF_KB);
             for (int jb = 0; jb < kn; ++jb) {
-                float dw[2][2];
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) dw[i][h] = dwp[jb * 32 + 16 * i + 8 * h];
+                const float4 w4 = dwp[jb * 8];  // rows g, g + 8, 16 + g, 24 + g of the warp
+                const uint64_t dw[2][2] = {{f2_splat(w4.x), f2_splat(w4.y)}, {f2_splat(w4.z), f2_splat(w4.w)}};
                 uint32_t af[2][4];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -635,18 +681,17 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                         const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sB + (2 * jb) * (PF_N * 16) + n * 16 + 4 * tq);
                         const uint32_t b1 =
                             *reinterpret_cast<const uint32_t *>(sB + (2 * jb + 1) * (PF_N * 16) + n * 16 + 4 * tq);
-                        // (scale, offset) of positions 32 wc + 8 jj + 2 tq and + 1
-                        const float4 so = sSO[(jb * PF_N + 32 * wc + 8 * jj + 2 * tq) >> 1];
-                        const float2 off = make_float2(so.y, so.w), dx = make_float2(so.x, so.z);
+                        // scales (x) and offsets (y) of positions 32 wc + 8 jj + 2 tq and + 1
+                        const ulonglong2 so = sSO[(jb * PF_N + 32 * wc + 8 * jj + 2 * tq) >> 1];
 #pragma unroll
                         for (int i = 0; i < 2; ++i) {
-                            uint32_t d[4];
-                            mma_u8s8(d, af[i][0], af[i][1], af[i][2], af[i][3], b0, b1, PF_MAGIC_BITS);
+                            uint64_t d[2];  // rows g, g + 8; each the f32x2 of positions 2 tq, 2 tq + 1
+                            mma_u8s8_x2(d, af[i][0], af[i][1], af[i][2], af[i][3], b0, b1, PF_MAGIC_BITS);
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
-                                const float2 sc = f2_mul(make_float2(dw[i][h], dw[i][h]), dx);
-                                const float2 t = f2_add(make_float2(__uint_as_float(d[2 * h]), __uint_as_float(d[2 * h + 1])), off);
-                                acc[i][jj][h] = f2_add(acc[i][jj][h], f2_prod(t, sc, nz2));
+                                const uint64_t sc = f2x_mul(dw[i][h], so.x);
+                                const uint64_t t = f2x_add(d[h], so.y);
+                                acc[i][jj][h] = f2x_add(acc[i][jj][h], f2x_prod(t, sc, nz2));
                             }
                         }
                     }
@@ -676,8 +721,8 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int row = row0 + 32 * wr + 16 * i + 8 * h + g, tok = 32 * wc + 8 * jj + 2 * tq;
-                        if (tok < nt) a.y[(size_t)(p0 + tok) * a.n_embd + row] = acc[i][jj][h].x;
-                        if (tok + 1 < nt) a.y[(size_t)(p0 + tok + 1) * a.n_embd + row] = acc[i][jj][h].y;
+                        if (tok < nt) a.y[(size_t)(p0 + tok) * a.n_embd + row] = f2x_lo(acc[i][jj][h]);
+                        if (tok + 1 < nt) a.y[(size_t)(p0 + tok + 1) * a.n_embd + row] = f2x_hi(acc[i][jj][h]);
                     }
         }
     } else {
@@ -698,8 +743,8 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                     for (int h = 0; h < 2; ++h) {
                         const int c = 16 * i + 8 * h + g, tok = 32 * wc + 8 * jj + 2 * tq;
                         float *hp = H + ((size_t)(u * 2 + x) * PF_N + tok) * PM_H_PITCH + c;
-                        hp[0] = acc[i][jj][h].x;
-                        hp[PM_H_PITCH] = acc[i][jj][h].y;
+                        hp[0] = f2x_lo(acc[i][jj][h]);
+                        hp[PM_H_PITCH] = f2x_hi(acc[i][jj][h]);
                     }
         }
         named_sync_n(6, n_active * 32);
@@ -716,7 +761,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                 const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);
                 const int q = (row0 >> 6) + uu;  // h block within the expert's ff columns
                 q8rec_store(a.hrec + (size_t)(p0 + tok) * hrb, a.nh, q, lane, qv, dbits, qsum);
-                if (lane == 0) a.hso[(size_t)q * a.ppad + p0 + tok] = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
+                if (lane == 0) pf_store_so(a.hso, a.ppad, q, p0 + tok, pf_scale_offset(f16_bits_to_f32(dbits), qsum));
             }
         }
     }
