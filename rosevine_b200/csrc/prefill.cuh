@@ -572,6 +572,11 @@ __device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 
+template <bool B>
+struct BoolTag {
+    static constexpr bool value = B;
+};
+
 // The same MMA with the accumulator fragment returned as two f32x2-ready 64-bit values: rows g and
 // g + 8, each (position 2 tq, position 2 tq + 1) in (low, high) halves.
 __device__ __forceinline__ void mma_u8s8_x2(uint64_t (&d)[2], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -661,6 +666,12 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
             const ulonglong2 *sSO = reinterpret_cast<const ulonglong2 *>(sN + PM_OFF_SO);
             const float4 *dwp = reinterpret_cast<const float4 *>(sdw + (st & 1) * (PF_KB * 32)) + g;
             const int kn = min(PF_KB, nblk - st * PF_KB);
+            // FULL: all four position fragments hold tokens (every warp of a full tile), so the
+            // block loop runs without per-fragment branches (nor the convergence points
+            // mma.sync needs after them)
+            auto blocks = [&](auto full_tag) {
+            constexpr bool FULL = decltype(full_tag)::value;
+#pragma unroll 2
             for (int jb = 0; jb < kn; ++jb) {
                 const float4 w4 = dwp[jb * 8];  // rows g, g + 8, 16 + g, 24 + g of the warp
                 const uint64_t dw[2][2] = {{f2_splat(w4.x), f2_splat(w4.y)}, {f2_splat(w4.z), f2_splat(w4.w)}};
@@ -676,7 +687,7 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                 }
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
-                    if (jj < nj) {
+                    if (FULL || jj < nj) {
                         const int n = 32 * wc + 8 * jj + g;  // the B column this lane supplies
                         const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sB + (2 * jb) * (PF_N * 16) + n * 16 + 4 * tq);
                         const uint32_t b1 =
@@ -697,6 +708,11 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                     }
                 }
             }
+            };
+            if (nj == 4)
+                blocks(BoolTag<true>{});
+            else
+                blocks(BoolTag<false>{});
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage's buffers
