@@ -218,35 +218,64 @@ __global__ void __launch_bounds__(128) k_debug_mma_i8(const int8_t *__restrict__
 }
 
 // ------------------------------------------------------------------ quantise + scatter
-// Q8_0 of x, once per token: warp w quantises 8 blocks of token w / (nb / 8) one by one (the
-// next block's values loaded while this one is processed) and writes each into the records of
-// the token's
-// `used` plan positions pos_of[t used + j], with the block's (scale, offset) pair in the
-// block-major plane xso[b][position] the GEMM's scale tiles come from.
+// Q8_0 of x, once per token, written into the records of the token's `used` plan positions
+// pos_of[t used + j], with each block's (scale, offset) pair in the block-major plane xso the
+// GEMM's scale tiles come from. Four lanes per block: lane l of warp w takes values
+// 8 (l & 3) .. + 7 of block 8 w' + (l >> 2) of its token (one 16-byte load for bf16, two for
+// f32; rows are 16-byte aligned, as the entry points require), so a warp quantises 8 blocks at
+// once, each reduction taking two shuffles within the group of four lanes, and writes a plan
+// position's 8 quants per lane with one 8-byte store. Per value the arithmetic is
+// quant_q8_lane's (ops.rs:95-105); a block's amax and integer sum do not depend on the
+// reduction order.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int n_embd, int n_tok, int used,
                                                   const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
                                                   float2 *__restrict__ xso, int ppad) {
     const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, part = lane & 3;
     const int nc = (nb + 7) / 8, wi = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (wi >= n_tok * nc) return;
-    const int t = wi / nc, b0 = (wi - t * nc) * 8, b1 = min(nb, b0 + 8);
+    if (wi >= n_tok * nc) return;  // whole warps leave together
+    const int t = wi / nc, b = (wi - t * nc) * 8 + (lane >> 2);
+    const bool in = b < nb;  // lanes past the row's last block take part in the shuffles only
+    float v[8];
+    if (in) {
+        ld8<XT>(x + (size_t)t * n_embd, (size_t)b * QK + part * 8, v);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t qw[2] = {0u, 0u};
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float r = roundf(__fmul_rn(v[k], id));
+        const int q = r != r ? 0 : (r > 127.0f ? 127 : (r < -128.0f ? -128 : (int)r));
+        s += q;
+        qw[k >> 2] |= (uint32_t)(uint8_t)(int8_t)q << (8 * (k & 3));
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    const float df = f16_bits_to_f32(f32_to_f16_bits(d));
+    const float2 so = pf_scale_offset(df, s);
     const int my_pos = lane < used ? __ldg(pos_of + (size_t)t * used + lane) : 0;
-    const size_t xrow = (size_t)t * n_embd + lane;
-    float v = ld_val<XT>(x, xrow + (size_t)b0 * QK);
-    for (int b = b0; b < b1; ++b) {
-        const float vn = b + 1 < b1 ? ld_val<XT>(x, xrow + (size_t)(b + 1) * QK) : 0.0f;
-        uint16_t dbits;
-        int qsum;
-        const int8_t q = quant_q8_lane(v, &dbits, &qsum);
-        const float2 so = pf_scale_offset(f16_bits_to_f32(dbits), qsum);
-        for (int j = 0; j < used; ++j) {
-            const int k = __shfl_sync(0xffffffffu, my_pos, j);
-            q8rec_store(xperm + (size_t)k * xrb, nb, b, lane, q, dbits, qsum);
-            if (lane == 0) pf_store_so(xso, ppad, b, k, so);
+    for (int j = 0; j < used; ++j) {
+        const int k = __shfl_sync(0xffffffffu, my_pos, j);
+        if (in) {
+            uint8_t *rec = xperm + (size_t)k * xrb;
+            *reinterpret_cast<uint2 *>(rec + b * 32 + part * 8) = make_uint2(qw[0], qw[1]);
+            if (part == 0) {
+                reinterpret_cast<float *>(rec + nb * 32)[b] = df;
+                reinterpret_cast<int *>(rec + nb * 36)[b] = s;
+                pf_store_so(xso, ppad, b, k, so);
+            }
         }
-        v = vn;
     }
 }
 

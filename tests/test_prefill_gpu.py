@@ -1,11 +1,11 @@
-"""GPU parity of the prefill path (batches above 64 tokens: the tensor-core grouped GEMM).
+"""GPU parity of the prefill path (batches above 16 tokens: the grouped expert GEMMs).
 
-The first test checks one tensor-core tile (tcgen05.mma kind::i8 through the shared-memory
-layouts and tensor-memory reads of the GEMM) against numpy's int32 product, so that a layout
-mistake shows there before the full kernels run. The layer tests compare rvc_moe_forward with
-the oracle's scalar kernel: the router runs in the reference's order, the int32 block dots come
-from the tensor cores exactly, and the epilogue accumulates them in the scalar reference's
-order with separately rounded operations, so ids, weights and the output are bit-identical.
+The first test checks one tensor-core tile (the tcgen05.mma kind::i8 debug kernel, through the
+shared-memory layouts and tensor-memory reads) against numpy's int32 product. The layer tests
+compare rvc_moe_forward with the oracle's scalar kernel: the router runs in the reference's
+order, the int32 block dots come from the tensor cores (mma.sync) exactly, and the epilogue
+accumulates them in the scalar reference's order with separately rounded operations, so ids,
+weights and the output are bit-identical.
 """
 import numpy as np
 import pytest
@@ -56,6 +56,22 @@ def test_prefill_layer_bit_exact(layer, weights, oracle, pool, n_tok):
     want, want_ids, want_w, _ = oracle.moe_layer(pool, x, x, weights["w_router"], weights["gate_up"], weights["down"])
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     assert np.array_equal(wts.cpu().numpy().view(np.uint32), want_w.view(np.uint32))
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"max abs diff {np.abs(got - want).max():.3e}"
+
+
+def test_prefill_f32_inputs_bit_exact(layer, weights, oracle, pool):
+    """f32 activations (the reference model's own format) through the f32 loads of the router
+    chains and of the quantisation kernel."""
+    from rosevine_b200 import synth
+    n_tok = 100
+    x = synth.rms_normalise(np.random.default_rng(901).standard_normal((n_tok, 2816)).astype(np.float32))
+    ids = torch.empty((n_tok, 8), dtype=torch.int32, device="cuda")
+    out = layer.forward(torch.from_numpy(x).cuda(), ids=ids)
+    layer.status()
+    want, want_ids, _, _ = oracle.moe_layer(pool, x, x, weights["w_router"], weights["gate_up"], weights["down"])
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
     got = out.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
         f"max abs diff {np.abs(got - want).max():.3e}"
