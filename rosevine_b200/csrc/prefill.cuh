@@ -601,6 +601,15 @@ __device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
 }
 
+// Four 8 x 8 b16 matrices from shared memory: lane L supplies the address of row L & 7 of
+// matrix L >> 3 (16 bytes); each lane receives, per matrix, the 4 bytes at columns 4 (L & 3) ..
+// of row L >> 2, the layout of an mma.sync m16n8k32 int8 operand fragment.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 template <bool B>
 struct BoolTag {
     static constexpr bool value = B;
@@ -656,6 +665,9 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
     const int wr = warp & 3, wc = warp >> 2;  // rows 32 wr .., positions 32 wc ..
     const int g = lane >> 2, tq = lane & 3;
     const int nj = min(4, (nt - 32 * wc + 7) >> 3);  // 8-position fragments holding tokens
+    // this lane's row address for the ldmatrix loads of A (nibble rows) and B (position rows)
+    const uint32_t a_row = (uint32_t)(32 * wr + lane) * (PF_KB * 16);
+    const uint32_t b_lane = (uint32_t)((lane >> 3) & 1) * (PF_N * 16) + (uint32_t)(32 * wc + 8 * (lane >> 4) + (lane & 7)) * 16;
     // the warp's weight scales: lane l loads row 32 wr + l's 8 scales of a stage one stage ahead
     // (four f16 pairs) and stores them as f32 in the warp's own slice [2][8 blocks][8][4], where
     // row l = 16 i + 8 h + g sits at [g][2 i + h]: one 16-byte load gives a lane its four rows
@@ -691,8 +703,9 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
         if (lane == 0) ok = pf_wait(&full[s], (uint32_t)(st / PM_STAGES) & 1u, a.status);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok) {
-            const uint8_t *sN = smem + s * PM_STAGE_BYTES, *sB = sN + PM_OFF_B;
+            const uint8_t *sN = smem + s * PM_STAGE_BYTES;
             const ulonglong2 *sSO = reinterpret_cast<const ulonglong2 *>(sN + PM_OFF_SO);
+            const uint32_t sN32 = smem_u32(sN), sB32 = sN32 + PM_OFF_B;
             const float4 *dwp = reinterpret_cast<const float4 *>(sdw + (st & 1) * (PF_KB * 32)) + g;
             const int kn = min(PF_KB, nblk - st * PF_KB);
             // FULL: all four position fragments hold tokens (every warp of a full tile), so the
@@ -704,23 +717,28 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
             for (int jb = 0; jb < kn; ++jb) {
                 const float4 w4 = dwp[jb * 8];  // rows g, g + 8, 16 + g, 24 + g of the warp
                 const uint64_t dw[2][2] = {{f2_splat(w4.x), f2_splat(w4.y)}, {f2_splat(w4.z), f2_splat(w4.w)}};
+                // A: one ldmatrix gives each lane 4 nibble bytes of rows g, g + 8, 16 + g, 24 + g
+                // of the warp (lane L addresses row 8 (L >> 3) + (L & 7), whose swizzle key is
+                // L & 7), the byte columns 4 tq .. of their block-jb chunks
+                uint32_t wq[4];
+                ldsm_x4(sN32 + a_row + ((a.swizzled ? (jb ^ (lane & 7)) : jb) << 4), wq);
                 uint32_t af[2][4];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
-                    const int r = 32 * wr + 16 * i + g;  // r and r + 8 share r & 7: one swizzled position
-                    const int pos = a.swizzled ? (jb ^ (r & 7)) : jb;
-                    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(sN + r * (PF_KB * 16) + pos * 16 + 4 * tq);
-                    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(sN + (r + 8) * (PF_KB * 16) + pos * 16 + 4 * tq);
+                    const uint32_t w0 = wq[2 * i], w1 = wq[2 * i + 1];
                     af[i][0] = w0 & 0x0F0F0F0Fu, af[i][1] = w1 & 0x0F0F0F0Fu;
                     af[i][2] = (w0 >> 4) & 0x0F0F0F0Fu, af[i][3] = (w1 >> 4) & 0x0F0F0F0Fu;
                 }
+                // B: one ldmatrix per two position fragments: both K-halves of block jb for the
+                // 8 positions of fragment jj and of jj + 1 (lane L addresses K-half 2 jb +
+                // ((L >> 3) & 1), position 8 (L >> 4) + (L & 7) of the pair)
+                uint32_t bq[2][4];
+                ldsm_x4(sB32 + b_lane + jb * (2 * PF_N * 16), bq[0]);
+                if (FULL || nj > 2) ldsm_x4(sB32 + b_lane + jb * (2 * PF_N * 16) + 16 * 16, bq[1]);
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                     if (FULL || jj < nj) {
-                        const int n = 32 * wc + 8 * jj + g;  // the B column this lane supplies
-                        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sB + (2 * jb) * (PF_N * 16) + n * 16 + 4 * tq);
-                        const uint32_t b1 =
-                            *reinterpret_cast<const uint32_t *>(sB + (2 * jb + 1) * (PF_N * 16) + n * 16 + 4 * tq);
+                        const uint32_t b0 = bq[jj >> 1][2 * (jj & 1)], b1 = bq[jj >> 1][2 * (jj & 1) + 1];
                         // scales (x) and offsets (y) of positions 32 wc + 8 jj + 2 tq and + 1
                         const ulonglong2 so = sSO[(jb * PF_N + 32 * wc + 8 * jj + 2 * tq) >> 1];
 #pragma unroll
