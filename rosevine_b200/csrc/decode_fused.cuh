@@ -515,13 +515,15 @@ __device__ __noinline__ float2 fd_gu_wide(const uint8_t *slot, const uint8_t *re
 }
 
 // One down-projection dot: row `nrow`/`srow` of a staged tile against the h record `hrec`,
-// nbh blocks in block order (expert_kernel.rs:147-161).
-__device__ __noinline__ float fd_dn_row(const uint8_t *nrow, const uint16_t *srow, const uint8_t *hrec, int nbh) {
+// nbh blocks in block order (expert_kernel.rs:147-161); `key` is the low 3 bits of the row's
+// index, by which its complete 8-block groups are swizzled in the packed plane (nib_pos).
+__device__ __noinline__ float fd_dn_row(const uint8_t *nrow, const uint16_t *srow, const uint8_t *hrec, int nbh,
+                                       int key) {
     const Q8Rec hr{hrec, nbh};
     float acc = 0.0f;
 #pragma unroll 4
     for (int b = 0; b < nbh; ++b) {
-        const uint4 nib = *reinterpret_cast<const uint4 *>(nrow + b * 16);
+        const uint4 nib = *reinterpret_cast<const uint4 *>(nrow + nib_pos(b, nbh, key) * 16);
         const int sumi = q4q8_sumi(nib, hr.qa(b), hr.qb(b), hr.s(b));
         acc = __fadd_rn(acc, __fmul_rn((float)sumi, __fmul_rn(f16_bits_to_f32(srow[b]), hr.d(b))));
     }
@@ -1238,7 +1240,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
                     const uint8_t *t0 = slot + (size_t)(x - alo) * C.tile;
                     const float acc = fd_dn_row(t0 + (size_t)rr * nbh * 16,
                                                 reinterpret_cast<const uint16_t *>(t0 + C.dn_nib) + rr * nbh,
-                                                recs + (size_t)pl * hrb, nbh);
+                                                recs + (size_t)pl * hrb, nbh, (C.r0 + rr) & 7);
                     if (L.y_in_smem)
                         ys[(size_t)pos * L.rpc_max + rr] = acc;
                     else

@@ -7,9 +7,11 @@
 // copy is 16-byte aligned for TMA and every row of nibbles is one contiguous run), and
 // interleaves gate and up rows per 32 columns:
 //   packed gate_up row R = q*64 + s*32 + i  holds  original row s*ff + q*32 + i,
-// and within a gate_up row the 16-byte nibble block b sits at position b ^ (R & 7) (so that
-// 32 threads reading block b of 32 consecutive rows hit distinct shared-memory banks; rows
-// hold a multiple of 8 blocks). Scales are not swizzled.
+// and within a packed row R (gate_up or down) the 16-byte nibble block b sits at position
+// nib_pos(b) = b ^ (R & 7) when b lies in a complete group of 8 blocks, at b otherwise (the
+// tail of a down row: 22 blocks per row for ff = 704), so that threads reading block b of 8
+// consecutive rows hit distinct shared-memory banks. Gate_up rows hold a multiple of 8
+// blocks. Scales are not swizzled.
 // Nibble bytes and scale bits are copied unchanged, so every dot product sees the same
 // integers and scales as the reference.
 #pragma once
@@ -25,6 +27,9 @@ struct PackedView {
     const uint16_t *dn_scl;  // [E][n_embd][nbh]
 };
 
+// Position of nibble block b in a packed row of nblk blocks whose row index has low bits key.
+__host__ __device__ __forceinline__ int nib_pos(int b, int nblk, int key) { return b < (nblk & ~7) ? (b ^ key) : b; }
+
 __global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int rows, int nblk, bool interleave_gu,
                           int ff, uint8_t *__restrict__ nib, uint16_t *__restrict__ scl) {
     const size_t total = (size_t)n_experts * rows * nblk;
@@ -39,8 +44,7 @@ __global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int ro
         }
         const uint8_t *blk = src + i * Q4_BLOCK;
         const size_t dst = (e * rows + prow) * nblk + b;
-        // gate/up nibble blocks are XOR-swizzled within a row: block b at position b ^ (prow & 7)
-        const size_t dnib = interleave_gu ? (e * rows + prow) * nblk + (b ^ (prow & 7)) : dst;
+        const size_t dnib = (e * rows + prow) * nblk + nib_pos((int)b, nblk, (int)(prow & 7));
         // 18-byte blocks are only 2-byte aligned: read as 9 halfwords
         const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
         uint32_t w[4];

@@ -480,7 +480,6 @@ struct PfArgs {
     const int *n_tiles;
     int rows_per_expert;  // 2 ff (gate/up) or n_embd (down)
     int nblk;             // K blocks (n_embd / 32 or ff / 32)
-    int swizzled;         // the nibble plane's blocks are XOR-swizzled per row (gate/up)
     const uint8_t *nib;   // weight nibbles [E][rows][nblk][16] (for the L2 prefetch; copies go through the map)
     const uint16_t *scl;  // weight scales [E][rows][nblk] (f16 bits)
     int nh;               // (gate/up) h blocks per pair (ff / 32): the h record geometry
@@ -719,9 +718,11 @@ __global__ void __launch_bounds__(PM_THREADS, 1) k_pf_gemm_ms(const __grid_const
                 const uint64_t dw[2][2] = {{f2_splat(w4.x), f2_splat(w4.y)}, {f2_splat(w4.z), f2_splat(w4.w)}};
                 // A: one ldmatrix gives each lane 4 nibble bytes of rows g, g + 8, 16 + g, 24 + g
                 // of the warp (lane L addresses row 8 (L >> 3) + (L & 7), whose swizzle key is
-                // L & 7), the byte columns 4 tq .. of their block-jb chunks
+                // L & 7), the byte columns 4 tq .. of their block-jb chunks. A stage of 8 blocks
+                // is one complete group, swizzled in the packed plane (nib_pos); a shorter last
+                // stage is the row's unswizzled tail.
                 uint32_t wq[4];
-                ldsm_x4(sN32 + a_row + ((a.swizzled ? (jb ^ (lane & 7)) : jb) << 4), wq);
+                ldsm_x4(sN32 + a_row + ((kn == PF_KB ? (jb ^ (lane & 7)) : jb) << 4), wq);
                 uint32_t af[2][4];
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {

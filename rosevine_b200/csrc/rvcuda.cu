@@ -234,7 +234,7 @@ __global__ void k_debug_block_sums(PackedView pk, int which, int expert, int n_e
             const int prow = (col / 32) * 64 + s * 32 + (col % 32);
             nibp = pk.gu_nib + (((size_t)expert * 2 * ff + prow) * nblk + (b ^ (prow & 7))) * 16;
         } else {
-            nibp = pk.dn_nib + (((size_t)expert * n_embd + row) * nblk + b) * 16;
+            nibp = pk.dn_nib + (((size_t)expert * n_embd + row) * nblk + nib_pos(b, nblk, row & 7)) * 16;
         }
         const uint4 nib = *reinterpret_cast<const uint4 *>(nibp);
         const uint8_t *xb = xq8 + ((size_t)t * nblk + b) * Q8_BLOCK + 2;
@@ -491,13 +491,13 @@ int pf_gemms(const rvc_moe_weights *w, const Workspace &L, void *ws, int n_pairs
     const int tiles_y = n_pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
     PfArgs g{};
     g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles);
-    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.swizzled = 1, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
+    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
     g.nh = nbh, g.hrec = hrec, g.hso = hso, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
     g.negzero2 = 0x8000000080000000ull;
     k_pf_gemm_ms<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
     if ((rc = launched())) return rc;
     PfArgs d = g;
-    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.swizzled = 0, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
+    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
     d.hrec = nullptr, d.hso = nullptr, d.y = at<float>(ws, L.ybuf);
     k_pf_gemm_ms<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
     return launched();
