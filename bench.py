@@ -324,13 +324,15 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
     for _ in range(args.warmup):
         fwd()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     # one sampler per node (local rank 0, its own GPU): several nvidia-smi processes polling at
     # once slow the expert-parallel step's host synchronisations
     clocks = ClockSampler(gpu_smi_id(local_rank)) if local_rank == 0 else None
     if clocks:
         clocks.start()
+    # the barrier after the sampler's start-up (up to a second on local rank 0): otherwise the
+    # other ranks' first timed step waits for it inside the all-to-all
+    if world > 1:
+        dist.barrier()
     step_ms, disp_ms, comb_ms = loop(args.steps, False)
     clk = clocks.stop() if clocks else None
     phases_main = dict(phases)
