@@ -182,6 +182,16 @@ int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, cons
                             const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
                             void *stream);
 
+/* Measurement hook (no counterpart in the reference): enqueue on `stream`, again, the two
+ * grouped expert GEMMs (gate/up with GELU and h quantisation, then down) of the last
+ * rvc_moe_forward call of more than 16 tokens enqueued with this workspace and these weights,
+ * on the plan, records and scale planes that call left in the workspace. The GEMMs rewrite the
+ * same h records and y, so the layer's outputs stay as they were. Lets a caller time the
+ * layer's dominant kernels alone with events on `stream`. Returns cudaErrorInvalidValue if no
+ * such call was made with this workspace and these weights. Calls on the workspace from other
+ * streams must be ordered by the caller, as for every entry point. */
+int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Test hook: the exact int32 Q4_0 x Q8_0 block sums the expert kernels form, for
  * `n_rows` rows of one expert of the packed weights against Q8_0 activation rows.
  * which: 0 = gate_up (original row numbering), 1 = down. xq8: device [n_in][nblk*34]

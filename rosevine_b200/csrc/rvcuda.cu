@@ -523,6 +523,35 @@ int pf_plan(const int32_t *pair_expert, int n_pairs, int ne, const Workspace &L,
 
 // The prefill layer (n_tok > 64): the reference-order router (logits, selection, plan), Q8_0
 // of x in plan order, the grouped GEMMs, the slot-order combine.
+// The token count of the last prefill call enqueued with each (workspace, weights) pair (host
+// side, for rvc_prefill_gemms): the grouped GEMMs may only be re-run on a workspace holding the
+// plan, records and scale planes of such a call, at that call's layout.
+struct LastPrefill {
+    const void *ws;
+    const rvc_moe_weights *w;
+    int n_tok;
+};
+std::mutex g_last_mu;
+LastPrefill g_last[64];
+int g_n_last = 0;
+
+void note_prefill(const void *ws, const rvc_moe_weights *w, int n_tok) {
+    std::lock_guard<std::mutex> lock(g_last_mu);
+    for (int i = 0; i < g_n_last; ++i)
+        if (g_last[i].ws == ws) {
+            g_last[i].w = w, g_last[i].n_tok = n_tok;
+            return;
+        }
+    if (g_n_last < 64) g_last[g_n_last++] = LastPrefill{ws, w, n_tok};
+}
+
+int last_prefill(const void *ws, const rvc_moe_weights *w) {
+    std::lock_guard<std::mutex> lock(g_last_mu);
+    for (int i = 0; i < g_n_last; ++i)
+        if (g_last[i].ws == ws) return g_last[i].w == w ? g_last[i].n_tok : 0;
+    return 0;
+}
+
 int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype, const float *bias,
                 int bias_stride, int n_tok, float *out, int32_t *ids, float *wts, void *ws, size_t ws_bytes,
                 cudaStream_t st) {
@@ -551,6 +580,7 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
     if ((rc = launched())) return rc;
     // 3. gate/up and down GEMMs
     if ((rc = pf_gemms(w, L, ws, pairs, st))) return rc;
+    note_prefill(ws, w, n_tok);
     // 4. slot-order combine
     k_pf_combine<<<n_tok, 256, 0, st>>>(at<float>(ws, L.ybuf), pos_of, id, wt, w->down_scale, used, w->n_embd, n_tok,
                                         out, at<int>(ws, L.status));
@@ -743,6 +773,14 @@ int rvc_moe_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype,
     if (ws_max_tok(workspace_bytes, w) < n_tok) return RVC_ERR_WORKSPACE;
     return run_decode(w, x_expert, x_expert, x_dtype, nullptr, 0, ids, wts, n_tok, out, nullptr, nullptr, workspace,
                       S(stream));
+}
+
+int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!dims_ok(w) || !workspace || !aligned(workspace, 256)) return (int)cudaErrorInvalidValue;
+    const int n_tok = last_prefill(workspace, w);
+    if (n_tok <= PF_MIN_TOK || ws_max_tok(workspace_bytes, w) < n_tok) return (int)cudaErrorInvalidValue;
+    Workspace L(n_tok, w->n_embd, w->ff, w->n_experts, w->used);
+    return pf_gemms(w, L, workspace, n_tok * w->used, S(stream));
 }
 
 int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,

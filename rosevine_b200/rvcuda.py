@@ -32,7 +32,7 @@ EXPORTS = [
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
     "rvc_debug_mma_i8", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
-    "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce",
+    "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms",
 ]
 
 
@@ -105,6 +105,7 @@ def lib() -> ctypes.CDLL:
             "rvc_ep_workspace_bytes": ([I, I, I, I, I], Z),
             "rvc_ep_experts": ([W, P, I, I, P, P, Z, P], I),
             "rvc_ep_reduce": ([P, P, I, I, I, P, P], I),
+            "rvc_prefill_gemms": ([W, P, Z, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -282,6 +283,13 @@ def moe_forward_noalloc(w: MoeWeights, x_router, x_expert, x_dtype: int, n_tok: 
                                         _ptr(bias, bias_rows * 4), bias_stride, n_tok,
                                         _ptr(out, n_tok * w.n_embd * 4), _ptr(ids, n_tok * w.used * 4),
                                         _ptr(wts, n_tok * w.used * 4), stream))
+
+
+def prefill_gemms(w: MoeWeights, workspace, stream: int | None = None) -> None:
+    """Re-enqueue the grouped GEMMs of the last prefill call made with this workspace and
+    these weights (rvc_prefill_gemms): for timing the layer's dominant kernels alone."""
+    ws = view_of(workspace)
+    check(lib().rvc_prefill_gemms(ctypes.byref(w), ws.ptr, ws.nbytes, stream))
 
 
 def workspace_reset(workspace, stream: int | None = None) -> None:

@@ -97,3 +97,23 @@ def test_prefill_zipf_groups(weights, oracle, pool):
     got = out.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
         f"max abs diff {np.abs(got - want).max():.3e}"
+
+
+def test_prefill_gemms_rerun_leaves_workspace_unchanged(weights):
+    """rvc_prefill_gemms re-runs the last prefill call's grouped GEMMs on its plan and records
+    (bench.py times them this way): they rewrite the same h records, scales and y, so the whole
+    workspace is byte-identical afterwards; a workspace without such a call is refused."""
+    from rosevine_b200 import rvcuda as rc
+    from rosevine_b200 import synth
+    from rosevine_b200.moe import MoeLayer, to_device_x
+    lyr = MoeLayer(weights["w_router"], weights["gate_up"], weights["down"], max_tok=300)
+    with pytest.raises(rc.DeviceError):
+        rc.prefill_gemms(lyr.w, lyr.ws)
+    lyr.forward(to_device_x(synth.tokens(300, 1300), "cuda"))
+    torch.cuda.synchronize()
+    before = lyr.ws.clone()
+    rc.prefill_gemms(lyr.w, lyr.ws)
+    rc.prefill_gemms(lyr.w, lyr.ws)
+    torch.cuda.synchronize()
+    assert torch.equal(lyr.ws, before)
+    lyr.status()
