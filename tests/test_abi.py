@@ -76,6 +76,16 @@ def test_invalid_scalars_rejected_without_device_work(lib):
     assert lib.rvc_moe_forward(ctypes.byref(w5), odd, q, rc.BF16, None, 0, 1, q, None, None, q, 1 << 20, None) == 1
 
 
+def test_prefill_gemms_needs_a_prior_prefill_call(lib):
+    """rvc_prefill_gemms re-runs a prefill call's GEMMs on its workspace; a workspace that never
+    held one (as here) is refused on the host, before any device work."""
+    w = rc.MoeWeights(2816, 704, 128, 8, rc.BF16, 4096, 4096, None)
+    p = ctypes.c_void_p(4096)  # aligned, never dereferenced
+    big = rc.workspace_bytes(64, 2816, 704, 128, 8)
+    assert lib.rvc_prefill_gemms(ctypes.byref(w), p, big, None) == 1
+    assert lib.rvc_prefill_gemms(None, p, big, None) == 1
+
+
 def test_workspace_too_small_is_rejected(lib):
     w = rc.MoeWeights(2816, 704, 128, 8, rc.BF16, 4096, 4096, None)
     p = ctypes.c_void_p(4096)  # aligned, never dereferenced: the size check fails first
