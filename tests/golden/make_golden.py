@@ -1,7 +1,7 @@
 """Generate tests/golden/golden_v1.json from the reference's binary64 scalar oracle.
 
 Runs Rosevine's own independent reference math, scripts/correctness_oracle.py (imported from a
-Rosevine checkout given by --reference, default /root/reference), and its scalar operator
+Rosevine checkout given by --reference), and its scalar operator
 fixture research/fixtures/scalar-operators-v1.json, on seeded inputs, and writes the results as
 a small JSON fixture. The committed fixture is what the tests read; the reference checkout is
 only needed to regenerate it:
@@ -37,7 +37,7 @@ def f16_bytes(v: float) -> bytes:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of a Rosevine checkout")
     ap.add_argument("--out", default=os.path.join(HERE, "golden_v1.json"))
     args = ap.parse_args()
     C, fixture = load_reference(args.reference)
