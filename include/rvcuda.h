@@ -188,8 +188,9 @@ int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, cons
  * on the plan, records and scale planes that call left in the workspace. The GEMMs rewrite the
  * same h records and y, so the layer's outputs stay as they were. Lets a caller time the
  * layer's dominant kernels alone with events on `stream`. Returns cudaErrorInvalidValue if no
- * such call was made with this workspace and these weights. Calls on the workspace from other
- * streams must be ordered by the caller, as for every entry point. */
+ * such call was made with this workspace and these weights, or if any other entry point has
+ * been given the workspace since (rvc_workspace_reset included). Calls on the workspace from
+ * other streams must be ordered by the caller, as for every entry point. */
 int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Test hook: the exact int32 Q4_0 x Q8_0 block sums the expert kernels form, for

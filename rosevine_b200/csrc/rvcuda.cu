@@ -545,6 +545,17 @@ void note_prefill(const void *ws, const rvc_moe_weights *w, int n_tok) {
     if (g_n_last < 64) g_last[g_n_last++] = LastPrefill{ws, w, n_tok};
 }
 
+// Any other use of a workspace (another layout written over it, a reset, a new owner of the
+// same address) ends what rvc_prefill_gemms may re-run on it.
+void forget_prefill(const void *ws) {
+    std::lock_guard<std::mutex> lock(g_last_mu);
+    for (int i = 0; i < g_n_last; ++i)
+        if (g_last[i].ws == ws) {
+            g_last[i] = g_last[--g_n_last];
+            return;
+        }
+}
+
 int last_prefill(const void *ws, const rvc_moe_weights *w) {
     std::lock_guard<std::mutex> lock(g_last_mu);
     for (int i = 0; i < g_n_last; ++i)
@@ -737,6 +748,7 @@ size_t rvc_moe_workspace_bytes(int max_tok, int n_embd, int ff, int n_experts, i
 int rvc_moe_router(const rvc_moe_weights *w, const void *x, int x_dtype, const float *bias, int bias_stride,
                    int n_tok, int32_t *ids, float *wts, int32_t *hist, int32_t *perm, float *logits, void *workspace,
                    size_t workspace_bytes, void *stream) {
+    forget_prefill(workspace);
     if (!dims_ok(w) || !x || n_tok <= 0 || !workspace || bias_stride < 0 || !aligned(x, 16) ||
         !aligned(workspace, 256) || (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
@@ -767,6 +779,7 @@ int rvc_moe_router(const rvc_moe_weights *w, const void *x, int x_dtype, const f
 
 int rvc_moe_experts(const rvc_moe_weights *w, const void *x_expert, int x_dtype, const int32_t *ids,
                     const float *wts, int n_tok, float *out, void *workspace, size_t workspace_bytes, void *stream) {
+    forget_prefill(workspace);
     if (!dims_ok(w) || !x_expert || !ids || !wts || !out || n_tok <= 0 || !workspace || !aligned(x_expert, 16) ||
         !aligned(workspace, 256) || (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
         return (int)cudaErrorInvalidValue;
@@ -786,6 +799,7 @@ int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspac
 int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *x_expert, int x_dtype,
                     const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
                     void *workspace, size_t workspace_bytes, void *stream) {
+    forget_prefill(workspace);  // a prefill call notes the workspace again once its GEMMs are enqueued
     if (!dims_ok(w) || !x_router || !x_expert || !out || n_tok <= 0 || !workspace || bias_stride < 0 ||
         !aligned(x_router, 16) || !aligned(x_expert, 16) || !aligned(workspace, 256) ||
         (x_dtype != RVC_F32 && x_dtype != RVC_BF16))
@@ -799,6 +813,7 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
 }
 
 int rvc_workspace_reset(void *workspace, void *stream) {
+    forget_prefill(workspace);
     if (!workspace) return (int)cudaErrorInvalidValue;
     return (int)cudaMemsetAsync(workspace, 0, 256, S(stream));
 }
@@ -851,6 +866,7 @@ size_t rvc_ep_workspace_bytes(int max_rows, int used, int n_embd, int ff, int n_
 
 int rvc_ep_experts(const rvc_moe_weights *w, const void *rows, int n_rows, int used, float *partial, void *workspace,
                    size_t workspace_bytes, void *stream) {
+    forget_prefill(workspace);
     if (!dims_ok(w) || n_rows < 0 || used <= 0 || used > MAX_USED || !workspace || !aligned(workspace, 256) ||
         (n_rows > 0 && (!rows || !partial || !aligned(rows, 16) || !aligned(partial, 16))))
         return (int)cudaErrorInvalidValue;

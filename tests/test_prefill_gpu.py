@@ -102,7 +102,8 @@ def test_prefill_zipf_groups(weights, oracle, pool):
 def test_prefill_gemms_rerun_leaves_workspace_unchanged(weights):
     """rvc_prefill_gemms re-runs the last prefill call's grouped GEMMs on its plan and records
     (bench.py times them this way): they rewrite the same h records, scales and y, so the whole
-    workspace is byte-identical afterwards; a workspace without such a call is refused."""
+    workspace is byte-identical afterwards; a workspace without such a call, or reset since, is
+    refused."""
     from rosevine_b200 import rvcuda as rc
     from rosevine_b200 import synth
     from rosevine_b200.moe import MoeLayer, to_device_x
@@ -117,3 +118,6 @@ def test_prefill_gemms_rerun_leaves_workspace_unchanged(weights):
     torch.cuda.synchronize()
     assert torch.equal(lyr.ws, before)
     lyr.status()
+    rc.workspace_reset(lyr.ws)  # any other use of the workspace ends what may be re-run on it
+    with pytest.raises(rc.DeviceError):
+        rc.prefill_gemms(lyr.w, lyr.ws)
