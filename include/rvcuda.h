@@ -118,7 +118,6 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
                     const float *bias, int bias_stride, int n_tok, float *out, int32_t *ids, float *wts,
                     void *workspace, size_t workspace_bytes, void *stream);
 
-/* Zero the workspace's status word (call once after allocating a workspace). */
 /* ---------------------------------------------------------------- expert parallelism
  * No reference counterpart: the reference runs every expert on one device. Rank r of N holds
  * experts [r n_local, (r + 1) n_local). A rank routes its own tokens (rvc_moe_router), quantises
@@ -160,6 +159,7 @@ int rvc_ep_experts(const rvc_moe_weights *w, const void *rows, int n_rows, int u
 int rvc_ep_reduce(const float *back, const int32_t *owner_map, int n_tok, int world, int n_embd, float *out,
                   void *stream);
 
+/* Zero the workspace's status word (call once after allocating a workspace). */
 int rvc_workspace_reset(void *workspace, void *stream);
 
 /* Synchronise `stream`, then read and clear the workspace's device status word:
@@ -200,11 +200,17 @@ int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspac
 int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,
                          const void *xq8, int n_in, int32_t *out, void *stream);
 
-/* Test hook: one tensor-core tile through the shared-memory layouts and tensor-memory reads
- * the prefill GEMM uses: d[128][n] = a[128][32] . b[n][32]^T, int8 inputs (device, row-major,
- * 16-byte aligned), int32 output. n = 16 .. 128, a multiple of 16. status: device int, a
- * bounded wait that ran out sets bit 1. */
-int rvc_debug_mma_i8(const int8_t *a, const int8_t *b, int n, int32_t *d, int *status, void *stream);
+/* Test hook (no counterpart in the reference): the int32 block dots of one tile of the prefill
+ * GEMM, formed by the production kernel (k_pf_gemm_tc: TMA copies, nibble unpack, tcgen05.mma
+ * kind::i8 into tensor memory, tensor-memory loads) in a mode whose epilogue writes the dots
+ * instead of scaling them. The tile: rows row_tile*128 .. +127 of expert `expert`'s gate_up
+ * (which = 0; packed row order, gate and up interleaved per 32 rows) or down (which = 1) rows,
+ * against n (1..128) Q8_0 records (rvc_q8_record_bytes layout over n_embd (which = 0) or ff
+ * (which = 1) columns; device, 16-byte aligned). out: device int32 [nblk][128 positions][128
+ * rows]; positions >= n read 0. scratch: device, 256-byte aligned, at least 256 + nblk * 4 *
+ * round_up(n, 4) bytes; its int at byte 12 receives the kernel's status bits. */
+int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, int row_tile, const void *records,
+                              int n, int32_t *out, void *scratch, size_t scratch_bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -16,6 +16,7 @@
 #include "decode_fused.cuh"
 #include "pack.cuh"
 #include "prefill.cuh"
+#include "prefill_tc.cuh"
 
 #include <cudaTypedefs.h>
 #include "router.cuh"
@@ -104,8 +105,8 @@ struct Workspace {
         ybuf = take(ppos * n_embd * 4);
         // prefill calls only
         xperm = prefill ? take(ppos * q8rec_bytes((int)nb)) : o;
-        xd = prefill ? take(nb * ppad * 8) : o;   // (scale, offset) f32 pairs, block-major
-        hd = prefill ? take(nbh * ppad * 8) : o;
+        xd = prefill ? take(nb * ppad * 4) : o;   // x block scales, f32, block-major
+        hd = prefill ? take(nbh * ppad * 4) : o;  // h block scales
         tiles = prefill ? take((pairs / 128 + 1 + (size_t)ne) * 8) : o;
         n_tiles = take(4);
         plan = take(fd_plan_words(std::min(max_tok, FD_MAX_TOK) * used, ne) * 4);
@@ -462,50 +463,65 @@ int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-// Gate/up and down GEMMs over the plan positions already filled (xperm records, xso pairs):
+// The grouped GEMM's tensor maps: weight nibbles [rows][blocks][16 B]; activation quants as
+// [K halves][positions][16 B] (a tile's positions contiguous per K half: the MMA's K-major B
+// layout); activation block scales [blocks][positions] f32.
+struct TcMaps {
+    CUtensorMap nib, act, dx;
+};
+
+int tc_maps(TcMaps *m, const uint8_t *nib, int n_rows, int nblk, const uint8_t *rec, int rec_bytes, int ppos,
+            const float *scales, int ppad) {
+    int rc;
+    if ((rc = map3d(&m->nib, nib, 16, nblk, (uint64_t)n_rows, 16, (uint64_t)nblk * 16, 16, TC_KB, TC_M)) ||
+        (rc = map3d(&m->act, rec, 16, ppos, 2 * nblk, rec_bytes, 16, 16, TC_N, 2 * TC_KB)) ||
+        (rc = map2d(&m->dx, scales, (uint64_t)ppad, nblk, (uint64_t)ppad * 4, TC_N, TC_KB,
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+        return rc;
+    return 0;
+}
+
+template <int MODE>
+int launch_tc(const TcMaps &m, const TcArgs &g, int max_units, cudaStream_t st) {
+    size_t smax = 0;
+    int rc;
+    if ((rc = fd_smem_max(k_pf_gemm_tc<MODE>, &smax))) return rc;
+    if (smax < (size_t)TC_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
+    const int grid = std::max(1, std::min(num_sms(), max_units));  // persistent: one CTA per SM
+    k_pf_gemm_tc<MODE><<<grid, TC_THREADS, TC_SMEM_BYTES, st>>>(m.nib, m.act, m.dx, g);
+    return launched();
+}
+
+// Gate/up and down GEMMs over the plan positions already filled (xperm records, x scale plane):
 // y [positions][n_embd] in the workspace.
 int pf_gemms(const rvc_moe_weights *w, const Workspace &L, void *ws, int n_pairs, cudaStream_t st) {
     int rc;
     const int ne = w->n_experts, nb = w->n_embd / QK, nbh = w->ff / QK;
     const PackedView pk = packed_view(w);
     uint8_t *xperm = at<uint8_t>(ws, L.xperm), *hrec = at<uint8_t>(ws, L.hrec);
-    float2 *xso = at<float2>(ws, L.xd), *hso = at<float2>(ws, L.hd);
+    float *xsc = at<float>(ws, L.xd), *hsc = at<float>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
-    CUtensorMap m_gu, m_x, m_xd, m_dn, m_h, m_hd;
-    const int xrb = q8rec_bytes(nb), hrb = q8rec_bytes(nbh);
-    // weight nibbles [rows][blocks][16 B]; activation quants as [halves][positions][16 B] (a
-    // chunk's positions contiguous: the canonical K-major layout); activation (scale, offset)
-    // pairs [blocks][positions][2] f32
-    if ((rc = map3d(&m_gu, pk.gu_nib, 16, nb, (uint64_t)ne * 2 * w->ff, 16, (uint64_t)nb * 16, 16, PF_KB, PF_M)) ||
-        (rc = map3d(&m_x, xperm, 16, ppos, 2 * nb, xrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_xd, xso, 2 * (uint64_t)ppad, nb, (uint64_t)ppad * 8, 2 * PF_N, PF_KB,
-                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
-        (rc = map3d(&m_dn, pk.dn_nib, 16, nbh, (uint64_t)ne * w->n_embd, 16, (uint64_t)nbh * 16, 16, PF_KB, PF_M)) ||
-        (rc = map3d(&m_h, hrec, 16, ppos, 2 * nbh, hrb, 16, 16, PF_N, 2 * PF_KB)) ||
-        (rc = map2d(&m_hd, hso, 2 * (uint64_t)ppad, nbh, (uint64_t)ppad * 8, 2 * PF_N, PF_KB,
-                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+    TcMaps mg, md;
+    if ((rc = tc_maps(&mg, pk.gu_nib, ne * 2 * w->ff, nb, xperm, q8rec_bytes(nb), ppos, xsc, ppad)) ||
+        (rc = tc_maps(&md, pk.dn_nib, ne * w->n_embd, nbh, hrec, q8rec_bytes(nbh), ppos, hsc, ppad)))
         return rc;
-    size_t smax = 0;
-    if ((rc = fd_smem_max(k_pf_gemm_ms<PF_GU>, &smax)) || (rc = fd_smem_max(k_pf_gemm_ms<PF_DN>, &smax))) return rc;
-    if (smax < (size_t)PM_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
-    const int tiles_y = n_pairs / PF_N + 1 + ne;  // an upper bound on the (expert, token tile) count
-    PfArgs g{};
-    g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles);
-    g.rows_per_expert = 2 * w->ff, g.nblk = nb, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
-    g.nh = nbh, g.hrec = hrec, g.hso = hso, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
+    const int tiles_max = n_pairs / TC_N + 1 + ne;  // an upper bound on the (expert, position tile) count
+    TcArgs g{};
+    g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles), g.max_tiles = tiles_max;
+    g.n_experts = ne, g.ppos = ppos, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
+    g.rows_per_expert = 2 * w->ff, g.row_tiles = 2 * w->ff / TC_M, g.nblk = nb, g.scl = pk.gu_scl;
+    g.nh = nbh, g.hrec = hrec, g.hsc = hsc;
     g.negzero2 = 0x8000000080000000ull;
-    k_pf_gemm_ms<PF_GU><<<dim3(2 * w->ff / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_gu, m_x, m_xd, g);
-    if ((rc = launched())) return rc;
-    PfArgs d = g;
-    d.rows_per_expert = w->n_embd, d.nblk = nbh, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
-    d.hrec = nullptr, d.hso = nullptr, d.y = at<float>(ws, L.ybuf);
-    k_pf_gemm_ms<PF_DN><<<dim3(w->n_embd / PF_M, tiles_y), PM_THREADS, PM_SMEM_BYTES, st>>>(m_dn, m_h, m_hd, d);
-    return launched();
+    if ((rc = launch_tc<PF_GU>(mg, g, tiles_max * g.row_tiles, st))) return rc;
+    TcArgs d = g;
+    d.rows_per_expert = w->n_embd, d.row_tiles = w->n_embd / TC_M, d.nblk = nbh, d.scl = pk.dn_scl;
+    d.hrec = nullptr, d.hsc = nullptr, d.y = at<float>(ws, L.ybuf);
+    return launch_tc<PF_DN>(md, d, tiles_max * d.row_tiles, st);
 }
 
 int pf_supported(const rvc_moe_weights *w) {
     const int nb = w->n_embd / QK;
-    if (nb % PF_KB || (2 * w->ff) % PF_M || w->n_embd % PF_M || w->n_experts > MAX_EXPERTS || w->used > MAX_USED)
+    if (nb % TC_KB || (2 * w->ff) % TC_M || w->n_embd % TC_M || w->n_experts > MAX_EXPERTS || w->used > MAX_USED)
         return RVC_ERR_UNSUPPORTED;
     return tensor_map_encode();
 }
@@ -517,7 +533,7 @@ int pf_plan(const int32_t *pair_expert, int n_pairs, int ne, const Workspace &L,
     k_plan<<<1, PLAN_THREADS, 0, st>>>(pair_expert, n_pairs, ne, at<int32_t>(ws, L.counts), at<int32_t>(ws, L.offsets),
                                        at<int32_t>(ws, L.order), at<int32_t>(ws, L.pos_of), at<int32_t>(ws, L.active),
                                        at<int32_t>(ws, L.n_active), at<int>(ws, L.status), 4, at<int2>(ws, L.tiles),
-                                       at<int32_t>(ws, L.n_tiles), PF_N, false, skip_empty);
+                                       at<int32_t>(ws, L.n_tiles), TC_N, false, skip_empty);
     return launched();
 }
 
@@ -580,13 +596,13 @@ int run_prefill(const rvc_moe_weights *w, const void *x_router, const void *x_ex
         return rc;
     // 2. Q8_0 of x, once per token, to its plan positions
     uint8_t *xperm = at<uint8_t>(ws, L.xperm);
-    float2 *xso = at<float2>(ws, L.xd);
+    float *xsc = at<float>(ws, L.xd);
     const int qblocks = (n_tok * ((nb + 7) / 8) + 7) / 8;  // one warp per 8 blocks of a token
     if (x_dtype == RVC_BF16)
         k_pf_quant<uint16_t><<<qblocks, 256, 0, st>>>((const uint16_t *)x_expert, w->n_embd, n_tok, used, pos_of, xperm,
-                                                      xso, (int)L.ppad);
+                                                      xsc, (int)L.ppad);
     else
-        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xso,
+        k_pf_quant<float><<<qblocks, 256, 0, st>>>((const float *)x_expert, w->n_embd, n_tok, used, pos_of, xperm, xsc,
                                                    (int)L.ppad);
     if ((rc = launched())) return rc;
     // 3. gate/up and down GEMMs
@@ -652,7 +668,10 @@ int rvc_alloc(size_t bytes, void **out) {
     return (int)cudaMalloc(out, bytes ? bytes : 1);
 }
 
-int rvc_free(void *ptr) { return ptr ? (int)cudaFree(ptr) : 0; }
+int rvc_free(void *ptr) {
+    forget_prefill(ptr);  // a later allocation may reuse the address: nothing is left to re-run there
+    return ptr ? (int)cudaFree(ptr) : 0;
+}
 
 int rvc_upload(void *dst, const void *src, size_t bytes) {
     return (int)cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
@@ -886,7 +905,7 @@ int rvc_ep_experts(const rvc_moe_weights *w, const void *rows, int n_rows, int u
     const long long tasks = (long long)n_rows * nb;
     k_ep_scatter<<<(int)std::min<long long>(16 * num_sms(), (tasks + 7) / 8), 256, 0, st>>>(
         (const uint8_t *)rows, nb, n_rows, used, slot_e, at<int32_t>(workspace, L.pos_of), at<uint8_t>(workspace, L.xperm),
-        at<float2>(workspace, L.xd), (int)L.ppad);
+        at<float>(workspace, L.xd), (int)L.ppad);
     if ((rc = launched()) || (rc = pf_gemms(w, L, workspace, n_pairs, st))) return rc;
     k_pf_combine<<<n_rows, 256, 0, st>>>(at<float>(workspace, L.ybuf), at<int32_t>(workspace, L.pos_of), slot_e, slot_w,
                                          w->down_scale, used, w->n_embd, n_rows, partial, at<int>(workspace, L.status));
@@ -919,11 +938,37 @@ int rvc_status(void *workspace, void *stream) {
     return 0;
 }
 
-int rvc_debug_mma_i8(const int8_t *a, const int8_t *b, int n, int32_t *d, int *status, void *stream) {
-    if (!a || !b || !d || n < 16 || n > PF_N || n % 16 || !aligned(a, 16) || !aligned(b, 16))
+int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, int row_tile, const void *records,
+                              int n, int32_t *out, void *scratch, size_t scratch_bytes, void *stream) {
+    if (!dims_ok(w) || (which != 0 && which != 1) || expert < 0 || expert >= w->n_experts || !records || n < 1 ||
+        n > TC_N || !out || !scratch || !aligned(records, 16) || !aligned(scratch, 256))
         return (int)cudaErrorInvalidValue;
-    k_debug_mma_i8<<<1, 128, 0, S(stream)>>>(a, b, n, d, status);
-    return launched();
+    int rc;
+    if ((rc = pf_supported(w))) return rc;
+    const int rows = which == 0 ? 2 * w->ff : w->n_embd, nblk = (which == 0 ? w->n_embd : w->ff) / QK;
+    if (row_tile < 0 || row_tile >= rows / TC_M) return (int)cudaErrorInvalidValue;
+    const int ppad = (n + 3) / 4 * 4;
+    // scratch: the one-entry tile list and its count, then an (unused) scale plane
+    if (scratch_bytes < 256 + (size_t)nblk * ppad * 4) return RVC_ERR_WORKSPACE;
+    cudaStream_t st = S(stream);
+    const int2 tile = make_int2(expert | (n << 8), 0);
+    const int hdr[4] = {tile.x, tile.y, 1, 0};
+    if ((rc = (int)cudaMemcpyAsync(scratch, hdr, sizeof hdr, cudaMemcpyHostToDevice, st))) return rc;
+    if ((rc = (int)cudaMemsetAsync(static_cast<uint8_t *>(scratch) + 256, 0, (size_t)nblk * ppad * 4, st))) return rc;
+    const PackedView pk = packed_view(w);
+    TcMaps m;
+    if ((rc = tc_maps(&m, which == 0 ? pk.gu_nib : pk.dn_nib, w->n_experts * rows, nblk, (const uint8_t *)records,
+                      q8rec_bytes(nblk), n, reinterpret_cast<const float *>(static_cast<uint8_t *>(scratch) + 256),
+                      ppad)))
+        return rc;
+    TcArgs g{};
+    g.tiles = static_cast<const int2 *>(scratch), g.n_tiles = static_cast<const int *>(scratch) + 2, g.max_tiles = 1;
+    g.n_experts = w->n_experts, g.ppos = n, g.ppad = ppad, g.n_embd = w->n_embd;
+    g.status = static_cast<int *>(scratch) + 3;
+    g.rows_per_expert = rows, g.row_tiles = 1, g.row_base = row_tile * TC_M, g.nblk = nblk;
+    g.scl = which == 0 ? pk.gu_scl : pk.dn_scl;
+    g.y = reinterpret_cast<float *>(out);
+    return launch_tc<PF_RAW>(m, g, 1, st);
 }
 
 int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,

@@ -31,7 +31,7 @@ EXPORTS = [
     "rvc_event_elapsed", "rvc_upload_async", "rvc_download_async", "rvc_event_record_on", "rvc_stream_sync",
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
-    "rvc_debug_mma_i8", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
+    "rvc_debug_gemm_block_dots", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
     "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms",
 ]
 
@@ -97,7 +97,7 @@ def lib() -> ctypes.CDLL:
             "rvc_status": ([P, P], I),
             "rvc_debug_block_sums": ([W, I, I, P, I, P, I, P, P], I),
             "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
-            "rvc_debug_mma_i8": ([P, P, I, P, P, P], I),
+            "rvc_debug_gemm_block_dots": ([W, I, I, I, P, I, P, P, Z, P], I),
             "rvc_q8_record_bytes": ([I], Z),
             "rvc_ep_row_bytes": ([I, I], Z),
             "rvc_quant_q8_rows": ([P, I, I, I, P, P], I),
@@ -307,13 +307,18 @@ def debug_block_sums(w: MoeWeights, which: int, expert: int, rows, n_rows: int, 
                                      _ptr(xq8, n_in * nblk * 34), n_in, _ptr(out, n_in * n_rows * nblk * 4), stream))
 
 
-def debug_mma_i8(a, b, n: int, d, status, stream: int | None = None) -> None:
-    """d[128][n] = a[128][32] . b[n][32]^T through one tensor-core tile (int8 in, int32 out)."""
-    check(lib().rvc_debug_mma_i8(_ptr(a, 128 * 32), _ptr(b, n * 32), n, _ptr(d, 128 * n * 4), _ptr(status, 4),
-                                 stream))
+def debug_gemm_block_dots(w: MoeWeights, which: int, expert: int, row_tile: int, records, n: int, out, scratch,
+                          stream: int | None = None) -> None:
+    """int32 block dots of one prefill-GEMM tile from the production tensor-core kernel:
+    out [nblk][128 positions][128 rows] int32 (rvc_debug_gemm_block_dots)."""
+    k = w.n_embd if which == 0 else w.ff
+    nblk = k // 32
+    sv = view_of(scratch)
+    check(lib().rvc_debug_gemm_block_dots(ctypes.byref(w), which, expert, row_tile, _ptr(records, n * (k // 32) * 40),
+                                          n, _ptr(out, nblk * 128 * 128 * 4), sv.need(256 + nblk * 4 * ((n + 3) // 4 * 4)),
+                                          sv.nbytes, stream))
 
 
-# -------------------------------------------------------------- expert parallelism
 def q8_record_bytes(n_embd: int) -> int:
     return lib().rvc_q8_record_bytes(n_embd)
 

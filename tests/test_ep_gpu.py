@@ -99,8 +99,9 @@ def test_ep_multi_rank(oracle, pool, hot):
     got, ids = _run(world, n_tok, hot)
     want, want_ids = _want(oracle, pool, n_tok, hot)
     assert np.array_equal(ids, want_ids)
-    err = np.abs(got - want).max() / np.abs(want).max()
-    assert err <= EP_RTOL, err
+    # per row, as the north star's bar: max |gpu - cpu| over the row / max |cpu| over the row
+    err = np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)
+    assert err.max() <= EP_RTOL, f"max row rel err {err.max():.3e} (row {int(err.argmax())})"
 
 
 def synth_experts():

@@ -1,11 +1,12 @@
 """GPU parity of the prefill path (batches above 16 tokens: the grouped expert GEMMs).
 
-The first test checks one tensor-core tile (the tcgen05.mma kind::i8 debug kernel, through the
-shared-memory layouts and tensor-memory reads) against numpy's int32 product. The layer tests
-compare rvc_moe_forward with the oracle's scalar kernel: the router runs in the reference's
-order, the int32 block dots come from the tensor cores (mma.sync) exactly, and the epilogue
-accumulates them in the scalar reference's order with separately rounded operations, so ids,
-weights and the output are bit-identical.
+The grouped GEMM (k_pf_gemm_tc) forms each 32-column block's int32 dot on the tensor cores
+(tcgen05.mma kind::i8 into tensor memory) and scales and accumulates the dots on the CUDA cores
+in the scalar reference's order, each operation rounded where the reference rounds it
+(expert_kernel.rs:147-161). The first tests read the block dots of one tile straight from the
+production kernel (its debug mode writes them instead of scaling them) and compare them with the
+exact integer dots; the layer tests compare rvc_moe_forward with the oracle's scalar kernel:
+ids, weights and the output are bit-identical.
 """
 import numpy as np
 import pytest
@@ -15,20 +16,67 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n", [16, 48, 128])
-def test_tensor_core_tile_exact(n):
+def _records(xq: np.ndarray) -> np.ndarray:
+    """Reference Q8_0 rows (34-byte blocks: f16 d, 32 int8) -> this backend's records (per block
+    32 int8, then the f32 scales, then the int32 quant sums)."""
+    n, nb = xq.shape[0], xq.shape[1] // 34
+    blk = xq.reshape(n, nb, 34)
+    q = blk[:, :, 2:].copy()
+    d = blk[:, :, :2].copy().view(np.float16).reshape(n, nb).astype(np.float32)
+    sums = q.view(np.int8).astype(np.int32).sum(axis=2, dtype=np.int32)
+    return np.concatenate([q.reshape(n, -1), d.view(np.uint8).reshape(n, -1), sums.view(np.uint8).reshape(n, -1)],
+                          axis=1)
+
+
+def _block_dots_want(mat: np.ndarray, xq: np.ndarray) -> np.ndarray:
+    """Exact int32 block dots [nblk][n][rows] of Q4_0 rows mat [rows][nblk*18] with Q8_0 rows."""
+    rows, n = mat.shape[0], xq.shape[0]
+    nb = mat.shape[1] // 18
+    nib = mat.reshape(rows, nb, 18)[:, :, 2:]
+    w = np.concatenate([(nib & 15).astype(np.int64) - 8, (nib >> 4).astype(np.int64) - 8], axis=2)  # [r][b][32]
+    x = xq.reshape(n, nb, 34)[:, :, 2:].view(np.int8).astype(np.int64)                               # [n][b][32]
+    return np.einsum("rbk,nbk->bnr", w, x).astype(np.int32)
+
+
+@pytest.mark.parametrize("which,expert,row_tile,n,extreme", [(0, 3, 0, 128, False), (0, 77, 10, 37, True),
+                                                             (1, 5, 21, 128, False), (1, 127, 7, 64, True)])
+def test_gemm_block_dots_bit_exact(layer, weights, oracle, which, expert, row_tile, n, extreme):
+    """The production GEMM's int32 block dots for one tile (row_tile: 128 packed rows; gate_up
+    rows interleave gate and up per 32) against the exact integer dots, pinned to the oracle's
+    block_sumi on a sample. Extreme: every quant +-127, the largest |dot| the formats allow."""
     from rosevine_b200 import rvcuda as rc
-    rng = np.random.default_rng(n)
-    a = rng.integers(-128, 128, size=(128, 32), dtype=np.int8)
-    b = rng.integers(-128, 128, size=(n, 32), dtype=np.int8)
-    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
-    d = torch.zeros((128, n), dtype=torch.int32, device="cuda")
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc.debug_mma_i8(da, db, n, d, status)
+    rng = np.random.default_rng(100 * which + expert)
+    k = layer.n_embd if which == 0 else layer.ff
+    nb = k // 32
+    if extreme:
+        xq = np.zeros((n, nb * 34), np.uint8)
+        for t in range(n):
+            for b in range(nb):
+                xq[t, 34 * b:34 * b + 2] = np.frombuffer(np.float16(0.5).tobytes(), np.uint8)
+                xq[t, 34 * b + 2:34 * b + 34] = 0x81 if (t + b) % 2 else 0x7F
+    else:
+        xq = oracle.quantize_q8_0(rng.standard_normal((n, k)).astype(np.float32))
+    src = weights["gate_up"] if which == 0 else weights["down"]
+    rows_total = 2 * layer.ff if which == 0 else layer.n_embd
+    mat = src[expert].reshape(rows_total, nb * 18)
+    packed = np.arange(row_tile * 128, row_tile * 128 + 128)
+    if which == 0:  # packed row R = q 64 + s 32 + i holds original row s ff + q 32 + i
+        orig = (packed % 64 // 32) * layer.ff + (packed // 64) * 32 + packed % 32
+    else:
+        orig = packed
+    want = _block_dots_want(mat[orig], xq)
+    for b, t, r in [(0, 0, 0), (nb - 1, n - 1, 127), (nb // 2, n // 2, 64)]:
+        assert want[b, t, r] == oracle.block_sumi(mat[orig[r], 18 * b:18 * b + 18], xq[t, 34 * b:34 * b + 34])
+    rec = torch.from_numpy(_records(xq)).cuda()
+    out = torch.full((nb, 128, 128), -1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(256 + nb * 4 * 128, dtype=torch.uint8, device="cuda")
+    rc.debug_gemm_block_dots(layer.w, which, expert, row_tile, rec, n, out, scratch)
     torch.cuda.synchronize()
-    assert int(status.item()) == 0
-    want = a.astype(np.int32) @ b.astype(np.int32).T
-    assert np.array_equal(d.cpu().numpy(), want)
+    assert int(scratch[12:16].view(torch.int32).item()) == 0, "device status set"
+    got = out.cpu().numpy()
+    assert np.array_equal(got[:, :n, :], want)
+    end = (n + 31) // 32 * 32  # the rest of the last loaded 32-position chunk: zero-filled operands
+    assert not got[:, n:end, :].any()
 
 
 @pytest.fixture(scope="module")
@@ -121,3 +169,27 @@ def test_prefill_gemms_rerun_leaves_workspace_unchanged(weights):
     rc.workspace_reset(lyr.ws)  # any other use of the workspace ends what may be re-run on it
     with pytest.raises(rc.DeviceError):
         rc.prefill_gemms(lyr.w, lyr.ws)
+
+
+def test_prefill_gemms_refused_after_free(weights):
+    """A workspace freed through rvc_free ends what rvc_prefill_gemms may re-run on it, even
+    when the next allocation gets the same address."""
+    from rosevine_b200 import rvcuda as rc
+    from rosevine_b200 import synth
+    from rosevine_b200.moe import MoeLayer, to_device_x
+    lyr = MoeLayer(weights["w_router"], weights["gate_up"], weights["down"], max_tok=100)
+    nbytes = rc.workspace_bytes(100, 2816, 704, 128, 8)
+    ws = rc.DevBuf(nbytes)
+    rc.workspace_reset(ws.view())
+    x = to_device_x(synth.tokens(100, 1400), "cuda")
+    out = torch.empty((100, 2816), dtype=torch.float32, device="cuda")
+    rc.moe_forward(lyr.w, x, x, rc.BF16, 100, out, ws.view())
+    rc.prefill_gemms(lyr.w, ws.view())
+    rc.status(ws.view())
+    ws.close()
+    ws2 = rc.DevBuf(nbytes)
+    try:
+        with pytest.raises(rc.DeviceError):
+            rc.prefill_gemms(lyr.w, ws2.view())
+    finally:
+        ws2.close()
