@@ -80,22 +80,56 @@ def gpu_smi_id(local_rank: int) -> str:
 
 
 class ClockSampler:
+    """SM clock, power and clock-event (throttle) reasons of one GPU during the timed region,
+    read-only. Sampled through NVML from a background thread of this process, every 20 ms (the
+    thread never touches the CUDA context; an nvidia-smi subprocess polling at 100 ms stretched the
+    expert-parallel step's host synchronisations); falls back to `nvidia-smi -lms 200`."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_id: str):
         self.idx = gpu_id  # "GPU-<uuid>" of the device under test (or an nvidia-smi index)
         self.proc = None
+        self.thread = None
+        self.samples = []
         self.path = os.path.join("/tmp", f"rvc_clocks_{os.getpid()}.csv")
 
+    def _nvml_loop(self, nv, h):
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:  # noqa: BLE001 - a failed read is a missing sample
+                pass
+            self.stop_flag.wait(0.02)
+
     def start(self):
-        """Start sampling every 100 ms and wait (up to 5 s) until the first sample is written,
-        so that the timed region that follows is covered from its start."""
+        """Start sampling and wait (up to 5 s) for the first sample, so that the timed region that
+        follows is covered from its start."""
+        import threading
+        self.stop_flag = threading.Event()
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = (nv.nvmlDeviceGetHandleByUUID(self.idx) if self.idx.startswith("GPU-")
+                 else nv.nvmlDeviceGetHandleByIndex(int(self.idx)))
+            self.nv = nv
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+            t_end = time.time() + 5.0
+            while not self.samples and time.time() < t_end:
+                time.sleep(0.01)
+            return
+        except Exception:  # noqa: BLE001 - no NVML: the nvidia-smi fallback
+            self.thread = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -105,11 +139,18 @@ class ClockSampler:
             if os.path.getsize(self.path) > 0:
                 break
             time.sleep(0.01)
-        self.t_start = time.time()
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            sm = [float(x[0]) for x in self.samples]
+            mx = [float(x[1]) for x in self.samples]
+            reasons = sorted({n for _, _, r in self.samples for n, bit in self.REASONS if r & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml"}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -133,7 +174,7 @@ class ClockSampler:
                         reasons.add(n)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -284,7 +325,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
 
         def fwd():
             return layer.forward(x, out=out)
-        launches = 7  # k_router_chains4, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_ms, k_pf_combine
+        launches = 7  # k_router_chains4, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_tc, k_pf_combine
         check = layer.status
     else:
         from rosevine_b200.ep import EpMoeLayer, GpuBackend, local_experts
@@ -296,56 +337,60 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
         def fwd():
             return layer.forward(x)
         # k_router_chains4, k_select, k_quant_rows, k_ep_count, k_ep_pack, k_ep_meta, k_plan, k_ep_scatter,
-        # 2 x k_pf_gemm_ms, k_pf_combine, k_ep_reduce (NCCL's and torch's own kernels not counted)
+        # 2 x k_pf_gemm_tc, k_pf_combine, k_ep_reduce (NCCL's and torch's own kernels not counted)
         launches = 12
         check = be.status
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    phases = {}
-
     def loop(steps, e2e: bool):
-        tot, disp, comb = 0.0, 0.0, 0.0
-        phases.clear()
+        """K steps back to back between two events: no host synchronisation of the bench's own
+        (the expert-parallel layer reads its row counts once per step)."""
+        ev0.record(stream)
         for _ in range(steps):
-            ev0.record(stream)
             if e2e:
                 x.copy_(hx.view(torch.bfloat16), non_blocking=True)
             o = fwd()
             if e2e:
                 ho.copy_(o, non_blocking=True)
-            ev1.record(stream)
-            torch.cuda.synchronize()
-            tot += ev0.elapsed_time(ev1)
-            if world > 1:
-                disp += layer.stats.dispatch_ms
-                comb += layer.stats.combine_ms
-                for k, v in layer.stats.phases_ms.items():
-                    phases[k] = phases.get(k, 0.0) + v / steps
-        return tot / steps, disp / steps, comb / steps
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / steps
 
     for _ in range(args.warmup):
         fwd()
     torch.cuda.synchronize()
-    # one sampler per node (local rank 0, its own GPU): several nvidia-smi processes polling at
-    # once slow the expert-parallel step's host synchronisations
+    # one sampler per node (local rank 0, its own GPU)
     clocks = ClockSampler(gpu_smi_id(local_rank)) if local_rank == 0 else None
     if clocks:
         clocks.start()
-    # the barrier after the sampler's start-up (up to a second on local rank 0): otherwise the
-    # other ranks' first timed step waits for it inside the all-to-all
     if world > 1:
         dist.barrier()
-    step_ms, disp_ms, comb_ms = loop(args.steps, False)
+    torch.cuda.synchronize()
+    step_ms = loop(args.steps, False)
+    if world > 1:
+        dist.barrier()
     clk = clocks.stop() if clocks else None
-    phases_main = dict(phases)
-    if world > 1:
-        dist.barrier()
-    e2e_ms, _, _ = loop(max(3, args.steps // 2), True)
+    e2e_ms = loop(max(3, args.steps // 2), True)
     check()
+    disp_ms = comb_ms = 0.0
+    phases = {}
+    if world > 1:
+        # the phase split, in a separate pass: events between the phases, read after each step
+        layer.timing = True
+        k = max(3, args.steps // 2)
+        for _ in range(k):
+            fwd()
+            torch.cuda.synchronize()
+            st = layer.phase_times()
+            disp_ms += st.dispatch_ms / k
+            comb_ms += st.combine_ms / k
+            for name, v in st.phases_ms.items():
+                phases[name] = phases.get(name, 0.0) + v / k
+        layer.timing = False
     gemm_ms = None
     if world == 1:
-        # the dominant kernels alone: the two grouped GEMMs (k_pf_gemm_ms gate/up and down)
+        # the dominant kernels alone: the two grouped GEMMs (k_pf_gemm_tc gate/up and down)
         # re-run on the last call's plan, records and scale planes (rvc_prefill_gemms), timed
         # with events on the stream they run on; weights and records exceed the L2
         from rosevine_b200 import rvcuda as rc
@@ -361,34 +406,93 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
         torch.cuda.synchronize()
         gemm_ms = ev0.elapsed_time(ev1) / k
         check()
+    if world == 1:
+        ids_t = torch.empty((n, 8), dtype=torch.int32, device=dev)
+        o = layer.forward(x, ids=ids_t)
+    else:
+        o = layer.forward(x)
+        ids_t = layer.last_ids
+    par = prefill_parity(args, o, ids_t, xs, weights, rank, world, dev)
     t = torch.tensor([step_ms, e2e_ms, disp_ms, comb_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms, e2e_ms, disp_ms, comb_ms = (float(v) for v in t)
+    par = reduce_parity(par, world, dev)
     tops = OPS_PER_TOKEN * PREFILL_TOK / world / (step_ms * 1e-3) / 1e12
     gemm_tops = OPS_PER_TOKEN * PREFILL_TOK / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
     return {"gemm_ms": gemm_ms, "gemm_int8_tops": gemm_tops, "step_ms": step_ms, "e2e_ms": e2e_ms, "tokens_per_s": PREFILL_TOK / (step_ms * 1e-3),
             "e2e_tokens_per_s": PREFILL_TOK / (e2e_ms * 1e-3), "int8_tops_per_gpu": tops,
             "int8_frac_per_gpu": tops / peaks["int8_tops"], "exposed_all_to_all_ms": disp_ms + comb_ms,
             "dispatch_ms": disp_ms, "combine_ms": comb_ms, "launches": launches, "clocks": clk,
-            "rank0_phases_ms": phases_main or None,
+            "rank0_phases_ms": phases or None, "parity": par,
             "h2d_bytes_per_step": PREFILL_TOK * 2816 * 2, "d2h_bytes_per_step": PREFILL_TOK * 2816 * 4}
 
 
+PARITY_ROWS = 32   # oracle-checked output rows per rank
+PARITY_TOL = 1e-3  # max |gpu - cpu| / max |cpu| per row (the north star's tolerance)
+
+
+def prefill_parity(args, out, ids_t, xs, weights, rank: int, world: int, dev) -> dict:
+    """A seeded sample of this rank's output rows against the oracle (the reference's scalar
+    Q8_0 CPU path): expert ids exact, per-row relative error. Rows whose router has an exact
+    tie among the top 9 probabilities would be left out and counted."""
+    import torch
+    from oracle import oracle as O
+    O.build()
+    n = xs.shape[0]
+    rows = np.sort(np.random.default_rng(args.seed + 1000 + rank).choice(n, size=min(PARITY_ROWS, n), replace=False))
+    got = out[torch.as_tensor(rows, device=dev)].cpu().numpy()
+    ids = ids_t[torch.as_tensor(rows, device=dev)].cpu().numpy()
+    threads = max(1, (os.cpu_count() or 1) // world)
+    pool = O.Pool(threads, kernel=O.KERNEL_SCALAR)
+    try:
+        want, want_ids, _, lg = O.moe_layer(pool, xs[rows], xs[rows], weights["w_router"], weights["gate_up"],
+                                            weights["down"])
+    finally:
+        pool.close()
+    _, _, probs = O.select_experts(lg, 8)
+    srt = -np.sort(-probs, axis=1)
+    tie = np.any(srt[:, :8] == srt[:, 1:9], axis=1)
+    keep = ~tie
+    err = np.abs(got - want).max(axis=1) / np.maximum(np.abs(want).max(axis=1), 1e-30)
+    return {"rows": int(keep.sum()), "ties_excluded": int(tie.sum()),
+            "ids_mismatch": int((ids[keep] != want_ids[keep]).any(axis=1).sum()),
+            "max_row_rel_err": float(err[keep].max()) if keep.any() else 0.0}
+
+
+def reduce_parity(p: dict, world: int, dev) -> dict:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([p["rows"], p["ties_excluded"], p["ids_mismatch"]], dtype=torch.float64, device=dev)
+    e = torch.tensor([p["max_row_rel_err"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t)
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    rows, ties, bad = (int(v) for v in t.tolist())
+    err = float(e.item())
+    return {"checked_rows": rows, "ranks": world, "ties_excluded": ties, "ids_mismatch_rows": bad,
+            "max_row_rel_err": err, "tol": PARITY_TOL, "oracle": "oracle/rv_oracle.c scalar Q8_0 (reference order)",
+            "pass": bad == 0 and err <= PARITY_TOL}
+
+
 def roofline(pf: dict, peaks: dict) -> dict:
-    """The dominant kernels (the two grouped GEMMs, timed alone at N=1) against the int8 peak;
-    at N>1 the expert-parallel layer as a whole."""
+    """The dominant kernels (the two grouped GEMMs, timed alone at N=1) against the int8 peak
+    (derived: 2 x the measured bf16 dense peak; no int8 GEMM is measured on this pool), with the
+    fraction of the f16 tensor pipe they run on (kind::f16 MMAs) beside it; at N>1 the
+    expert-parallel layer as a whole."""
     r = {"bound": "tensor", "peak": peaks["int8_tops"], "unit": "TOP/s",
-         "peak_source": peaks["source"] + " (2 x bf16 dense)", "traffic": None,
+         "peak_source": "derived: 2 x " + peaks["source"] + " bf16 dense", "traffic": None,
          "layer_achieved": pf["int8_tops_per_gpu"], "layer_frac": pf["int8_frac_per_gpu"]}
     if pf.get("gemm_int8_tops"):
-        r.update(kernel="k_pf_gemm_ms<gate/up> + k_pf_gemm_ms<down> (the grouped expert GEMMs, re-run alone by "
-                        "rvc_prefill_gemms on the layer's plan and records), int8 MACs of the experts x 2 per "
-                        "average launch pair", achieved=pf["gemm_int8_tops"],
-                 frac=pf["gemm_int8_tops"] / peaks["int8_tops"], gemm_ms=pf["gemm_ms"])
+        r.update(kernel="k_pf_gemm_tc<gate/up> + k_pf_gemm_tc<down> (the grouped expert GEMMs on tcgen05 kind::f16 "
+                        "with f16-held integer operands, re-run alone by rvc_prefill_gemms on the layer's plan and "
+                        "records), int8 MACs of the experts x 2 per average launch pair", achieved=pf["gemm_int8_tops"],
+                 frac=pf["gemm_int8_tops"] / peaks["int8_tops"], gemm_ms=pf["gemm_ms"],
+                 f16_pipe_frac=pf["gemm_int8_tops"] / (peaks["int8_tops"] / 2))
     else:
-        r.update(kernel="prefill layer (router, plan, quantise, grouped GEMMs k_pf_gemm_ms, combine), int8 MACs "
-                        "of the experts x 2", achieved=pf["int8_tops_per_gpu"], frac=pf["int8_frac_per_gpu"])
+        r.update(kernel="expert-parallel prefill layer (router, pack, all-to-allv, grouped GEMMs k_pf_gemm_tc, "
+                        "combine, reduce), int8 MACs of the experts x 2", achieved=pf["int8_tops_per_gpu"],
+                 frac=pf["int8_frac_per_gpu"])
     return r
 
 

@@ -200,15 +200,16 @@ int rvc_prefill_gemms(const rvc_moe_weights *w, void *workspace, size_t workspac
 int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const int32_t *rows, int n_rows,
                          const void *xq8, int n_in, int32_t *out, void *stream);
 
-/* Test hook (no counterpart in the reference): the int32 block dots of one tile of the prefill
- * GEMM, formed by the production kernel (k_pf_gemm_tc: TMA copies, nibble unpack, tcgen05.mma
- * kind::i8 into tensor memory, tensor-memory loads) in a mode whose epilogue writes the dots
- * instead of scaling them. The tile: rows row_tile*128 .. +127 of expert `expert`'s gate_up
- * (which = 0; packed row order, gate and up interleaved per 32 rows) or down (which = 1) rows,
- * against n (1..128) Q8_0 records (rvc_q8_record_bytes layout over n_embd (which = 0) or ff
- * (which = 1) columns; device, 16-byte aligned). out: device int32 [nblk][128 positions][128
- * rows]; positions >= n read 0. scratch: device, 256-byte aligned, at least 256 + nblk * 4 *
- * round_up(n, 4) bytes; its int at byte 12 receives the kernel's status bits. */
+/* Test hook (no counterpart in the reference): the integer block dots of one tile of the prefill
+ * GEMM, formed by the production kernel (k_pf_gemm_tc: weight unpack, TMA copies, tcgen05.mma
+ * into tensor memory with the integer operands held exactly as f16, tensor-memory loads) in a
+ * mode whose epilogue writes the dots instead of scaling them. The tile: rows row_tile*128 ..
+ * +127 of expert `expert`'s gate_up (which = 0; packed row order, gate and up interleaved per 32
+ * rows) or down (which = 1) rows, against n (1..128) activation rows in the GEMM's operand
+ * layout: per 32-element block of n_embd (which = 0) or ff (which = 1) columns, the 32 Q8_0
+ * quants as f16 integers (64 bytes; device, 16-byte aligned). out: device int32 [nblk][128
+ * positions][128 rows]; positions >= n read 0. scratch: device, 256-byte aligned, at least
+ * 256 + nblk * 4 * round_up(n, 4) bytes; its int at byte 12 receives the kernel's status bits. */
 int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, int row_tile, const void *records,
                               int n, int32_t *out, void *scratch, size_t scratch_bytes, void *stream);
 

@@ -37,7 +37,21 @@ __device__ long long g_prof_clk[8][1024][8];  // SM clock counter at the same ma
             ::rvc::g_prof_clk[K][b_][P] = clock64();                                               \
         }                                                                                          \
     } while (0)
+// Event trace of CTA 0 (profiling builds): slot K, index I (a block or stage counter), point P.
+#define RVC_TRACE(K, I, P)                                                                         \
+    do {                                                                                           \
+        const int i_ = (I);                                                                        \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && i_ >= 0 && i_ < 1024) {                          \
+            unsigned long long t_;                                                                 \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                 \
+            ::rvc::g_prof[K][i_][P] = t_;                                                          \
+            ::rvc::g_prof_clk[K][i_][P] = clock64();                                               \
+        }                                                                                          \
+    } while (0)
 #else
+#define RVC_TRACE(K, I, P) \
+    do {                   \
+    } while (0)
 #define RVC_MARK(K, P) \
     do {               \
     } while (0)

@@ -22,6 +22,10 @@
 
 namespace rvc {
 
+// Bytes of one position's activation operand for the grouped GEMM (the prefill path's x and h
+// records): nblk blocks of 32 quants held as f16 integers.
+__host__ __device__ constexpr int pf_rec_bytes(int nblk) { return nblk * 64; }
+
 // Activation block scales: a block-major f32 plane, ppad floats per block (ppad a multiple of
 // 4, so that a tile's 128 positions start 16-byte aligned for the GEMM's tensor copies).
 __device__ __forceinline__ void pf_store_scale(float *plane, int ppad, int b, int k, float d) {
@@ -29,20 +33,20 @@ __device__ __forceinline__ void pf_store_scale(float *plane, int ppad, int b, in
 }
 
 // ------------------------------------------------------------------ quantise + scatter
-// Q8_0 of x, once per token, written into the records of the token's `used` plan positions
-// pos_of[t used + j], with each block's scale in the block-major plane xsc the GEMM's scale
-// tiles come from. Four lanes per block: lane l of warp w takes values
-// 8 (l & 3) .. + 7 of block 8 w' + (l >> 2) of its token (one 16-byte load for bf16, two for
-// f32; rows are 16-byte aligned, as the entry points require), so a warp quantises 8 blocks at
-// once, each reduction taking two shuffles within the group of four lanes, and writes a plan
-// position's 8 quants per lane with one 8-byte store. Per value the arithmetic is
-// quant_q8_lane's (ops.rs:95-105); a block's amax and integer sum do not depend on the
-// reduction order.
+// Q8_0 of x, once per token, written to the token's `used` plan positions pos_of[t used + j]: the
+// quants as f16 integers in the GEMM's activation operand (pf_rec_bytes per position, 32 f16
+// per block), each block's scale in the block-major plane xsc the GEMM's scale tiles come from.
+// Four lanes per block: lane l of warp w takes values 8 (l & 3) .. + 7 of block 8 w' + (l >> 2)
+// of its token (one 16-byte load for bf16, two for f32; rows are 16-byte aligned, as the entry
+// points require), so a warp quantises 8 blocks at once, each amax taking two shuffles within
+// the group of four lanes, and writes a plan position's 8 quants per lane with one 16-byte
+// store. Per value the arithmetic is quant_q8_lane's (ops.rs:95-105); a block's amax does not
+// depend on the reduction order.
 template <typename XT>
 __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int n_embd, int n_tok, int used,
                                                   const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
                                                   float *__restrict__ xsc, int ppad) {
-    const int nb = n_embd / QK, xrb = q8rec_bytes(nb);
+    const int nb = n_embd / QK;
     const int lane = threadIdx.x & 31, part = lane & 3;
     const int nc = (nb + 7) / 8, wi = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (wi >= n_tok * nc) return;  // whole warps leave together
@@ -62,29 +66,23 @@ __global__ void __launch_bounds__(256) k_pf_quant(const XT *__restrict__ x, int 
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t qw[2] = {0u, 0u};
-    int s = 0;
+    uint32_t qh[4];  // the 8 quants as f16 (exact integers), two per word
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         const float r = roundf(__fmul_rn(v[k], id));
         const int q = r != r ? 0 : (r > 127.0f ? 127 : (r < -128.0f ? -128 : (int)r));
-        s += q;
-        qw[k >> 2] |= (uint32_t)(uint8_t)(int8_t)q << (8 * (k & 3));
+        const uint32_t h = __half_as_ushort(__int2half_rn(q));
+        qh[k >> 1] = (k & 1) ? (qh[k >> 1] | (h << 16)) : h;
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
     const float df = f16_bits_to_f32(f32_to_f16_bits(d));
     const int my_pos = lane < used ? __ldg(pos_of + (size_t)t * used + lane) : 0;
+    const int xrb = pf_rec_bytes(nb);
     for (int j = 0; j < used; ++j) {
         const int k = __shfl_sync(0xffffffffu, my_pos, j);
         if (in) {
             uint8_t *rec = xperm + (size_t)k * xrb;
-            *reinterpret_cast<uint2 *>(rec + b * 32 + part * 8) = make_uint2(qw[0], qw[1]);
-            if (part == 0) {
-                reinterpret_cast<float *>(rec + nb * 32)[b] = df;
-                reinterpret_cast<int *>(rec + nb * 36)[b] = s;
-                pf_store_scale(xsc, ppad, b, k, df);
-            }
+            *reinterpret_cast<uint4 *>(rec + b * 64 + part * 16) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
+            if (part == 0) pf_store_scale(xsc, ppad, b, k, df);
         }
     }
 }
@@ -233,32 +231,27 @@ __global__ void __launch_bounds__(256) k_ep_meta(const uint8_t *__restrict__ row
     }
 }
 
-// Received rows to plan positions: warp task (row r, block b) copies the block into the records
-// of the row's occupied slots' plan positions, and its scale into the block-major plane.
+// Received rows to plan positions: warp task (row r, block b) writes the block's quants as f16
+// integers into the activation operand of each occupied slot's plan position, and its scale into
+// the block-major plane.
 __global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ rows, int nb, int n_rows, int used,
                                                     const int32_t *__restrict__ slot_e,
                                                     const int32_t *__restrict__ pos_of, uint8_t *__restrict__ xperm,
                                                     float *__restrict__ xsc, int ppad) {
-    const int xrb = q8rec_bytes(nb), rb = ep_row_bytes(nb, used);
+    const int rb = ep_row_bytes(nb, used), xrb = pf_rec_bytes(nb);
     const int lane = threadIdx.x & 31;
     const long long total = (long long)n_rows * nb;
     for (long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += (long long)gridDim.x * 8) {
         const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
         const uint8_t *src = rows + (size_t)r * rb;
-        const uint8_t q = src[b * 32 + lane];
+        const uint16_t qh = __half_as_ushort(__int2half_rn((int)(int8_t)src[b * 32 + lane]));
         const float d = reinterpret_cast<const float *>(src + nb * 32)[b];
-        const int qs = reinterpret_cast<const int *>(src + nb * 36)[b];
         for (int j = 0; j < used; ++j) {
             const int p = r * used + j;
             if (__ldg(slot_e + p) < 0) continue;
             const int k = __ldg(pos_of + p);
-            uint8_t *dst = xperm + (size_t)k * xrb;
-            dst[b * 32 + lane] = q;
-            if (lane == 0) {
-                reinterpret_cast<float *>(dst + nb * 32)[b] = d;
-                reinterpret_cast<int *>(dst + nb * 36)[b] = qs;
-                pf_store_scale(xsc, ppad, b, k, d);
-            }
+            reinterpret_cast<uint16_t *>(xperm + (size_t)k * xrb)[b * 32 + lane] = qh;
+            if (lane == 0) pf_store_scale(xsc, ppad, b, k, d);
         }
     }
 }

@@ -1,5 +1,5 @@
 // prefill_tc.cuh - the grouped expert GEMM of the prefill path on the 5th-generation tensor
-// cores: tcgen05.mma kind::i8 into tensor memory, exact per-block scaling on the CUDA cores.
+// cores: tcgen05.mma into tensor memory, exact per-block scaling on the CUDA cores.
 //
 // Computes what the reference's CPU-experts Q8_0 path computes for every (weight row, plan
 // position) pair of an expert group (runtime/src/expert_pool.rs:86-135 driving
@@ -9,35 +9,46 @@
 //
 // with sumi_b the exact int32 dot of block b's Q4_0 nibbles (minus 8) and the activation's Q8_0
 // quants, and every f32 operation rounded where the reference rounds it. Then, for gate/up,
-// h = gelu(gate) * up and its Q8_0 records (exec.rs:606-611, ops.rs:95-105); for down, y per
+// h = gelu(gate) * up and its Q8_0 quants (exec.rs:606-611, ops.rs:95-105); for down, y per
 // (position, row), combined afterwards in slot order (k_pf_combine).
 //
-// Design, from measurements on B200 (rosevine_b200/micro/tc_probe.cu):
-//   - one tcgen05.mma (M = 128 rows, N = 128 positions, K = 32) per 32-column block writes the
-//     block's int32 dots to a tensor-memory buffer; four buffers of 128 columns let the MMAs run
-//     ahead of the epilogue (an MMA completes about 640 cycles after issue);
-//   - tensor-memory loads do not wait for MMAs in flight on other columns, so the epilogue
-//     drains one buffer while the next blocks' MMAs run;
-//   - the epilogue's three f32 operations per (row, position, block) on the 128 f32 lanes of an
-//     SM bound the kernel: the tensor cores are idle most of the time by design. One issuing
-//     warp (333 cycles per MMA) keeps up with an epilogue of about 390 cycles per block.
+// The block dots: the integer operands n - 8 (-8..7) and q (-127..127) are held as f16, which
+// represents them exactly, and multiplied by tcgen05.mma kind::f16 with f32 accumulation: every
+// product and every partial sum is an integer below 2^15 in magnitude, so the tensor core's f32
+// accumulation is exact and tensor memory receives (float)sumi_b itself. (An i8 MMA gives the
+// same integers as int32, but their conversion to f32 competes with the f32x2 arithmetic for the
+// CUDA cores' issue and pipes: measured on B200, 4 conversions + 6 f32x2 operations run at 6.8
+// iterations per SM cycle against 9.1 without the conversions, rosevine_b200/micro/tc_probe.cu.)
+//
+// Design, from measurements on B200 (tc_probe.cu):
+//   - per 32-column block two MMAs (M = 128 rows, N = 128 positions, K = 16 each; the second
+//     accumulates) write the block's dots to a tensor-memory buffer; four buffers of 128 columns
+//     let the MMAs run ahead of the epilogue. The accumulate flag is an immediate: with a runtime
+//     predicate an MMA costs 200-280 issue cycles instead of about 80;
+//   - tensor-memory loads do not wait for MMAs in flight on other columns; an epilogue warp
+//     hands its buffer back as soon as the dots are in registers;
+//   - the epilogue's three f32 operations per (row, position, block) bound the kernel.
 //
 // Roles (one CTA per SM, persistent over the (row tile, position tile) list):
-//   warp 0       tensor-memory allocation; TMA copies of a stage (8 blocks): weight nibbles
-//                [128 rows][8 blocks][16 B], activation quants [16 K-halves][128 positions]
-//                [16 B] (the MMA's K-major B layout as stored), activation scales [8][128] f32
+//   warp 0       tensor-memory allocation; TMA copies of a stage (2 blocks): activation quants
+//                [8 K chunks][128 positions][16 B] (the MMA's K-major B layout as stored) and
+//                activation scales [2][128] f32. Five stages in shared memory: the copies and the
+//                unpacking of a stage start up to 6 blocks before its MMAs (a stage's copy takes
+//                about 2 us; with the MMAs 4 blocks ahead of the epilogue, fewer stages expose it)
 //   warp 1       MMA issue (the whole warp runs the loop; one elected lane issues)
-//   warps 2-5    nibble unpack: thread r turns row r's nibbles into signed bytes n - 8 in the
-//                MMA's K-major A layout (the packed plane swizzles blocks within complete groups
-//                of 8: nib_pos in pack.cuh)
-//   warps 6-13   epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (one weight row
-//                per thread) and one half of the 128 positions; per block and position
-//                t = (float)D, s = dw * dx, p = t * s (rounded product), acc = acc + p.
+//   warps 2-3    weight unpack: thread r turns rows r and r + 64's nibbles (read from global one
+//                stage ahead; the packed plane swizzles blocks within complete groups of 8:
+//                nib_pos in pack.cuh) into f16 n - 8 in the MMA's K-major A layout, and their
+//                f16 scales into an f32 table
+//   warps 4-19   epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (one weight row
+//                per thread) and positions 32 ((w - 4) / 4) .. + 31; per block and position
+//                s = dw * dx, p = t * s (rounded product), acc = acc + p.
 // Every wait is bounded; a wait that runs out records STATUS_TIMEOUT and ends the CTA's work
 // (all roles see the abort flag), after the MMAs and copies in flight have completed.
 #pragma once
 #include "common.cuh"
 #include "pack.cuh"
+#include "prefill.cuh"
 
 #include <cuda.h>
 
@@ -45,22 +56,27 @@ namespace rvc {
 
 constexpr int TC_M = 128;     // weight rows per tile (tensor-memory lanes)
 constexpr int TC_N = 128;     // plan positions per tile (tensor-memory columns per buffer)
-constexpr int TC_KB = 8;      // blocks per stage
-constexpr int TC_STAGES = 2;  // shared-memory stages
+constexpr int TC_KB = 2;      // blocks per stage
+constexpr int TC_STAGES = 5;  // shared-memory stages: copies and unpacking run up to 6 blocks ahead of the MMAs
 constexpr int TC_TBUF = 4;    // tensor-memory buffers of TC_N columns
-constexpr int TC_EPI_WARPS = 8;
-constexpr int TC_THREADS = (6 + TC_EPI_WARPS) * 32;
-// a stage in shared memory
-constexpr int TC_OFF_NIB = 0;                              // [128 rows][8 blocks][16 B] raw nibbles
-constexpr int TC_OFF_B = TC_OFF_NIB + TC_M * TC_KB * 16;   // [16 halves][128 positions][16 B] quants
-constexpr int TC_OFF_DX = TC_OFF_B + 2 * TC_KB * TC_N * 16;  // [8 blocks][128 positions] f32 scales
-constexpr int TC_OFF_A = TC_OFF_DX + TC_KB * TC_N * 4;     // [8 blocks][2 halves][128 rows][16 B] s8
-constexpr int TC_STAGE_BYTES = TC_OFF_A + TC_KB * 2 * TC_M * 16;  // 84 KB
-constexpr int TC_TMA_BYTES = TC_OFF_A;                     // bytes the three copies of a stage write
-// gate/up output staging: [2 units][64 positions][65] f32 (one column half at a time)
-constexpr int TC_STG_PITCH = 65;
+constexpr int TC_EPI_WARPS = 16;  // four per SM sub-partition: one lane quarter x one 32-position quarter each
+constexpr int TC_EPI_POS = TC_N * 4 / TC_EPI_WARPS;  // positions per epilogue warp (32)
+constexpr int TC_THREADS = (4 + TC_EPI_WARPS) * 32;  // 640: up to 96 registers a thread
+// An operand row holds a block's 32 values as 4 K chunks of 8 f16 (16 B): chunk c = elements
+// 8 c .. 8 c + 7. In shared memory a block's operand is [4 chunks][128 rows][16 B]; MMA k (k = 0,
+// 1) reads chunks 2 k, 2 k + 1 (lbo 2048 B between them, 8-row groups 128 B apart).
+constexpr int TC_BLK_BYTES = 4 * 128 * 16;                 // 8 KB
+constexpr int TC_OFF_B = 0;                                // [TC_KB blocks] activation operands
+constexpr int TC_OFF_DX = TC_OFF_B + TC_KB * TC_BLK_BYTES;  // [TC_KB blocks][128 positions] f32 scales
+constexpr int TC_OFF_A = TC_OFF_DX + TC_KB * TC_N * 4;     // [TC_KB blocks] weight operands
+constexpr int TC_OFF_DW = TC_OFF_A + TC_KB * TC_BLK_BYTES;  // [TC_KB blocks][128 rows] f32 weight scales
+constexpr int TC_STAGE_BYTES = TC_OFF_DW + TC_KB * TC_M * 4;  // 34 KB
+constexpr int TC_TMA_BYTES = TC_OFF_A;                     // bytes the two copies of a stage write
+// gate/up output exchange: per (unit, position half) pair of warps, gate values of 32 positions
+// and up values of 32 positions, [32][32 columns] f32 each
 constexpr int TC_OFF_STG = TC_STAGES * TC_STAGE_BYTES;
-constexpr int TC_SMEM_BYTES = TC_OFF_STG + 2 * 64 * TC_STG_PITCH * 4 + 1024;  // + alignment slack
+constexpr int TC_STG_PAIR = 2 * (TC_EPI_POS / 2) * 32 * 4;
+constexpr int TC_SMEM_BYTES = TC_OFF_STG + 2 * (TC_EPI_WARPS / 4) * TC_STG_PAIR + 1024;  // + alignment slack
 static_assert(TC_SMEM_BYTES <= 227 * 1024, "shared memory of k_pf_gemm_tc");
 static_assert(TC_STAGE_BYTES % 1024 == 0, "stage alignment");
 
@@ -76,9 +92,10 @@ struct TcArgs {
     int row_tiles;        // row tiles per position tile (rows_per_expert / TC_M)
     int row_base;         // first weight row of row tile 0 (0; another row tile for the debug check)
     int nblk;             // K blocks (n_embd / 32 or ff / 32)
+    const uint8_t *nib;   // weight nibbles [E][rows][nblk][16 B] (packed plane, pack.cuh)
     const uint16_t *scl;  // weight scales [E][rows][nblk] f16 bits
     int nh;               // (gate/up) h blocks per pair (ff / 32)
-    uint8_t *hrec;        // (gate/up) out: h Q8_0 records by plan position
+    uint8_t *hrec;        // (gate/up) out: h quants (pf_rec_bytes per plan position)
     float *hsc;           // (gate/up) out: h block scales, block-major [nh][ppad] f32
     int ppad;
     float *y;             // (down) out: [positions][n_embd]; (raw) out: int32 [nblk][128][128]
@@ -111,20 +128,28 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
 }
 
-// Instruction descriptor of kind::i8: s32 accumulator (bits 4-5 = 2), A and B signed (bits 7-9
-// and 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// Instruction descriptor of kind::f16: f32 accumulator (bits 4-5 = 1), A and B f16 (bits 7-9 and
+// 10-12 = 0), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// D[tmem] = A * B, issued by one elected lane of a converged warp (all lanes pass the same,
-// warp-uniform operands: issuing from a one-lane branch costs about 100 more cycles per MMA).
-__device__ __forceinline__ void mma_i8_elect(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .pred e, acc;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 acc, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, acc;\n\t}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(0u)
-        : "memory");
+// D[tmem] = A * B (ACC false) or D += A * B (ACC true), issued by one elected lane of a converged
+// warp (all lanes pass the same, warp-uniform operands). The accumulate flag is an immediate.
+template <bool ACC>
+__device__ __forceinline__ void mma_f16_elect(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc) {
+    if (ACC)
+        asm volatile(
+            "{\n\t.reg .pred e, acc;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 acc, 1, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, acc;\n\t}\n" ::"r"(tmem_d),
+            "l"(da), "l"(db), "r"(idesc)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred e, acc;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 acc, 0, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, acc;\n\t}\n" ::"r"(tmem_d),
+            "l"(da), "l"(db), "r"(idesc)
+            : "memory");
 }
 // Arrive on `bar` once every tcgen05 operation issued before by this thread has completed
 // (elected lane of a converged warp).
@@ -156,6 +181,36 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&v)[32]
         : "r"(taddr)
         : "memory");
     asm volatile("tcgen05.wait::ld.sync.aligned;" : RVC_LD32_INOUT : : "memory");
+}
+
+// The same load with the 32 values delivered as 16 f32x2-ready pairs (column 2 k in the low half):
+// the pairs are formed inside the asm, so that the register allocator places each pair's halves
+// together instead of copying them afterwards.
+__device__ __forceinline__ void tmem_ld32_pairs(uint32_t taddr, uint64_t (&p)[16]) {
+    asm volatile(
+        "{\n\t.reg .b32 r<32>;\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {r0, r1, r2, r3, r4, r5, r6, r7, r8, r9, r10, r11, r12, r13, r14, r15, "
+        "r16, r17, r18, r19, r20, r21, r22, r23, r24, r25, r26, r27, r28, r29, r30, r31}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t"
+        "mov.b64 %0, {r0, r1};\n\tmov.b64 %1, {r2, r3};\n\tmov.b64 %2, {r4, r5};\n\tmov.b64 %3, {r6, r7};\n\t"
+        "mov.b64 %4, {r8, r9};\n\tmov.b64 %5, {r10, r11};\n\tmov.b64 %6, {r12, r13};\n\tmov.b64 %7, {r14, r15};\n\t"
+        "mov.b64 %8, {r16, r17};\n\tmov.b64 %9, {r18, r19};\n\tmov.b64 %10, {r20, r21};\n\tmov.b64 %11, {r22, r23};\n\t"
+        "mov.b64 %12, {r24, r25};\n\tmov.b64 %13, {r26, r27};\n\tmov.b64 %14, {r28, r29};\n\tmov.b64 %15, {r30, r31};\n\t}"
+        : "=l"(p[0]), "=l"(p[1]), "=l"(p[2]), "=l"(p[3]), "=l"(p[4]), "=l"(p[5]), "=l"(p[6]), "=l"(p[7]), "=l"(p[8]),
+          "=l"(p[9]), "=l"(p[10]), "=l"(p[11]), "=l"(p[12]), "=l"(p[13]), "=l"(p[14]), "=l"(p[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Two f32x2 pairs (four consecutive f32) from shared memory.
+__device__ __forceinline__ void lds_2x2(uint32_t addr, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+// One f32 from shared memory in both halves of an f32x2 pair.
+__device__ __forceinline__ uint64_t lds_splat(uint32_t addr) {
+    uint64_t r;
+    asm volatile("{\n\t.reg .b32 t;\n\tld.shared.b32 t, [%1];\n\tmov.b64 %0, {t, t};\n\t}" : "=l"(r) : "r"(addr));
+    return r;
 }
 
 // 2-D / 3-D TMA tensor copies global -> shared, completion on `bar`.
@@ -204,15 +259,56 @@ __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
 __device__ __forceinline__ float f2x_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float f2x_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
-// Signed bytes n - 8 of four nibble values n in 0..15 (one per byte): (n | 0x80) - 8 cannot
-// borrow across bytes, and the xor restores the sign bit.
-__device__ __forceinline__ uint32_t nib_s8(uint32_t n4) { return ((n4 | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
+// gelu_tanh (common.cuh) with tanh inlined, so that independent evaluations overlap: the same
+// operations in the same order (ops.rs:145-149), tanh in double rounded once to f32.
+__device__ __forceinline__ float gelu_tanh_inl(float x) {
+    const float A = 0.044715f;
+    const float S = 0.7978846f;
+    const float inner = __fmul_rn(__fmul_rn(S, x), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(A, x), x)));
+    const float t = (float)tanh((double)inner);
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
 
-// Bounded mbarrier wait that gives up early once another role has aborted the CTA's work.
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
-    for (long long i = 0; i < kSpinLimit; ++i) {
+// Four nibble values n in 0..15 (one per byte of n4) as two f16x2 words of n - 8: a byte
+// permute builds the f16 bits 0x6400 | n (the value 1024 + n, exact), and one f16x2 subtraction
+// of 1032 leaves n - 8 exactly.
+__device__ __forceinline__ uint2 nib_f16x4(uint32_t n4) {
+    uint32_t a, b;
+    asm("prmt.b32 %0, %1, 0x64646464, 0x4140;" : "=r"(a) : "r"(n4));
+    asm("prmt.b32 %0, %1, 0x64646464, 0x4342;" : "=r"(b) : "r"(n4));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(a) : "r"(0x64086408u));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(b) : "r"(0x64086408u));
+    return make_uint2(a, b);
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded mbarrier wait that gives up early once another role has aborted the CTA's work. A phase
+// that has completed already is seen by one non-blocking test. A role that is ahead of the
+// epilogue (TMA copies, unpack, MMA issue) waits with `backoff`: between polls it sleeps, from
+// 32 ns doubling up to 512 ns, so that it does not take issue slots from the epilogue warps that
+// share its SM sub-partition (measured: spinning waits issued as many instructions as the
+// epilogue's arithmetic). The epilogue polls without sleeping.
+constexpr long long TC_WAIT_ITERS = 1ll << 22;  // at most about 2 s of polls
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *status,
+                                        bool backoff = false) {
+    if (mbar_test_wait(bar, parity)) return true;
+    uint32_t ns = 32;
+    for (long long i = 0; i < TC_WAIT_ITERS; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255 && *abort) return false;
+        if (*abort) return false;
+        if (backoff) {
+            __nanosleep(ns);
+            ns = ns < 512 ? 2 * ns : 512;
+        }
     }
     set_status(status, STATUS_TIMEOUT);
     *abort = 1;
@@ -221,10 +317,23 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
 
 // The same wait in every lane of a warp, with one outcome for the whole warp (the warp-wide
 // tcgen05 and barrier operations that follow need all its lanes).
-__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
-    const bool r = tc_wait(bar, parity, abort, status);
+__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort, int *status,
+                                             bool backoff = false) {
+    const bool r = tc_wait(bar, parity, abort, status, backoff);
     return __all_sync(0xffffffffu, r);
 }
+
+// 16-byte shared-memory load (four f32).
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+// The epilogue warps' barrier (named barrier 1, all TC_EPI_WARPS warps). Every epilogue warp runs
+// the same sequence of tiles, stages and blocks, so each reaches every such barrier; waits on
+// mbarriers stay with one leader warp and are bounded, and their outcome travels through epi_ok.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory"); }
 
 // A tile entry from k_plan, checked against the layout: false for an entry that does not fit
 // (a stale or foreign workspace), which every role then skips alike.
@@ -235,16 +344,23 @@ __device__ __forceinline__ bool tc_tile(const TcArgs &a, int L, int &e, int &nt,
     return e < a.n_experts && nt >= 1 && nt <= TC_N && p0 >= 0 && p0 + nt <= a.ppos;
 }
 
+// Profiling builds: a timeline of CTA 0's gate/up GEMM (stage events in slot 6, block events in
+// slot 5); compiled away otherwise.
+#define TC_TRACE(K, I, P)                          \
+    do {                                           \
+        if (MODE == PF_GU) RVC_TRACE(K, I, P);     \
+    } while (0)
+
 // ------------------------------------------------------------------ the kernel
 template <int MODE>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_constant__ CUtensorMap map_nib,
-                                                              const __grid_constant__ CUtensorMap map_act,
+__global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_constant__ CUtensorMap map_act,
                                                               const __grid_constant__ CUtensorMap map_dx, TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base, as an offset from the shared array (keeps shared addressing)
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     __shared__ uint64_t full[TC_STAGES], afull[TC_STAGES], empty[TC_STAGES];
-    __shared__ uint64_t tfull[TC_TBUF], tempty[TC_TBUF], drain, stg_bar;
+    __shared__ uint64_t tfull[TC_TBUF], tempty[TC_TBUF], drain;
+    __shared__ int epi_ok;  // the epilogue leader's wait outcome, read by all epilogue warps after bar.sync
     __shared__ uint32_t taddr_s;
     __shared__ int abort_s;
     volatile int *abort = &abort_s;
@@ -258,12 +374,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
     if (tid == 32) {
         for (int s = 0; s < TC_STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&afull[s], 4);                     // the four unpack warps
+            mbar_init(&afull[s], 2);                     // the two unpack warps
             mbar_init(&empty[s], 1 + TC_EPI_WARPS);      // the MMAs' commit and every epilogue warp
         }
         for (int b = 0; b < TC_TBUF; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], TC_EPI_WARPS);
         mbar_init(&drain, 1);
-        mbar_init(&stg_bar, TC_EPI_WARPS);
         abort_s = 0;
         fence_barrier_init();
     }
@@ -281,16 +396,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
             for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
                 int e, nt, p0, row0;
                 if (!tc_tile(a, L, e, nt, p0, row0)) continue;
-                const int wrow0 = e * a.rows_per_expert + row0;
                 for (int st = 0; st < nst && ok; ++st, ++sc) {
                     const int s = sc % TC_STAGES;
                     if (sc >= TC_STAGES && !(ok = tc_wait(&empty[s], (uint32_t)((sc / TC_STAGES - 1) & 1), abort,
-                                                          a.status)))
+                                                          a.status, true)))
                         break;
+                    TC_TRACE(6, sc, 0);
                     const uint32_t base = sbase + s * TC_STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[s], TC_TMA_BYTES);
-                    tma_load_3d(base + TC_OFF_NIB, &map_nib, 0, st * TC_KB, wrow0, &full[s]);
-                    tma_load_3d(base + TC_OFF_B, &map_act, 0, p0, 2 * st * TC_KB, &full[s]);
+                    tma_load_3d(base + TC_OFF_B, &map_act, 0, p0, 4 * st * TC_KB, &full[s]);
                     tma_load_2d(base + TC_OFF_DX, &map_dx, p0, st * TC_KB, &full[s]);
                 }
             }
@@ -301,7 +415,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issue (whole warp)
-        const uint32_t idesc = idesc_i8(TC_M, TC_N);
+        const uint32_t idesc = idesc_f16(TC_M, TC_N);
         int sc = 0, bc = 0;
         bool ok = true;
         for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
@@ -310,80 +424,141 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
                 const uint32_t par = (uint32_t)((sc / TC_STAGES) & 1);
-                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status) &&
-                           tc_wait_warp(&afull[s], par, abort, a.status)))
+                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status, true) &&
+                           tc_wait_warp(&afull[s], par, abort, a.status, true)))
                     break;
+                if (lane == 0) TC_TRACE(6, sc, 3);
                 tc_fence_after();
                 const uint32_t base = sbase + s * TC_STAGE_BYTES;
                 const int kn = min(TC_KB, nblk - st * TC_KB);
                 for (int j = 0; j < kn; ++j, ++bc) {
                     const int tb = bc % TC_TBUF;
+                    if (lane == 0) TC_TRACE(5, bc, 0);
                     if (bc >= TC_TBUF &&
-                        !(ok = tc_wait_warp(&tempty[tb], (uint32_t)((bc / TC_TBUF - 1) & 1), abort, a.status)))
+                        !(ok = tc_wait_warp(&tempty[tb], (uint32_t)((bc / TC_TBUF - 1) & 1), abort, a.status, true)))
                         break;
                     tc_fence_after();
-                    // A: block j's two K halves of 128 rows x 16 B; B: K halves 2j, 2j + 1 of 128 positions
-                    const uint64_t da = umma_desc(base + TC_OFF_A + j * (2 * TC_M * 16), TC_M * 16, 128);
-                    const uint64_t db = umma_desc(base + TC_OFF_B + j * (2 * TC_N * 16), TC_N * 16, 128);
-                    mma_i8_elect(tmem + (uint32_t)(tb * TC_N), da, db, idesc);
+                    // block j: K chunks 0, 1 then 2, 3 of the weight (A) and activation (B) operands
+                    const uint32_t ab = base + TC_OFF_A + j * TC_BLK_BYTES, bb = base + TC_OFF_B + j * TC_BLK_BYTES;
+                    const uint32_t d = tmem + (uint32_t)(tb * TC_N);
+                    mma_f16_elect<false>(d, umma_desc(ab, 2048, 128), umma_desc(bb, 2048, 128), idesc);
+                    mma_f16_elect<true>(d, umma_desc(ab + 4096, 2048, 128), umma_desc(bb + 4096, 2048, 128), idesc);
                     mma_commit_elect(&tfull[tb]);
+                    if (lane == 0) TC_TRACE(5, bc, 1);
+#ifdef RVC_TC_TRACE_MMA_DONE
+                    // profiling builds only: the MMA warp itself timestamps the block's completion
+                    if (MODE == PF_GU) {
+                        while (!mbar_test_wait(&tfull[tb], (uint32_t)((bc / TC_TBUF) & 1))) {
+                        }
+                        if (lane == 0) TC_TRACE(5, bc, 6);
+                    }
+#endif
                 }
-                if (ok) mma_commit_elect(&empty[s]);  // the stage's A and B are free once its MMAs complete
+                if (ok) mma_commit_elect(&empty[s]);  // the stage's operands are free once its MMAs complete
             }
         }
         // every MMA issued has completed before the tensor memory is freed
         mma_commit_elect(&drain);
         fd_mbar_wait(&drain, 0, a.status);
-    } else if (warp < 6) {
-        // ---------------------------------------------------------- nibble unpack (row r)
-        const int r = tid - 64;
+    } else if (warp < 4) {
+        // ---------------------------------------------------------- weight unpack (rows r, r + 64)
+        // Each row's nibbles (from global, one stage ahead) become f16 n - 8 in the MMA's A layout,
+        // and its f16 scales f32 values in the stage's scale table.
+        const int r0 = tid - 64;
         int sc = 0;
         bool ok = true;
         for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
             int e, nt, p0, row0;
             if (!tc_tile(a, L, e, nt, p0, row0)) continue;
+            const size_t grow0 = (size_t)e * a.rows_per_expert + row0;  // a multiple of 8: swizzle key = r & 7
+            uint4 wn[2][TC_KB];
+            uint32_t dn[2][TC_KB / 2];
+            auto ld_stage = [&](int st) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = r0 + 64 * h;
+                    const uint4 *nrow = reinterpret_cast<const uint4 *>(a.nib + (grow0 + r) * nblk * 16);
+                    const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + (grow0 + r) * nblk);
+#pragma unroll
+                    for (int j = 0; j < TC_KB; ++j) {
+                        const int b = st * TC_KB + j;
+                        wn[h][j] = b < nblk ? __ldg(nrow + nib_pos(b, nblk, r & 7)) : make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    // TC_KB f16 scales = TC_KB / 2 32-bit words (a row of the plane is 4-byte aligned;
+                    // words past the row's last block are not read)
+#pragma unroll
+                    for (int k = 0; k < TC_KB / 2; ++k)
+                        dn[h][k] = st * TC_KB + 2 * k < nblk ? __ldg(srow + (TC_KB / 2) * st + k) : 0u;
+                }
+            };
+            ld_stage(0);
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
-                if (!(ok = tc_wait_warp(&full[s], (uint32_t)((sc / TC_STAGES) & 1), abort, a.status))) break;
+                uint4 wc[2][TC_KB];
+                uint32_t dc[2][TC_KB / 2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                    for (int j = 0; j < TC_KB; ++j) wc[h][j] = wn[h][j];
+#pragma unroll
+                    for (int k = 0; k < TC_KB / 2; ++k) dc[h][k] = dn[h][k];
+                }
+                if (st + 1 < nst) ld_stage(st + 1);  // lands during this stage
+                // the stage's buffers are free once its copies have been issued again (full[s])
+                if (!(ok = tc_wait_warp(&full[s], (uint32_t)((sc / TC_STAGES) & 1), abort, a.status, true))) break;
+                if (tid == 64) TC_TRACE(6, sc, 1);
                 uint8_t *base = smem + s * TC_STAGE_BYTES;
                 const int kn = min(TC_KB, nblk - st * TC_KB);
-                const uint4 *nrow = reinterpret_cast<const uint4 *>(base + TC_OFF_NIB + r * (TC_KB * 16));
 #pragma unroll
-                for (int j = 0; j < TC_KB; ++j) {
-                    if (j < kn) {
-                        // a stage of 8 blocks is one complete group, swizzled in the packed plane
-                        const uint4 w = nrow[kn == TC_KB ? (j ^ (r & 7)) : j];
-                        const uint4 lo = make_uint4(nib_s8(w.x & 0x0F0F0F0Fu), nib_s8(w.y & 0x0F0F0F0Fu),
-                                                    nib_s8(w.z & 0x0F0F0F0Fu), nib_s8(w.w & 0x0F0F0F0Fu));
-                        const uint4 hi = make_uint4(nib_s8((w.x >> 4) & 0x0F0F0F0Fu), nib_s8((w.y >> 4) & 0x0F0F0F0Fu),
-                                                    nib_s8((w.z >> 4) & 0x0F0F0F0Fu), nib_s8((w.w >> 4) & 0x0F0F0F0Fu));
-                        uint4 *ablk = reinterpret_cast<uint4 *>(base + TC_OFF_A + j * (2 * TC_M * 16));
-                        ablk[r] = lo;          // K half 0: elements 0..15 (low nibbles)
-                        ablk[TC_M + r] = hi;   // K half 1: elements 16..31 (high nibbles)
+                for (int h = 0; h < 2; ++h) {
+                    const int r = r0 + 64 * h;
+                    float *dws = reinterpret_cast<float *>(base + TC_OFF_DW) + r;
+#pragma unroll
+                    for (int j = 0; j < TC_KB; ++j) {
+                        if (j < kn) {
+                            // chunk 0: low nibbles of bytes 0..7 (elements 0..7), 1: of bytes 8..15,
+                            // 2: high nibbles of bytes 0..7 (elements 16..23), 3: of bytes 8..15
+                            const uint4 w = wc[h][j];
+                            uint4 *ablk = reinterpret_cast<uint4 *>(base + TC_OFF_A + j * TC_BLK_BYTES) + r;
+                            const uint2 c0a = nib_f16x4(w.x & 0x0F0F0F0Fu), c0b = nib_f16x4(w.y & 0x0F0F0F0Fu);
+                            const uint2 c1a = nib_f16x4(w.z & 0x0F0F0F0Fu), c1b = nib_f16x4(w.w & 0x0F0F0F0Fu);
+                            const uint2 c2a = nib_f16x4((w.x >> 4) & 0x0F0F0F0Fu), c2b = nib_f16x4((w.y >> 4) & 0x0F0F0F0Fu);
+                            const uint2 c3a = nib_f16x4((w.z >> 4) & 0x0F0F0F0Fu), c3b = nib_f16x4((w.w >> 4) & 0x0F0F0F0Fu);
+                            ablk[0 * TC_M] = make_uint4(c0a.x, c0a.y, c0b.x, c0b.y);
+                            ablk[1 * TC_M] = make_uint4(c1a.x, c1a.y, c1b.x, c1b.y);
+                            ablk[2 * TC_M] = make_uint4(c2a.x, c2a.y, c2b.x, c2b.y);
+                            ablk[3 * TC_M] = make_uint4(c3a.x, c3a.y, c3b.x, c3b.y);
+                            const uint32_t hw = dc[h][j >> 1];
+                            dws[j * TC_M] = f16_bits_to_f32((uint16_t)((j & 1) ? (hw >> 16) : (hw & 0xFFFFu)));
+                        }
                     }
                 }
                 fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&afull[s]);
+                if (tid == 64) TC_TRACE(6, sc, 2);
             }
         }
     } else {
         // ---------------------------------------------------------- epilogue
-        const int ew = warp - 6, q = warp & 3, hh = ew >> 2;  // lane quarter, column half
-        const int r = 32 * q + lane;                           // this thread's weight row in the tile
-        const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(64 * hh);
+        // Warp w (w = 4 .. 19) holds tensor-memory lanes 32 q .. + 31 (q = w % 4: one weight row per
+        // thread) and positions pb .. pb + 31 (pb = 32 ((w - 4) / 4)) of every block. Each warp waits
+        // for the buffers on its own and hands each one back as soon as its dots are in registers.
+        const int q = warp & 3, kq = (warp - 4) >> 2, pb = TC_EPI_POS * kq;
+        const bool leader = warp == 4;
+        const int r = 32 * q + lane;  // this thread's weight row in the tile
+        const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)pb;
         const uint64_t nz2 = a.negzero2;
-        float *stg = reinterpret_cast<float *>(smem + TC_OFF_STG);
-        int sc = 0, bc = 0, sp = 0;
+        int sc = 0, bc = 0;
         bool ok = true;
-        // rendezvous of the epilogue warps around the output staging (an mbarrier with a bounded
-        // wait, not bar.sync: a warp that aborted must not leave the others waiting forever)
+        // the output exchange's meeting point (named barrier 1 of the epilogue warps); the leader
+        // alone reads the abort flag, so every epilogue warp takes the same decision
         auto rendezvous = [&]() -> bool {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&stg_bar);
-            const bool r = tc_wait_warp(&stg_bar, (uint32_t)(sp & 1), abort, a.status);
-            ++sp;
-            return r;
+            if (leader && lane == 0) epi_ok = *abort ? 0 : 1;
+            epi_bar();
+            const bool w = *reinterpret_cast<volatile int *>(&epi_ok) != 0;
+            epi_bar();
+            return w;
         };
         for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
             int e, nt, p0, row0;
@@ -391,145 +566,132 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                 if (tid == TC_THREADS - 1) set_status(a.status, STATUS_BAD_INDEX);
                 continue;
             }
-            const int nch = max(0, min(2, (nt - 64 * hh + 31) >> 5));  // 32-position chunks holding tokens
-            // this row's weight scales, one stage ahead (8 f16 = four 32-bit words; a row of the
-            // plane is 4-byte aligned, and words past the row's last block are not read)
-            const uint32_t *srow =
-                reinterpret_cast<const uint32_t *>(a.scl + (size_t)(e * a.rows_per_expert + row0 + r) * nblk);
-            uint32_t wn[4];
-            auto ld_dw = [&](int st) {
+            const bool has = pb < nt;  // this warp's positions hold tokens
+            uint64_t acc[TC_EPI_POS / 2];  // positions pb + 2 m, + 1 as f32 pairs
 #pragma unroll
-                for (int k = 0; k < 4; ++k) wn[k] = st * TC_KB + 2 * k < nblk ? __ldg(srow + (st * TC_KB) / 2 + k) : 0u;
-            };
-            uint64_t acc[2][16];
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-                for (int k = 0; k < 16; ++k) acc[c][k] = 0ull;
-            ld_dw(0);
+            for (int m = 0; m < TC_EPI_POS / 2; ++m) acc[m] = 0ull;
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
-                uint32_t wc[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) wc[k] = wn[k];
-                if (st + 1 < nst) ld_dw(st + 1);  // lands during this stage
-                if (!(ok = tc_wait_warp(&full[s], (uint32_t)((sc / TC_STAGES) & 1), abort, a.status))) break;
-                const float *sdx = reinterpret_cast<const float *>(smem + s * TC_STAGE_BYTES + TC_OFF_DX) + 64 * hh;
+                const uint32_t par = (uint32_t)((sc / TC_STAGES) & 1);
+                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status) && tc_wait_warp(&afull[s], par, abort, a.status)))
+                    break;
+                const uint32_t sdx = sbase + s * TC_STAGE_BYTES + TC_OFF_DX + 4 * pb;  // this warp's positions
+                const uint32_t sdw = sbase + s * TC_STAGE_BYTES + TC_OFF_DW + 4 * r;   // this row's scales
                 const int kn = min(TC_KB, nblk - st * TC_KB);
                 for (int j = 0; j < kn; ++j, ++bc) {
-                    const int tb = bc % TC_TBUF;
+                    const int tb = bc & (TC_TBUF - 1);
                     if (!(ok = tc_wait_warp(&tfull[tb], (uint32_t)((bc / TC_TBUF) & 1), abort, a.status))) break;
+                    if (lane == 0 && (warp == 4 || warp == 19)) TC_TRACE(5, bc, warp == 4 ? 2 : 4);
                     tc_fence_after();
-                    const uint32_t hw = wc[j >> 1];
-                    const float dw = f16_bits_to_f32((uint16_t)((j & 1) ? (hw >> 16) : (hw & 0xFFFFu)));
-                    const uint64_t dw2 = f2_pack(dw, dw);
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        if (c < nch) {
-                            uint32_t v[32];
-                            tmem_ld32_sync(trow + (uint32_t)(tb * TC_N + 32 * c), v);
-                            if (MODE == PF_RAW) {
-                                // raw block dots of the first tile: [block][position][row] int32
-                                if (L == 0) {
-                                    int *out = reinterpret_cast<int *>(a.y) + (size_t)(st * TC_KB + j) * TC_N * TC_M;
-#pragma unroll
-                                    for (int k = 0; k < 32; ++k) out[(64 * hh + 32 * c + k) * TC_M + r] = (int)v[k];
-                                }
-                            } else {
-                                const float4 *dx4 = reinterpret_cast<const float4 *>(sdx + j * TC_N + 32 * c);
-#pragma unroll
-                                for (int k = 0; k < 8; ++k) {
-                                    const float4 d4 = dx4[k];  // the scales of 4 positions (broadcast)
-                                    const uint64_t t0 = f2_pack(__int2float_rn((int)v[4 * k]), __int2float_rn((int)v[4 * k + 1]));
-                                    const uint64_t t1 =
-                                        f2_pack(__int2float_rn((int)v[4 * k + 2]), __int2float_rn((int)v[4 * k + 3]));
-                                    const uint64_t s0 = f2x_mul(dw2, f2_pack(d4.x, d4.y));
-                                    const uint64_t s1 = f2x_mul(dw2, f2_pack(d4.z, d4.w));
-                                    acc[c][2 * k] = f2x_add(acc[c][2 * k], f2x_prod(t0, s0, nz2));
-                                    acc[c][2 * k + 1] = f2x_add(acc[c][2 * k + 1], f2x_prod(t1, s1, nz2));
-                                }
-                            }
-                        }
-                    }
+                    uint64_t t[TC_EPI_POS / 2];  // this block's dots of positions pb + 2 m, + 1 (exact f32 pairs)
+                    if (has) tmem_ld32_pairs(trow + (uint32_t)(tb * TC_N), t);
+                    // the block's dots are in registers: hand the buffer back to the MMAs before the
+                    // arithmetic, so that the next MMA into it overlaps this block's epilogue
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[tb]);
+                    if (has) {
+                        if (MODE == PF_RAW) {
+                            // raw block dots of the first tile: [block][position][row] int32
+                            if (L == 0) {
+                                int *out = reinterpret_cast<int *>(a.y) + (size_t)(st * TC_KB + j) * TC_N * TC_M;
+#pragma unroll
+                                for (int m = 0; m < TC_EPI_POS / 2; ++m) {
+                                    out[(pb + 2 * m) * TC_M + r] = (int)f2x_lo(t[m]);
+                                    out[(pb + 2 * m + 1) * TC_M + r] = (int)f2x_hi(t[m]);
+                                }
+                            }
+                        } else {
+                            const uint64_t dw2 = lds_splat(sdw + j * (TC_M * 4));
+                            const uint32_t dxj = sdx + j * (TC_N * 4);
+#pragma unroll
+                            for (int m = 0; m < TC_EPI_POS / 4; ++m) {
+                                uint64_t d01, d23;  // the scales of 4 positions (broadcast), as two pairs
+                                lds_2x2(dxj + 16 * m, d01, d23);
+                                const uint64_t s0 = f2x_mul(dw2, d01);
+                                const uint64_t s1 = f2x_mul(dw2, d23);
+                                acc[2 * m] = f2x_add(acc[2 * m], f2x_prod(t[2 * m], s0, nz2));
+                                acc[2 * m + 1] = f2x_add(acc[2 * m + 1], f2x_prod(t[2 * m + 1], s1, nz2));
+                            }
+                        }
+                    }
+                    if (lane == 0 && (warp == 4 || warp == 19)) TC_TRACE(5, bc, warp == 4 ? 3 : 5);
                 }
+                if (!ok) break;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);  // done with the stage's scales
+                if (lane == 0 && warp == 4) TC_TRACE(6, sc, 4);
             }
             if (!ok) break;
             // ------------------------------------------------------ tile outputs
             if (MODE == PF_DN) {
+                if (has) {
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const int pos = 64 * hh + 32 * c + 2 * k;
+                    for (int m = 0; m < TC_EPI_POS / 2; ++m) {
+                        const int pos = pb + 2 * m;
                         float *yp = a.y + (size_t)(p0 + pos) * a.n_embd + row0 + r;
-                        if (pos < nt) yp[0] = f2x_lo(acc[c][k]);
-                        if (pos + 1 < nt) yp[a.n_embd] = f2x_hi(acc[c][k]);
+                        if (pos < nt) yp[0] = f2x_lo(acc[m]);
+                        if (pos + 1 < nt) yp[a.n_embd] = f2x_hi(acc[m]);
                     }
+                }
             } else if (MODE == PF_GU) {
-                // rows 64 u .. + 63 of the tile are h block (row0 / 64 + u): gate columns at rows
-                // 64 u + i, up at 64 u + 32 + i (pack.cuh interleaving). One column half at a time
-                // the half's two warps per unit stage gate and up as [unit][position][64 + 1];
-                // then thread (unit, position) forms h = gelu(gate) * up over the block's 32
-                // columns and its Q8_0 record, as quant_q8_lane does (ops.rs:95-105).
-                const int u = q >> 1, col = (q & 1) * 32 + lane;
-                const int hrb = q8rec_bytes(a.nh);
-                for (int half = 0; half < 2 && ok; ++half) {
-                    if (!(ok = rendezvous())) break;  // the staging area is free
-                    if (hh == half) {
+                // Rows 64 u .. + 63 of the tile are h block (row0 / 64 + u): gate column i at row
+                // 64 u + i (lane quarter 2 u), up column i at 64 u + 32 + i (quarter 2 u + 1), so
+                // lane i of the gate warp and of the up warp of a position group hold gate and up of
+                // the same column. The gate warp hands the up warp its gate values of the group's
+                // last half of the positions, the up warp hands the gate warp its up values of the
+                // first half; then each forms h = gelu(gate) * up for its half and quantises each
+                // position's 32 columns (one per lane) to a Q8_0 block as quant_q8_lane does
+                // (ops.rs:95-105).
+                constexpr int HP = TC_EPI_POS / 2;  // positions each of the pair computes
+                const int u = q >> 1;
+                const bool gate = (q & 1) == 0;
+                float *xg = reinterpret_cast<float *>(smem + TC_OFF_STG + (u * (TC_EPI_WARPS / 4) + kq) * TC_STG_PAIR);
+                float *xu = xg + HP * 32;  // xg: gate of the last HP positions; xu: up of the first HP
+                if (!(ok = rendezvous())) break;  // the exchange area is free
+                if (has) {
 #pragma unroll
-                        for (int c = 0; c < 2; ++c)
-#pragma unroll
-                            for (int k = 0; k < 16; ++k) {
-                                float *sp = stg + ((size_t)u * 64 + 32 * c + 2 * k) * TC_STG_PITCH + col;
-                                sp[0] = f2x_lo(acc[c][k]);
-                                sp[TC_STG_PITCH] = f2x_hi(acc[c][k]);
-                            }
+                    for (int m = 0; m < HP / 2; ++m) {
+                        const uint64_t v = gate ? acc[HP / 2 + m] : acc[m];
+                        float *dst = (gate ? xg : xu) + (2 * m) * 32 + lane;
+                        dst[0] = f2x_lo(v);
+                        dst[32] = f2x_hi(v);
                     }
-                    if (!(ok = rendezvous())) break;
-                    const int item = tid - 6 * 32;  // 0..255: (unit, position) pairs 0..127
-                    const int iu = item >> 6, pos = item & 63, tok = 64 * half + pos;
-                    if (item < 128 && tok < nt) {
-                        const float *g = stg + ((size_t)iu * 64 + pos) * TC_STG_PITCH;
-                        float hv[32];
-                        float amax = 0.0f;
+                }
+                if (!(ok = rendezvous())) break;
+                if (has) {
+                    const int hrb = pf_rec_bytes(a.nh);
+                    const int hb = (row0 >> 6) + u;  // h block within the expert's ff columns
+                    const int t0 = pb + (gate ? 0 : HP);
+                    for (int i0 = 0; i0 < HP && t0 + i0 < nt; i0 += 8) {  // 8 positions at a time
+                        float hv[8];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            hv[i] = __fmul_rn(gelu_tanh(g[i]), g[32 + i]);
-                            amax = fmaxf(amax, fabsf(hv[i]));
+                        for (int i = 0; i < 8; ++i) {
+                            const uint64_t mine = gate ? acc[(i0 + i) >> 1] : acc[HP / 2 + ((i0 + i) >> 1)];
+                            const float own = ((i0 + i) & 1) ? f2x_hi(mine) : f2x_lo(mine);
+                            const float other = (gate ? xu : xg)[(i0 + i) * 32 + lane];
+                            const float g = gate ? own : other, uv = gate ? other : own;
+                            hv[i] = __fmul_rn(gelu_tanh(g), uv);
                         }
-                        const float d = __fdiv_rn(amax, 127.0f);
-                        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-                        uint32_t qw[8];
-                        int qs = 0;
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
+                        for (int i = 0; i < 8; ++i) {
+                            const int tok = t0 + i0 + i;
+                            if (tok >= nt) break;  // warp-uniform
+                            // the block's largest magnitude: non-negative floats order as their bit patterns
+                            const float amax =
+                                __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(hv[i]))));
+                            const float d = __fdiv_rn(amax, 127.0f);
+                            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
                             const float rr = roundf(__fmul_rn(hv[i], id));
                             const int qq = rr != rr ? 0 : (rr > 127.0f ? 127 : (rr < -128.0f ? -128 : (int)rr));
-                            qs += qq;
-                            if ((i & 3) == 0) qw[i >> 2] = 0u;
-                            qw[i >> 2] |= (uint32_t)(uint8_t)(int8_t)qq << (8 * (i & 3));
+                            // the quant as an f16 integer (the down GEMM's B operand), and the block scale
+                            uint16_t *rec = reinterpret_cast<uint16_t *>(a.hrec + (size_t)(p0 + tok) * hrb);
+                            rec[hb * 32 + lane] = __half_as_ushort(__int2half_rn(qq));
+                            if (lane == 0) a.hsc[(size_t)hb * a.ppad + p0 + tok] = f16_bits_to_f32(f32_to_f16_bits(d));
                         }
-                        const float df = f16_bits_to_f32(f32_to_f16_bits(d));
-                        const int hb = (row0 >> 6) + iu;  // h block within the expert's ff columns
-                        uint8_t *rec = a.hrec + (size_t)(p0 + tok) * hrb;
-                        uint4 *qd = reinterpret_cast<uint4 *>(rec + hb * 32);
-                        qd[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-                        qd[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
-                        reinterpret_cast<float *>(rec + a.nh * 32)[hb] = df;
-                        reinterpret_cast<int *>(rec + a.nh * 36)[hb] = qs;
-                        a.hsc[(size_t)hb * a.ppad + p0 + tok] = df;
                     }
                 }
             }
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-                for (int k = 0; k < 16; ++k) acc[c][k] = 0ull;
         }
     }
     // ------------------------------------------------------------------ teardown

@@ -101,10 +101,11 @@ struct Workspace {
         sel_wts = take(pairs * 4);
         sel_flag = take((size_t)max_tok * 4);
         xrec = take((size_t)max_tok * q8rec_bytes((int)nb));
-        hrec = take(ppos * q8rec_bytes((int)nbh));
+        // h records: the decode kernels' Q8_0 records, or the prefill GEMM's f16 operand
+        hrec = take(ppos * std::max(q8rec_bytes((int)nbh), pf_rec_bytes((int)nbh)));
         ybuf = take(ppos * n_embd * 4);
         // prefill calls only
-        xperm = prefill ? take(ppos * q8rec_bytes((int)nb)) : o;
+        xperm = prefill ? take(ppos * pf_rec_bytes((int)nb)) : o;
         xd = prefill ? take(nb * ppad * 4) : o;   // x block scales, f32, block-major
         hd = prefill ? take(nbh * ppad * 4) : o;  // h block scales
         tiles = prefill ? take((pairs / 128 + 1 + (size_t)ne) * 8) : o;
@@ -463,18 +464,16 @@ int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-// The grouped GEMM's tensor maps: weight nibbles [rows][blocks][16 B]; activation quants as
-// [K halves][positions][16 B] (a tile's positions contiguous per K half: the MMA's K-major B
-// layout); activation block scales [blocks][positions] f32.
+// The grouped GEMM's tensor maps: activation operands as [16-byte K chunks][positions][16 B] (a
+// tile's positions contiguous per chunk: the MMA's K-major B layout; rec_bytes apart per
+// position); activation block scales [blocks][positions] f32.
 struct TcMaps {
-    CUtensorMap nib, act, dx;
+    CUtensorMap act, dx;
 };
 
-int tc_maps(TcMaps *m, const uint8_t *nib, int n_rows, int nblk, const uint8_t *rec, int rec_bytes, int ppos,
-            const float *scales, int ppad) {
+int tc_maps(TcMaps *m, const uint8_t *rec, int rec_bytes, int nblk, int ppos, const float *scales, int ppad) {
     int rc;
-    if ((rc = map3d(&m->nib, nib, 16, nblk, (uint64_t)n_rows, 16, (uint64_t)nblk * 16, 16, TC_KB, TC_M)) ||
-        (rc = map3d(&m->act, rec, 16, ppos, 2 * nblk, rec_bytes, 16, 16, TC_N, 2 * TC_KB)) ||
+    if ((rc = map3d(&m->act, rec, 16, ppos, 4 * (uint64_t)nblk, rec_bytes, 16, 16, TC_N, 4 * TC_KB)) ||
         (rc = map2d(&m->dx, scales, (uint64_t)ppad, nblk, (uint64_t)ppad * 4, TC_N, TC_KB,
                     CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
         return rc;
@@ -488,7 +487,7 @@ int launch_tc(const TcMaps &m, const TcArgs &g, int max_units, cudaStream_t st) 
     if ((rc = fd_smem_max(k_pf_gemm_tc<MODE>, &smax))) return rc;
     if (smax < (size_t)TC_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
     const int grid = std::max(1, std::min(num_sms(), max_units));  // persistent: one CTA per SM
-    k_pf_gemm_tc<MODE><<<grid, TC_THREADS, TC_SMEM_BYTES, st>>>(m.nib, m.act, m.dx, g);
+    k_pf_gemm_tc<MODE><<<grid, TC_THREADS, TC_SMEM_BYTES, st>>>(m.act, m.dx, g);
     return launched();
 }
 
@@ -502,19 +501,19 @@ int pf_gemms(const rvc_moe_weights *w, const Workspace &L, void *ws, int n_pairs
     float *xsc = at<float>(ws, L.xd), *hsc = at<float>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
     TcMaps mg, md;
-    if ((rc = tc_maps(&mg, pk.gu_nib, ne * 2 * w->ff, nb, xperm, q8rec_bytes(nb), ppos, xsc, ppad)) ||
-        (rc = tc_maps(&md, pk.dn_nib, ne * w->n_embd, nbh, hrec, q8rec_bytes(nbh), ppos, hsc, ppad)))
+    if ((rc = tc_maps(&mg, xperm, pf_rec_bytes(nb), nb, ppos, xsc, ppad)) ||
+        (rc = tc_maps(&md, hrec, pf_rec_bytes(nbh), nbh, ppos, hsc, ppad)))
         return rc;
     const int tiles_max = n_pairs / TC_N + 1 + ne;  // an upper bound on the (expert, position tile) count
     TcArgs g{};
     g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles), g.max_tiles = tiles_max;
     g.n_experts = ne, g.ppos = ppos, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
-    g.rows_per_expert = 2 * w->ff, g.row_tiles = 2 * w->ff / TC_M, g.nblk = nb, g.scl = pk.gu_scl;
+    g.rows_per_expert = 2 * w->ff, g.row_tiles = 2 * w->ff / TC_M, g.nblk = nb, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
     g.nh = nbh, g.hrec = hrec, g.hsc = hsc;
     g.negzero2 = 0x8000000080000000ull;
     if ((rc = launch_tc<PF_GU>(mg, g, tiles_max * g.row_tiles, st))) return rc;
     TcArgs d = g;
-    d.rows_per_expert = w->n_embd, d.row_tiles = w->n_embd / TC_M, d.nblk = nbh, d.scl = pk.dn_scl;
+    d.rows_per_expert = w->n_embd, d.row_tiles = w->n_embd / TC_M, d.nblk = nbh, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
     d.hrec = nullptr, d.hsc = nullptr, d.y = at<float>(ws, L.ybuf);
     return launch_tc<PF_DN>(md, d, tiles_max * d.row_tiles, st);
 }
@@ -957,16 +956,15 @@ int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, i
     if ((rc = (int)cudaMemsetAsync(static_cast<uint8_t *>(scratch) + 256, 0, (size_t)nblk * ppad * 4, st))) return rc;
     const PackedView pk = packed_view(w);
     TcMaps m;
-    if ((rc = tc_maps(&m, which == 0 ? pk.gu_nib : pk.dn_nib, w->n_experts * rows, nblk, (const uint8_t *)records,
-                      q8rec_bytes(nblk), n, reinterpret_cast<const float *>(static_cast<uint8_t *>(scratch) + 256),
-                      ppad)))
+    if ((rc = tc_maps(&m, (const uint8_t *)records, pf_rec_bytes(nblk), nblk, n,
+                      reinterpret_cast<const float *>(static_cast<uint8_t *>(scratch) + 256), ppad)))
         return rc;
     TcArgs g{};
     g.tiles = static_cast<const int2 *>(scratch), g.n_tiles = static_cast<const int *>(scratch) + 2, g.max_tiles = 1;
     g.n_experts = w->n_experts, g.ppos = n, g.ppad = ppad, g.n_embd = w->n_embd;
     g.status = static_cast<int *>(scratch) + 3;
     g.rows_per_expert = rows, g.row_tiles = 1, g.row_base = row_tile * TC_M, g.nblk = nblk;
-    g.scl = which == 0 ? pk.gu_scl : pk.dn_scl;
+    g.nib = which == 0 ? pk.gu_nib : pk.dn_nib, g.scl = which == 0 ? pk.gu_scl : pk.dn_scl;
     g.y = reinterpret_cast<float *>(out);
     return launch_tc<PF_RAW>(m, g, 1, st);
 }

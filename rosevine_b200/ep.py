@@ -107,8 +107,9 @@ class GpuBackend:
         rc.quant_q8_rows(x, _xdtype(x), n, self.n_embd, self.rec, sh)
         rc.ep_pack(ids, wts, self.rec, n, self.used, self.n_embd, self.n_local, self.world, self.counts, self.send,
                    self.owner, self.status_ws, sh)
-        counts = self.counts[:self.world].tolist()
-        return self.send[:sum(counts)], counts, self.owner[:n]
+        # the row counts stay on the device: the layer reads them from the host once, together
+        # with the counts it receives
+        return self.send, self.counts[:self.world], self.owner[:n]
 
     def experts(self, rows) -> torch.Tensor:
         n_rows = rows.shape[0]
@@ -178,13 +179,18 @@ def pack_host(rec: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, world: in
 
 class EpMoeLayer:
     """One rank of the expert-parallel layer. `backend` does the compute on this rank's device;
-    `group` is the process group of the N ranks (rank r holds experts [r E/N, (r + 1) E/N))."""
+    `group` is the process group of the N ranks (rank r holds experts [r E/N, (r + 1) E/N)).
+    With timing=True each forward records CUDA events between its phases (no synchronisation);
+    phase_times() reads them once the caller has synchronised."""
 
-    def __init__(self, backend, rank: int, world: int, n_experts: int = synth.N_EXPERTS, group=None):
+    def __init__(self, backend, rank: int, world: int, n_experts: int = synth.N_EXPERTS, group=None,
+                 timing: bool = False):
         if n_experts % world:
             raise ValueError("experts must divide evenly over the ranks")
         self.be, self.rank, self.world, self.group = backend, rank, world, group
         self.n_local = n_experts // world
+        self.timing = timing
+        self.marks = []
         self.stats = EpStats()
 
     def _a2a(self, out, inp, out_splits, in_splits):
@@ -192,13 +198,14 @@ class EpMoeLayer:
 
     def forward(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's tokens x [n, n_embd] (bf16 or f32) -> their layer output [n, n_embd] f32.
-        bias: router logit offsets, [n_experts] or [n, n_experts] (the skewed-load configs)."""
+        bias: router logit offsets, [n_experts] or [n, n_experts] (the skewed-load configs).
+        One host synchronisation: the row counts (sent and received) are read together."""
         be = self.be
         dev = x.device
         marks = []
 
-        def mark(name):  # device timestamps between the phases (CUDA only)
-            if dev.type == "cuda":
+        def mark(name):  # device timestamps between the phases (CUDA, timing=True only)
+            if self.timing and dev.type == "cuda":
                 e = torch.cuda.Event(enable_timing=True)
                 e.record()
                 marks.append((name, e))
@@ -207,13 +214,15 @@ class EpMoeLayer:
         ids, wts = be.route(x, bias)
         self.last_ids = ids
         mark("route")
-        send, send_counts, owner_map = be.pack(x, ids, wts)
+        send, counts, owner_map = be.pack(x, ids, wts)
         mark("pack")
         # dispatch: row counts, then the rows (records with their slot metadata)
-        sc = torch.tensor(send_counts, dtype=torch.int64, device=dev)
+        sc = torch.as_tensor(counts, device=dev).to(torch.int64)
         rcnt = torch.empty_like(sc)
         self._a2a(rcnt, sc, None, None)
-        recv_counts = rcnt.tolist()
+        both = torch.cat([sc, rcnt]).tolist()  # the step's one host read
+        send_counts, recv_counts = both[:self.world], both[self.world:]
+        send = send[:sum(send_counts)]
         recv = torch.empty((int(sum(recv_counts)), send.shape[1]), dtype=send.dtype, device=dev)
         self._a2a(recv, send, recv_counts, send_counts)
         mark("dispatch")
@@ -224,13 +233,17 @@ class EpMoeLayer:
         mark("combine")
         out = be.reduce(back, owner_map, x.shape[0])
         mark("reduce")
-        st = EpStats(rows_sent=int(send.shape[0]), rows_received=int(recv.shape[0]))
-        if marks:
-            torch.cuda.synchronize(dev)
-            st.phases_ms = {n1: e0.elapsed_time(e1) for (_, e0), (n1, e1) in zip(marks, marks[1:])}
-            st.dispatch_ms, st.combine_ms = st.phases_ms["dispatch"], st.phases_ms["combine"]
-        self.stats = st
+        self.marks = marks
+        self.stats = EpStats(rows_sent=int(send.shape[0]), rows_received=int(recv.shape[0]))
         return out
+
+    def phase_times(self) -> EpStats:
+        """Device time of each phase of the last forward (timing=True; the caller has synchronised)."""
+        st = self.stats
+        if self.marks:
+            st.phases_ms = {n1: e0.elapsed_time(e1) for (_, e0), (n1, e1) in zip(self.marks, self.marks[1:])}
+            st.dispatch_ms, st.combine_ms = st.phases_ms["dispatch"], st.phases_ms["combine"]
+        return st
 
 
 def local_experts(gate_up: np.ndarray, down: np.ndarray, rank: int, world: int):

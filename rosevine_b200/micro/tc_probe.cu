@@ -123,6 +123,21 @@ __device__ __forceinline__ void ld_wait(uint32_t (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" : LD32_INOUTS : : "memory");
 }
 
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void ld16_wait(uint32_t (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+                 :
+                 : "memory");
+}
 __device__ __forceinline__ uint64_t f2x_mul(uint64_t a, uint64_t b) {
     uint64_t r;
     asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -432,6 +447,681 @@ __global__ void __launch_bounds__(128) k_mma(int kind, int layout, int m, int n,
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(tcols) : "memory");
 }
 
+
+// Issue-cost variants, one issuing warp (whole warp, elected lane), M = 128, N = 128, kind::i8:
+//   style 0: the loop of k_mma (operands recomputed per MMA from the loop counter)
+//   style 1: four MMAs per loop iteration, operands loop-invariant plus compile-time offsets
+//   style 2: style 1 with a commit (to an mbarrier nobody waits on) after every MMA
+//   style 3: style 1 with a commit after every fourth MMA
+//   style 4: one lane issues (no elect), operands as style 1
+__global__ void __launch_bounds__(128, 1) k_issue(int style, int iters, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t done, sink_bar;
+    __shared__ uint32_t taddr_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < (128 * 128 + 256 * 128) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = (uint32_t)(i * 2654435761u) & 0x3C3C3C3Cu;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&done, 1);
+        mbar_init(&sink_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    if (warp == 0) {
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 128 * 128, 128 * 16, 128, 0);
+        const uint32_t id = idesc_i8(128, 128);
+        const long long c0 = clock64();
+        if (style == 0) {
+            for (int i = 0; i < iters; ++i) mma_i8_elect(taddr + (uint32_t)((i & 3) * 128), da, db, id, 0u);
+        } else if (style == 1 || style == 2 || style == 3) {
+            for (int i = 0; i < iters; i += 4) {
+                mma_i8_elect(taddr + 0, da, db, id, 0u);
+                if (style == 2) mma_commit_elect(&sink_bar);
+                mma_i8_elect(taddr + 128, da + 256, db + 256, id, 0u);
+                if (style == 2) mma_commit_elect(&sink_bar);
+                mma_i8_elect(taddr + 256, da, db, id, 0u);
+                if (style == 2) mma_commit_elect(&sink_bar);
+                mma_i8_elect(taddr + 384, da + 256, db + 256, id, 0u);
+                if (style >= 2) mma_commit_elect(&sink_bar);
+            }
+        } else if (lane == 0) {
+            for (int i = 0; i < iters; i += 4) {
+                mma_i8(taddr + 0, da, db, id, 0u);
+                mma_i8(taddr + 128, da + 256, db + 256, id, 0u);
+                mma_i8(taddr + 256, da, db, id, 0u);
+                mma_i8(taddr + 384, da + 256, db + 256, id, 0u);
+            }
+        }
+        __syncwarp();
+        const long long c1 = clock64();  // issue done
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        const long long c2 = clock64();
+        if (lane == 0) {
+            ProbeOut &o = out[blockIdx.x];
+            o.mma_cyc = c2 - c0;
+            o.ld_cyc = c1 - c0;
+            o.mma_n = iters;
+        }
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+}
+
+
+// Ring round trip: one warp issues MMAs (M = N = 128) into 4 tensor-memory buffers and commits each
+// to full[b]; 16 warps each load one 32-column chunk of the buffer and arrive on empty[b] (count 16);
+// the MMA warp waits on empty[b] before reusing it. spin 0: mbarrier.try_wait loops; spin 1:
+// mbarrier.test_wait loops (no suspension); spin 2: test_wait loops with a 64-cycle nanosleep.
+__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t par) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok)
+                 : "r"(smem_u32(b)), "r"(par)
+                 : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool ring_wait(uint64_t *b, uint32_t par, int spin, int *flag) {
+    for (long long i = 0; i < kSpin; ++i) {
+        if (spin == 0 ? mbar_try(b, par) : mbar_test(b, par)) return true;
+        if (spin == 2) __nanosleep(32);
+    }
+    atomicOr(flag, 1);
+    return false;
+}
+__global__ void __launch_bounds__(18 * 32, 1) k_ring(int spin, int iters, ProbeOut *out, int *flag, int math = 0) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t full[4], empty[4], done;
+    __shared__ uint32_t taddr_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < (128 * 128 + 256 * 128) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = (uint32_t)(i * 2654435761u) & 0x3C3C3C3Cu;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < 4; ++b) mbar_init(&full[b], 1), mbar_init(&empty[b], 16);
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    long long cyc = 0;
+    if (warp == 1) {
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 128 * 128, 128 * 16, 128, 0);
+        const uint32_t id = idesc_i8(128, 128);
+        const long long c0 = clock64();
+        bool ok = true;
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            if (i >= 4) ok = __all_sync(0xffffffffu, ring_wait(&empty[b], (uint32_t)(((i >> 2) - 1) & 1), spin, flag));
+            tc_after();
+            mma_i8_elect(taddr + (uint32_t)(b * 128), da, db, id, 0u);
+            mma_commit_elect(&full[b]);
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        cyc = clock64() - c0;
+    } else if (warp >= 2) {
+        const int q = warp & 3, k = (warp - 2) >> 2;
+        const uint32_t trow = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * k);
+        uint32_t x = 0;
+        bool ok = true;
+        __shared__ __align__(16) float dx_s[128];
+        __shared__ float dw_s[128];
+        for (int i = lane; i < 128; i += 32) dx_s[i] = 1.0f + i * 0.001f, dw_s[i] = 0.5f + i * 0.002f;
+        __syncwarp();
+        const uint64_t nz2 = 0x8000000080000000ull;
+        uint64_t acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc[m] = 0ull;
+        const uint32_t sdx = smem_u32(dx_s) + 128 * k;
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            ok = __all_sync(0xffffffffu, ring_wait(&full[b], (uint32_t)((i >> 2) & 1), spin, flag));
+            tc_after();
+            uint32_t v[32];
+            ld32(taddr + (trow - taddr) + (uint32_t)(b * 128), v);
+            ld_wait(v);
+            if (math != 2) {
+                tc_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[b]);
+            }
+            if (math) {
+                const float dw = dw_s[32 * q + lane];
+                const uint64_t dw2 = pack2(dw, dw);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    float4 d4;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(d4.x), "=f"(d4.y), "=f"(d4.z), "=f"(d4.w) : "r"(sdx + 16 * m));
+                    const uint64_t t0 = math == 3 ? pack2(__int_as_float((int)v[4 * m]), __int_as_float((int)v[4 * m + 1]))
+                                                  : pack2(__int2float_rn((int)v[4 * m]), __int2float_rn((int)v[4 * m + 1]));
+                    const uint64_t t1 = math == 3 ? pack2(__int_as_float((int)v[4 * m + 2]), __int_as_float((int)v[4 * m + 3]))
+                                                  : pack2(__int2float_rn((int)v[4 * m + 2]), __int2float_rn((int)v[4 * m + 3]));
+                    const uint64_t s0 = f2x_mul(dw2, pack2(d4.x, d4.y));
+                    const uint64_t s1 = f2x_mul(dw2, pack2(d4.z, d4.w));
+                    acc[2 * m] = f2x_add(acc[2 * m], f2x_fma(t0, s0, nz2));
+                    acc[2 * m + 1] = f2x_add(acc[2 * m + 1], f2x_fma(t1, s1, nz2));
+                }
+            } else {
+                x ^= v[0] ^ v[31];
+            }
+            if (math == 2) {
+                tc_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[b]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 16; ++m) x ^= (uint32_t)acc[m];
+        if (x == 0x12345678u) out[blockIdx.x].pad = 1;
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+    if (warp == 1 && lane == 0) {
+        out[blockIdx.x].mma_cyc = cyc;
+        out[blockIdx.x].mma_n = iters;
+    }
+}
+
+
+// Pipe sharing: per iteration 4 int->f32 conversions and 6 f32x2 operations (mode 0), the
+// conversions alone (1), the f32x2 operations alone (2); independent chains, 1024 threads per SM.
+__global__ void __launch_bounds__(1024) k_mix(int mode, int iters, long long *cyc, int *sink) {
+    int iv[4];
+    uint64_t a[6];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) iv[j] = threadIdx.x * 4 + j;
+#pragma unroll
+    for (int j = 0; j < 6; ++j) a[j] = pack2(1.0f + j * 1e-3f, 1.0f - j * 1e-3f);
+    const uint64_t b = pack2(0.99999f, 1.00001f);
+    const long long c0 = clock64();
+    for (int i = 0; i < iters; ++i) {
+        if (mode != 2) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) iv[j] = __float_as_int(__int2float_rn(iv[j]));
+        }
+        if (mode != 1) {
+#pragma unroll
+            for (int j = 0; j < 6; ++j) a[j] = f2x_mul(a[j], b);
+        }
+    }
+    const long long c1 = clock64();
+    uint64_t x = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x ^= (uint32_t)iv[j];
+#pragma unroll
+    for (int j = 0; j < 6; ++j) x ^= a[j];
+    if (x == 0x12345678ull) sink[0] = 1;
+    if (threadIdx.x == 0) cyc[blockIdx.x] = c1 - c0;
+}
+
+
+// The epilogue of 16 positions of one block: t = (float)D, s = dw * dx, acc += t * s (rounded).
+__device__ __forceinline__ void epi16(const uint32_t (&v)[16], uint64_t dw2, uint32_t sdx, uint64_t *acc) {
+    const uint64_t nz2 = 0x8000000080000000ull;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        float4 d4;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(d4.x), "=f"(d4.y), "=f"(d4.z), "=f"(d4.w) : "r"(sdx + 16 * m));
+        const uint64_t t0 = pack2(__int2float_rn((int)v[4 * m]), __int2float_rn((int)v[4 * m + 1]));
+        const uint64_t t1 = pack2(__int2float_rn((int)v[4 * m + 2]), __int2float_rn((int)v[4 * m + 3]));
+        const uint64_t s0 = f2x_mul(dw2, pack2(d4.x, d4.y));
+        const uint64_t s1 = f2x_mul(dw2, pack2(d4.z, d4.w));
+        acc[2 * m] = f2x_add(acc[2 * m], f2x_fma(t0, s0, nz2));
+        acc[2 * m + 1] = f2x_add(acc[2 * m + 1], f2x_fma(t1, s1, nz2));
+    }
+}
+
+// Ring with software-pipelined tensor-memory loads: each warp's 32 columns as two 16-column
+// halves; the next half's load is in flight while the current half is computed.
+__global__ void __launch_bounds__(18 * 32, 1) k_ring2(int iters, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t full[4], empty[4], done;
+    __shared__ uint32_t taddr_s;
+    __shared__ __align__(16) float dx_s[128];
+    __shared__ float dw_s[128];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < (128 * 128 + 256 * 128) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = (uint32_t)(i * 2654435761u) & 0x3C3C3C3Cu;
+    for (int i = tid; i < 128; i += blockDim.x) dx_s[i] = 1.0f + i * 0.001f, dw_s[i] = 0.5f + i * 0.002f;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < 4; ++b) mbar_init(&full[b], 1), mbar_init(&empty[b], 16);
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    long long cyc = 0;
+    if (warp == 1) {
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 128 * 128, 128 * 16, 128, 0);
+        const uint32_t id = idesc_i8(128, 128);
+        const long long c0 = clock64();
+        bool ok = true;
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            if (i >= 4) ok = __all_sync(0xffffffffu, ring_wait(&empty[b], (uint32_t)(((i >> 2) - 1) & 1), 0, flag));
+            tc_after();
+            mma_i8_elect(taddr + (uint32_t)(b * 128), da, db, id, 0u);
+            mma_commit_elect(&full[b]);
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        cyc = clock64() - c0;
+    } else if (warp >= 2) {
+        const int q = warp & 3, k = (warp - 2) >> 2;
+        const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * k);
+        uint64_t acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc[m] = 0ull;
+        const uint32_t sdx = smem_u32(dx_s) + 128 * k;
+        const float dw = dw_s[32 * q + lane];
+        const uint64_t dw2 = pack2(dw, dw);
+        uint32_t va[16], vb[16];
+        bool ok = __all_sync(0xffffffffu, ring_wait(&full[0], 0, 0, flag));
+        tc_after();
+        ld16(tcol, va);
+        ld16_wait(va);
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            ld16(tcol + (uint32_t)(b * 128 + 16), vb);  // second half in flight
+            epi16(va, dw2, sdx, acc);
+            ld16_wait(vb);
+            tc_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[b]);  // both halves are in registers
+            if (i + 1 < iters) {
+                const int b1 = (i + 1) & 3;
+                ok = __all_sync(0xffffffffu, ring_wait(&full[b1], (uint32_t)(((i + 1) >> 2) & 1), 0, flag));
+                tc_after();
+                ld16(tcol + (uint32_t)(b1 * 128), va);  // next block's first half in flight
+            }
+            epi16(vb, dw2, sdx + 64, acc + 8);
+            ld16_wait(va);
+        }
+        uint32_t x = 0;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) x ^= (uint32_t)acc[m];
+        if (x == 0x12345678u) out[blockIdx.x].pad = 1;
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+    if (warp == 1 && lane == 0) {
+        out[blockIdx.x].mma_cyc = cyc;
+        out[blockIdx.x].mma_n = iters;
+    }
+}
+
+
+// Accumulate chains over rotating buffers: per block `chain` f16 MMAs (M = N = 128, K = 16) into
+// one of 4 tensor-memory buffers, the first with accumulate off; kind 0: i8 (K = 32) for reference.
+__device__ __forceinline__ void mma_f16_elect(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+// The same MMAs with the accumulate flag as an immediate (ptxas sees a constant predicate).
+template <bool ACC>
+__device__ __forceinline__ void mma_i8_k(uint32_t d, uint64_t a, uint64_t b, uint32_t id) {
+    if (ACC)
+        asm volatile("{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+                     "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d), "l"(a), "l"(b), "r"(id)
+                     : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, 0, 0;\n\t"
+                     "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d), "l"(a), "l"(b), "r"(id)
+                     : "memory");
+}
+template <bool ACC>
+__device__ __forceinline__ void mma_f16_k(uint32_t d, uint64_t a, uint64_t b, uint32_t id) {
+    if (ACC)
+        asm volatile("{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+                     "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d), "l"(a), "l"(b), "r"(id)
+                     : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, 0, 0;\n\t"
+                     "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d), "l"(a), "l"(b), "r"(id)
+                     : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1) k_chain(int kind, int chain, int blocks, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t done;
+    __shared__ uint32_t taddr_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < (128 * 128 + 256 * 128) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = (uint32_t)(i * 2654435761u) & 0x3C3C3C3Cu;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    if (warp == 0) {
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 128 * 128, 128 * 16, 128, 0);
+        const uint32_t id = (kind & 1) == 0 ? idesc_i8(128, 128) : idesc_f16(128, 128);
+        const long long c0 = clock64();
+        if (kind >= 2) {  // immediate predicates; kind 2: i8, 3: f16; chain 1 or 2
+            for (int i = 0; i < blocks; ++i) {
+                const uint32_t d = taddr + (uint32_t)((i & 3) * 128);
+                if (kind == 2) {
+                    mma_i8_k<false>(d, da, db, id);
+                    if (chain == 2) mma_i8_k<true>(d, da + 256, db + 256, id);
+                } else {
+                    mma_f16_k<false>(d, da, db, id);
+                    if (chain == 2) mma_f16_k<true>(d, da + 256, db + 256, id);
+                }
+            }
+        } else {
+            for (int i = 0; i < blocks; ++i) {
+                const uint32_t d = taddr + (uint32_t)((i & 3) * 128);
+                for (int c = 0; c < chain; ++c) {
+                    if (kind == 0)
+                        mma_i8_elect(d, da + 256 * (c & 1), db + 256 * (c & 1), id, c ? 1u : 0u);
+                    else
+                        mma_f16_elect(d, da + 256 * (c & 1), db + 256 * (c & 1), id, c ? 1u : 0u);
+                }
+            }
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        const long long c1 = clock64();
+        if (lane == 0) {
+            out[blockIdx.x].mma_cyc = c1 - c0;
+            out[blockIdx.x].mma_n = blocks;
+        }
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+}
+
+
+// The GEMM's skeleton, factor by factor. One MMA warp, 16 epilogue warps (lane quarter x 32
+// positions each), 2 writer warps; 4 tensor-memory buffers; M = N = 128. flags:
+//   1: f16, two chained MMAs per block with immediate accumulate flags (else one i8 MMA)
+//   2: operands rotate over 5 stage buffers of 34 KB (else one fixed tile)
+//   4: epilogue arithmetic (scale product, rounded product, sum per value)
+//   8: writer warps store 16 KB of operand bytes per block into the stage buffers (as the unpack
+//      warps do), with fence.proxy.async, paced by the MMA warp through a barrier
+__global__ void __launch_bounds__(20 * 32, 1) k_ring3(int flags, int iters, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t full[4], empty[4], done, wfull[5], wempty[5];
+    __shared__ uint32_t taddr_s;
+    __shared__ __align__(16) float dx_s[128];
+    __shared__ float dw_s[128];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool f16 = flags & 1, rot = flags & 2, math = flags & 4, wr = flags & 8;
+    for (int i = tid; i < 5 * 34816 / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = f16 ? 0x3C003C00u : ((uint32_t)(i * 2654435761u) & 0x3C3C3C3Cu);
+    for (int i = tid; i < 128; i += blockDim.x) dx_s[i] = 1.0f + i * 0.001f, dw_s[i] = 0.5f + i * 0.002f;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < 4; ++b) mbar_init(&full[b], 1), mbar_init(&empty[b], 16);
+        for (int b = 0; b < 5; ++b) mbar_init(&wfull[b], 2), mbar_init(&wempty[b], 1);
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    const uint32_t sb = smem_u32(smem);
+    long long cyc = 0;
+    if (warp == 1) {
+        const uint32_t id = f16 ? idesc_f16(128, 128) : idesc_i8(128, 128);
+        const long long c0 = clock64();
+        bool ok = true;
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            const int st = rot ? (i >> 1) % 5 : 0;          // 2 blocks per stage
+            const uint32_t base = sb + st * 34816 + (rot ? (i & 1) * 8192 : 0);
+            if (wr && (i & 1) == 0) ok = __all_sync(0xffffffffu, ring_wait(&wfull[st], (uint32_t)((i / 10) & 1), 0, flag));
+            if (i >= 4) ok = ok && __all_sync(0xffffffffu, ring_wait(&empty[b], (uint32_t)(((i >> 2) - 1) & 1), 0, flag));
+            tc_after();
+            const uint64_t da = desc_l(smem + (base - sb) + 17408, 2048, 128, 0);
+            const uint64_t db = desc_l(smem + (base - sb), 2048, 128, 0);
+            const uint32_t d = taddr + (uint32_t)(b * 128);
+            if (f16) {
+                mma_f16_k<false>(d, da, db, id);
+                mma_f16_k<true>(d, da + 256, db + 256, id);
+            } else {
+                mma_i8_k<false>(d, da, db, id);
+            }
+            mma_commit_elect(&full[b]);
+            if (wr && (i & 1) == 1) mma_commit_elect(&wempty[st]);
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        cyc = clock64() - c0;
+    } else if (warp >= 2 && warp < 4) {
+        if (wr) {  // writers: per stage (2 blocks) 16 KB of operand bytes, one stage ahead of the MMAs
+            const int r = tid - 64;
+            bool ok = true;
+            for (int s2 = 0; s2 < iters / 2 && ok; ++s2) {
+                const int st = s2 % 5;
+                if (s2 >= 5) ok = __all_sync(0xffffffffu, ring_wait(&wempty[st], (uint32_t)(((s2 / 5) - 1) & 1), 0, flag));
+                uint4 *a = reinterpret_cast<uint4 *>(smem + st * 34816 + 17408);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) a[(k * 128 + r + 64 * h) % 1024] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wfull[st]);
+            }
+        }
+    } else if (warp >= 4) {
+        const int q = warp & 3, k = (warp - 4) >> 2;
+        const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * k);
+        const uint64_t nz2 = 0x8000000080000000ull;
+        uint64_t acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc[m] = 0ull;
+        const uint32_t sdx = smem_u32(dx_s) + 128 * k;
+        const float dw = dw_s[32 * q + lane];
+        const uint64_t dw2 = pack2(dw, dw);
+        uint32_t x = 0;
+        bool ok = true;
+        for (int i = 0; i < iters && ok; ++i) {
+            const int b = i & 3;
+            ok = __all_sync(0xffffffffu, ring_wait(&full[b], (uint32_t)((i >> 2) & 1), 0, flag));
+            tc_after();
+            uint32_t v[32];
+            ld32(tcol + (uint32_t)(b * 128), v);
+            ld_wait(v);
+            tc_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[b]);
+            if (math) {
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    float4 d4;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(d4.x), "=f"(d4.y), "=f"(d4.z), "=f"(d4.w) : "r"(sdx + 16 * m));
+                    const uint64_t t0 = ((uint64_t)v[4 * m + 1] << 32) | v[4 * m];
+                    const uint64_t t1 = ((uint64_t)v[4 * m + 3] << 32) | v[4 * m + 2];
+                    const uint64_t s0 = f2x_mul(dw2, pack2(d4.x, d4.y));
+                    const uint64_t s1 = f2x_mul(dw2, pack2(d4.z, d4.w));
+                    acc[2 * m] = f2x_add(acc[2 * m], f2x_fma(t0, s0, nz2));
+                    acc[2 * m + 1] = f2x_add(acc[2 * m + 1], f2x_fma(t1, s1, nz2));
+                }
+            } else {
+                x ^= v[0] ^ v[31];
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 16; ++m) x ^= (uint32_t)acc[m];
+        if (x == 0x12345678u) out[blockIdx.x].pad = 1;
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+    if (warp == 1 && lane == 0) {
+        out[blockIdx.x].mma_cyc = cyc;
+        out[blockIdx.x].mma_n = iters;
+    }
+}
+
+
+// Legacy warp-level MMA throughput: 8 independent accumulator chains per warp, 1024 threads per SM.
+// kind 0: mma.sync m16n8k16 f16 x f16 -> f32; kind 1: m16n8k32 s8 x s8 -> s32.
+__global__ void __launch_bounds__(1024) k_mmasync(int kind, int iters, long long *cyc, int *sink) {
+    float c[8][4];
+    int ci[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) c[j][k] = 0.0f, ci[j][k] = 0;
+    const uint32_t a0 = 0x3C003C00u + threadIdx.x, a1 = a0 ^ 1, a2 = a0 ^ 2, a3 = a0 ^ 3, b0 = 0x3C003C00u, b1 = b0 ^ 4;
+    const long long c0 = clock64();
+    for (int i = 0; i < iters; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (kind == 0)
+                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                             : "+f"(c[j][0]), "+f"(c[j][1]), "+f"(c[j][2]), "+f"(c[j][3])
+                             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+            else
+                asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                             : "+r"(ci[j][0]), "+r"(ci[j][1]), "+r"(ci[j][2]), "+r"(ci[j][3])
+                             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        }
+    }
+    const long long c1 = clock64();
+    float x = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x += c[j][0] + (float)ci[j][0];
+    if (x == 1234.5f) sink[0] = 1;
+    if (threadIdx.x == 0) cyc[blockIdx.x] = c1 - c0;
+}
+
+
+// MMA throughput under contention: one warp issues f16 chains of 2 MMAs (M = N = 128, K = 16)
+// into 4 rotating buffers; 16 other warps, for the whole time, either idle (mode 0), issue
+// tcgen05.ld 32x32b.x32 of other columns (1), or issue ld.shared.v4 broadcasts (2).
+__global__ void __launch_bounds__(18 * 32, 1) k_contend(int mode, int blocks, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t done;
+    __shared__ uint32_t taddr_s;
+    __shared__ volatile int stop;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < (128 * 128 + 256 * 128) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t *>(smem)[i] = 0x3C003C00u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&done, 1);
+        stop = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    if (warp == 1) {
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 128 * 128, 128 * 16, 128, 0);
+        const uint32_t id = idesc_f16(128, 128);
+        const long long c0 = clock64();
+        for (int i = 0; i < blocks; ++i) {
+            const uint32_t d = taddr + (uint32_t)((i & 3) * 128);
+            mma_f16_k<false>(d, da, db, id);
+            mma_f16_k<true>(d, da + 256, db + 256, id);
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        const long long c1 = clock64();
+        if (lane == 0) {
+            out[blockIdx.x].mma_cyc = c1 - c0;
+            out[blockIdx.x].mma_n = blocks;
+            stop = 1;
+        }
+    } else if (warp >= 2 && mode != 0) {
+        const int q = warp & 3;
+        uint32_t x = 0;
+        long long n = 0;
+        while (!stop && n < (1ll << 22)) {
+            if (mode == 1) {
+                uint32_t v[32];
+                ld32(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)((n & 3) * 128 + 32 * ((warp - 2) >> 2)), v);
+                ld_wait(v);
+                x ^= v[0] ^ v[31];
+            } else {
+                float4 d4;
+                asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(d4.x), "=f"(d4.y), "=f"(d4.z), "=f"(d4.w) : "r"((uint32_t)(smem_u32(smem) + 16 * (uint32_t)(n & 255))));
+                x ^= __float_as_uint(d4.x) ^ __float_as_uint(d4.w);
+            }
+            ++n;
+        }
+        if (x == 0x12345678u) out[blockIdx.x].pad = 1;
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+}
+
 int g_sms = 148;
 
 double run_simple(void (*k)(int, long long *, int *), int iters, const char *name, double ops_per_thread_iter) {
@@ -530,6 +1220,127 @@ void run_mma(int kind, int layout, int m, int n, int iters, int lat, int issuers
     CK(cudaFree(out));
 }
 
+
+void run_issue(int style, int iters, int *flag) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_issue<<<g_sms, 128, SMEM_BYTES>>>(style, 400, out, flag);
+    CK(cudaDeviceSynchronize());
+    k_issue<<<g_sms, 128, SMEM_BYTES>>>(style, iters, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0, iss = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms, iss += (double)h[i].ld_cyc / g_sms;
+    printf("{\"probe\": \"issue\", \"style\": %d, \"iters\": %d, \"cyc_per_mma_total\": %.1f, "
+           "\"cyc_per_mma_issue\": %.1f, \"timeout\": %d}\n", style, iters, tot / iters, iss / iters, hf);
+    CK(cudaFree(out));
+}
+
+
+void run_ring(int spin, int iters, int *flag, int math = 0) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_ring<<<g_sms, 18 * 32, SMEM_BYTES>>>(spin, 200, out, flag, math);
+    CK(cudaDeviceSynchronize());
+    k_ring<<<g_sms, 18 * 32, SMEM_BYTES>>>(spin, iters, out, flag, math);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"ring\", \"spin\": %d, \"math\": %d, \"iters\": %d, \"cyc_per_block\": %.1f, \"timeout\": %d}\n",
+           spin, math, iters, tot / iters, hf);
+    CK(cudaFree(out));
+}
+
+
+void run_ring2(int iters, int *flag) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_ring2<<<g_sms, 18 * 32, SMEM_BYTES>>>(200, out, flag);
+    CK(cudaDeviceSynchronize());
+    k_ring2<<<g_sms, 18 * 32, SMEM_BYTES>>>(iters, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"ring2 (pipelined loads)\", \"iters\": %d, \"cyc_per_block\": %.1f, \"timeout\": %d}\n", iters,
+           tot / iters, hf);
+    CK(cudaFree(out));
+}
+
+
+void run_chain(int kind, int chain, int blocks, int *flag) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_chain<<<g_sms, 128, SMEM_BYTES>>>(kind, chain, 100, out, flag);
+    CK(cudaDeviceSynchronize());
+    k_chain<<<g_sms, 128, SMEM_BYTES>>>(kind, chain, blocks, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"chain\", \"kind\": \"%s\", \"chain\": %d, \"cyc_per_block\": %.1f, \"cyc_per_mma\": %.1f, \"timeout\": %d}\n",
+           (kind & 1) == 0 ? (kind ? "i8 imm" : "i8") : (kind == 3 ? "f16 imm" : "f16"), chain, tot / blocks, tot / blocks / chain, hf);
+    CK(cudaFree(out));
+}
+
+
+void run_ring3(int flags, int iters, int *flag) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_ring3<<<g_sms, 20 * 32, 5 * 34816 + 2048>>>(flags, 200, out, flag);
+    CK(cudaDeviceSynchronize());
+    k_ring3<<<g_sms, 20 * 32, 5 * 34816 + 2048>>>(flags, iters, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"ring3\", \"flags\": %d, \"f16x2\": %d, \"rotate\": %d, \"math\": %d, \"writers\": %d, "
+           "\"cyc_per_block\": %.1f, \"timeout\": %d}\n", flags, flags & 1, (flags >> 1) & 1, (flags >> 2) & 1, (flags >> 3) & 1,
+           tot / iters, hf);
+    CK(cudaFree(out));
+}
+
+
+void run_contend(int mode, int blocks, int *flag) {
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    k_contend<<<g_sms, 18 * 32, SMEM_BYTES>>>(mode, 100, out, flag);
+    CK(cudaDeviceSynchronize());
+    k_contend<<<g_sms, 18 * 32, SMEM_BYTES>>>(mode, blocks, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"contend\", \"mode\": \"%s\", \"cyc_per_block\": %.1f, \"timeout\": %d}\n",
+           mode == 0 ? "mma alone" : mode == 1 ? "with 16 tmem-load warps" : "with 16 lds warps", tot / blocks, hf);
+    CK(cudaFree(out));
+}
+
 }  // namespace
 
 int main() {
@@ -541,14 +1352,11 @@ int main() {
     CK(cudaMalloc(&flag, 4));
     CK(cudaMemset(flag, 0, 4));
     CK(cudaFuncSetAttribute(k_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    // kind, layout, m, n, iters, latency, issuers, kchain, ctas per SM, flag, uniform warp
-    for (int n : {64, 128, 256}) run_mma(0, 2, 128, n, 4000, 0, 1, 1, 1, flag, 1);
-    run_mma(0, 2, 128, 256, 4000, 0, 1, 4, 1, flag, 1);
-    run_mma(0, 2, 128, 256, 4000, 0, 2, 1, 1, flag, 1);
-    run_mma(0, 0, 128, 256, 4000, 0, 1, 1, 1, flag, 1);
-    run_mma(0, 2, 128, 256, 500, 1, 1, 1, 1, flag, 1);    // latency
-    run_mma(0, 2, 128, 128, 500, 1, 1, 1, 1, flag, 1);
-    run_mma(0, 2, 128, 256, 4000, 0, 1, 1, 1, flag, 0);   // single-lane branch, for comparison
+    CK(cudaFuncSetAttribute(k_issue, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    CK(cudaFuncSetAttribute(k_ring, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    CK(cudaFuncSetAttribute(k_ring2, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    CK(cudaFuncSetAttribute(k_contend, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    for (int mode : {0, 1, 2}) run_contend(mode, 4000, flag);
     CK(cudaFree(flag));
     return 0;
 }

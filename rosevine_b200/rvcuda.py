@@ -314,7 +314,7 @@ def debug_gemm_block_dots(w: MoeWeights, which: int, expert: int, row_tile: int,
     k = w.n_embd if which == 0 else w.ff
     nblk = k // 32
     sv = view_of(scratch)
-    check(lib().rvc_debug_gemm_block_dots(ctypes.byref(w), which, expert, row_tile, _ptr(records, n * (k // 32) * 40),
+    check(lib().rvc_debug_gemm_block_dots(ctypes.byref(w), which, expert, row_tile, _ptr(records, n * (k // 32) * 64),
                                           n, _ptr(out, nblk * 128 * 128 * 4), sv.need(256 + nblk * 4 * ((n + 3) // 4 * 4)),
                                           sv.nbytes, stream))
 

@@ -78,7 +78,7 @@ def simulate_ep(world, x_bits, bias, weights):
         i, w = be.route(x, b)
         send, cnt, owner = be.pack(x, i, w)
         sends.append(send.clone())
-        counts.append(cnt)
+        counts.append(cnt.tolist())
         owners.append(owner.clone())
         ids.append(i.cpu().numpy())
     offs = [np.concatenate([[0], np.cumsum(c)]).astype(np.int64) for c in counts]

@@ -1,8 +1,9 @@
 """GPU parity of the prefill path (batches above 16 tokens: the grouped expert GEMMs).
 
-The grouped GEMM (k_pf_gemm_tc) forms each 32-column block's int32 dot on the tensor cores
-(tcgen05.mma kind::i8 into tensor memory) and scales and accumulates the dots on the CUDA cores
-in the scalar reference's order, each operation rounded where the reference rounds it
+The grouped GEMM (k_pf_gemm_tc) forms each 32-column block's integer dot on the tensor cores
+(tcgen05.mma into tensor memory, the integer operands held exactly as f16, f32 accumulation exact
+for these integers) and scales and accumulates the dots on the CUDA cores in the scalar
+reference's order, each operation rounded where the reference rounds it
 (expert_kernel.rs:147-161). The first tests read the block dots of one tile straight from the
 production kernel (its debug mode writes them instead of scaling them) and compare them with the
 exact integer dots; the layer tests compare rvc_moe_forward with the oracle's scalar kernel:
@@ -17,15 +18,11 @@ pytestmark = pytest.mark.gpu
 
 
 def _records(xq: np.ndarray) -> np.ndarray:
-    """Reference Q8_0 rows (34-byte blocks: f16 d, 32 int8) -> this backend's records (per block
-    32 int8, then the f32 scales, then the int32 quant sums)."""
+    """Reference Q8_0 rows (34-byte blocks: f16 d, 32 int8) -> the prefill GEMM's activation
+    operand rows: each block's 32 quants as f16 integers (exact), 64 bytes per block."""
     n, nb = xq.shape[0], xq.shape[1] // 34
-    blk = xq.reshape(n, nb, 34)
-    q = blk[:, :, 2:].copy()
-    d = blk[:, :, :2].copy().view(np.float16).reshape(n, nb).astype(np.float32)
-    sums = q.view(np.int8).astype(np.int32).sum(axis=2, dtype=np.int32)
-    return np.concatenate([q.reshape(n, -1), d.view(np.uint8).reshape(n, -1), sums.view(np.uint8).reshape(n, -1)],
-                          axis=1)
+    q = xq.reshape(n, nb, 34)[:, :, 2:].copy().view(np.int8)
+    return np.ascontiguousarray(q.astype(np.float16).reshape(n, nb * 32)).view(np.uint8)
 
 
 def _block_dots_want(mat: np.ndarray, xq: np.ndarray) -> np.ndarray:
