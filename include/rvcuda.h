@@ -62,6 +62,14 @@ int rvc_download_async(void *dst, const void *src, size_t bytes, void *stream);
 int rvc_event_record_on(void *ev, void *stream);
 int rvc_stream_sync(void *stream);
 
+/* ---------------------------------------------------------------- norms
+ * rvh_rms_norm (rvhip.h:43, rvhip.hip:75-90) with a stream: per row of x [rows][width] f32,
+ * mean of squares summed in f64 and rounded to f32, scale = 1 / sqrt(mean + eps), out =
+ * x * scale (* post when post != 1) (* weight[i] when weight is not NULL). out may be x. The
+ * MoE branch's three norms (hip_exec.rs:786, :796, :846) call this. */
+int rvc_rms_norm(const float *x, float *out, const float *weight, int rows, int width, float eps, float post,
+                 void *stream);
+
 /* ------------------------------------------------------------- MoE layer */
 
 /* Weights of one MoE layer, as runtime/src/model.rs:11-41 binds them (gate_inp,
@@ -80,7 +88,9 @@ typedef struct rvc_moe_weights {
     const float *down_scale;  /* device [n_experts], or NULL for all ones */
 } rvc_moe_weights;
 
-/* Bytes of the packed expert planes (equal to the GGUF bytes of both tensors). */
+/* Bytes of the packed expert planes: the GGUF bytes of both tensors (nibble and f16 scale
+ * planes) plus, for shapes the prefill GEMM takes (2 ff and n_embd multiples of 128), an f32
+ * copy of the scales in 128-row tiles. */
 size_t rvc_packed_bytes(int n_experts, int n_embd, int ff);
 
 /* One-time repack at upload, replacing the raw uploads of runtime/src/hip_exec.rs:429-433.

@@ -43,6 +43,7 @@ def lib() -> ctypes.CDLL:
         L.rvo_quantize_q8_0.argtypes, L.rvo_quantize_q8_0.restype = [P, I, P], None
         L.rvo_gelu.argtypes, L.rvo_gelu.restype = [F], F
         L.rvo_softmax.argtypes, L.rvo_softmax.restype = [P, I], None
+        L.rvo_rms_norm.argtypes, L.rvo_rms_norm.restype = [P, P, P, I, I, F, F], None
         L.rvo_top_k.argtypes, L.rvo_top_k.restype = [P, I, I, P], None
         L.rvo_router_logits.argtypes = [P, I, P, I, P, I, I, I, I, P]
         L.rvo_router_logits.restype = None
@@ -93,6 +94,16 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     out = np.zeros((rows, k // 32 * 34), np.uint8)
     for r in range(rows):
         lib().rvo_quantize_q8_0(_p(x.reshape(rows, k)[r:r + 1]), k, _p(out[r:r + 1]))
+    return out
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray | None = None, eps: float = 1e-6, post: float = 1.0) -> np.ndarray:
+    """rvo_rms_norm over the rows of x [rows, width] f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, width = x.shape
+    out = np.empty_like(x)
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    lib().rvo_rms_norm(_p(x), _p(out), _p(w), rows, width, eps, post)
     return out
 
 

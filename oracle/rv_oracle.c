@@ -125,6 +125,24 @@ float rvo_gelu(float x) {
     return (0.5f * x) * (1.0f + rvo_tanhf(inner));
 }
 
+/* ops.rs:131-139 row by row, with rvhip.hip:84-88's post factor between scale and weight. */
+void rvo_rms_norm(const float *x, float *out, const float *weight, int rows, int width, float eps, float post) {
+    for (int r = 0; r < rows; ++r) {
+        const float *xr = x + (size_t)r * width;
+        float *o = out + (size_t)r * width;
+        double sum = 0.0;
+        for (int i = 0; i < width; ++i) sum += (double)xr[i] * (double)xr[i];
+        const float mean = (float)(sum / (double)width);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        for (int i = 0; i < width; ++i) {
+            float v = xr[i] * scale;
+            if (post != 1.0f) v = v * post;
+            if (weight) v = v * weight[i];
+            o[i] = v;
+        }
+    }
+}
+
 /* Softmax with f32 exp and an f64 sum, scaled by (1/sum) rounded to f32 (ops.rs:170-179). */
 void rvo_softmax(float *x, int n) {
     float mx = -INFINITY;

@@ -55,6 +55,11 @@ void rvo_top_k(const float *x, int n, int k, int32_t *idx);
  * sequential f32, plus bias[t * bias_stride + e] when bias != NULL. */
 void rvo_router_logits(const void *x, int x_dtype, const void *w, int w_dtype, const float *bias, int bias_stride,
                        int n_tok, int n_embd, int n_experts, float *logits);
+/* RMS norm of `rows` rows of `width` f32 (ops.rs:131-139; the HIP executor's rvh_rms_norm
+ * contract, runtime/hip/rvhip.h:43 and rvhip.hip:75-90, adds `post`): sum of squares in f64,
+ * mean rounded to f32, scale = 1 / sqrt(mean + eps) in f32, out = x * scale (* post when
+ * post != 1) (* weight[i] when weight is given), each product rounded. out may equal x. */
+void rvo_rms_norm(const float *x, float *out, const float *weight, int rows, int width, float eps, float post);
 /* exec.rs:507-517: softmax, top `used`, renormalise with the 2^-14 clamp.
  * logits are overwritten by probabilities. */
 void rvo_select_experts(float *logits, int n_tok, int n_experts, int used, int32_t *ids, float *weights);

@@ -12,8 +12,11 @@
 // tail of a down row: 22 blocks per row for ff = 704), so that threads reading block b of 8
 // consecutive rows hit distinct shared-memory banks. Gate_up rows hold a multiple of 8
 // blocks. Scales are not swizzled.
-// Nibble bytes and scale bits are copied unchanged, so every dot product sees the same
-// integers and scales as the reference.
+// The prefill GEMM reads the scales a third time, as f32 in a tile-major plane: 128-row tiles
+// of packed rows, per tile [block][row] (one block's scales of a tile are 512 contiguous bytes,
+// a stage's copy a single bulk transfer). Rows are padded up to a multiple of 128.
+// Nibble bytes and scale bits are copied unchanged (the f32 scales are the f16 values exactly),
+// so every dot product sees the same integers and scales as the reference.
 #pragma once
 #include "common.cuh"
 
@@ -25,7 +28,11 @@ struct PackedView {
     const uint16_t *gu_scl;  // [E][2*ff][nb]
     const uint8_t *dn_nib;   // [E][n_embd][nbh][16]
     const uint16_t *dn_scl;  // [E][n_embd][nbh]
+    const float *gu_dw;      // [E * 2*ff / 128][nb][128] f32
+    const float *dn_dw;      // [E * n_embd / 128][nbh][128] f32
 };
+
+constexpr int DW_TILE = 128;  // rows per tile of the f32 scale planes
 
 // Position of nibble block b in a packed row of nblk blocks whose row index has low bits key.
 __host__ __device__ __forceinline__ int nib_pos(int b, int nblk, int key) { return b < (nblk & ~7) ? (b ^ key) : b; }
@@ -52,6 +59,16 @@ __global__ void k_pack_q4(const uint8_t *__restrict__ src, int n_experts, int ro
         for (int j = 0; j < 4; ++j) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
         *reinterpret_cast<uint4 *>(nib + dnib * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         scl[dst] = h[0];
+    }
+}
+
+// The f32 tile-major scale plane from the packed f16 plane [E * rows][nblk] (rows per expert a
+// multiple of DW_TILE, so no tile straddles two experts).
+__global__ void k_pack_dw(const uint16_t *__restrict__ scl, size_t n_rows, int nblk, float *__restrict__ dw) {
+    const size_t total = n_rows * nblk;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i % DW_TILE, b = (i / DW_TILE) % nblk, t = i / ((size_t)DW_TILE * nblk);
+        dw[i] = f16_bits_to_f32(scl[(t * DW_TILE + r) * nblk + b]);
     }
 }
 

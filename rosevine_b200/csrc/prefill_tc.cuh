@@ -30,19 +30,24 @@
 //   - the epilogue's three f32 operations per (row, position, block) bound the kernel.
 //
 // Roles (one CTA per SM, persistent over the (row tile, position tile) list):
-//   warp 0       tensor-memory allocation; TMA copies of a stage (2 blocks): activation quants
-//                [8 K chunks][128 positions][16 B] (the MMA's K-major B layout as stored) and
-//                activation scales [2][128] f32. Five stages in shared memory: the copies and the
-//                unpacking of a stage start up to 6 blocks before its MMAs (a stage's copy takes
-//                about 2 us; with the MMAs 4 blocks ahead of the epilogue, fewer stages expose it)
+//   warp 0       tensor-memory allocation; the copies of a stage (2 blocks), all by TMA / bulk
+//                copy: the weight nibbles of the tile's 128 rows (four 1 KB tensor copies, one per
+//                swizzle key pair of the packed plane, below), then the activation quants of 128
+//                positions x 128 B (one tensor copy in the 128-byte swizzle layout, which the MMA
+//                reads as its K-major B operand: a copy of 16-byte rows instead ran at about 12 B
+//                per SM cycle and bounded the kernel), activation scales [2][128] f32 and weight
+//                scales [2][128] f32 (the tile-major scale plane). Five stages in shared memory
+//                run up to 10 blocks ahead of the MMAs
 //   warp 1       MMA issue (the whole warp runs the loop; one elected lane issues)
-//   warps 2-3    weight unpack: thread r turns rows r and r + 64's nibbles (read from global one
-//                stage ahead; the packed plane swizzles blocks within complete groups of 8:
-//                nib_pos in pack.cuh) into f16 n - 8 in the MMA's K-major A layout, and their
-//                f16 scales into an f32 table
+//   warps 2-3    weight unpack: thread r turns rows r and r + 64's nibbles (shared memory) into
+//                f16 n - 8 in the MMA's K-major A layout
 //   warps 4-19   epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (one weight row
 //                per thread) and positions 32 ((w - 4) / 4) .. + 31; per block and position
 //                s = dw * dx, p = t * s (rounded product), acc = acc + p.
+// The packed nibble plane stores row R's block b at b ^ (R & 7) within complete groups of 8 blocks
+// (pack.cuh). A stage's block pair (2 st, 2 st + 1) of row R = 8 g + 2 k + j then sits in stored
+// pair st ^ k with its blocks in order i ^ j: viewed as [g][k][j][pair][32 B], one tensor copy per
+// k of box [16 g][2 j][one pair] fetches the stage's nibbles of a whole row tile.
 // Every wait is bounded; a wait that runs out records STATUS_TIMEOUT and ends the CTA's work
 // (all roles see the abort flag), after the MMAs and copies in flight have completed.
 #pragma once
@@ -66,12 +71,15 @@ constexpr int TC_THREADS = (4 + TC_EPI_WARPS) * 32;  // 640: up to 96 registers 
 // 8 c .. 8 c + 7. In shared memory a block's operand is [4 chunks][128 rows][16 B]; MMA k (k = 0,
 // 1) reads chunks 2 k, 2 k + 1 (lbo 2048 B between them, 8-row groups 128 B apart).
 constexpr int TC_BLK_BYTES = 4 * 128 * 16;                 // 8 KB
-constexpr int TC_OFF_B = 0;                                // [TC_KB blocks] activation operands
+constexpr int TC_OFF_B = 0;  // activation operands: [128 positions][TC_KB blocks x 64 B], 128-byte swizzle
 constexpr int TC_OFF_DX = TC_OFF_B + TC_KB * TC_BLK_BYTES;  // [TC_KB blocks][128 positions] f32 scales
-constexpr int TC_OFF_A = TC_OFF_DX + TC_KB * TC_N * 4;     // [TC_KB blocks] weight operands
-constexpr int TC_OFF_DW = TC_OFF_A + TC_KB * TC_BLK_BYTES;  // [TC_KB blocks][128 rows] f32 weight scales
-constexpr int TC_STAGE_BYTES = TC_OFF_DW + TC_KB * TC_M * 4;  // 34 KB
-constexpr int TC_TMA_BYTES = TC_OFF_A;                     // bytes the two copies of a stage write
+constexpr int TC_OFF_DW = TC_OFF_DX + TC_KB * TC_N * 4;    // [TC_KB blocks][128 rows] f32 weight scales
+constexpr int TC_OFF_NIB = TC_OFF_DW + TC_KB * TC_M * 4;   // [4 k][16 g][2 j][2 blocks][16 B] weight nibbles
+constexpr int TC_NIB_BYTES = TC_KB * TC_M * 16;            // 4 KB
+constexpr int TC_OFF_A = TC_OFF_NIB + TC_NIB_BYTES;        // [TC_KB blocks] weight operands (unpacked)
+constexpr int TC_STAGE_BYTES = TC_OFF_A + TC_KB * TC_BLK_BYTES;  // 38 KB
+constexpr int TC_FULL_BYTES = TC_OFF_NIB;                  // bytes the copies on full[] write (B, DX, DW)
+static_assert(TC_KB == 2, "a stage is one block pair of the swizzled nibble plane");
 // gate/up output exchange: per (unit, position half) pair of warps, gate values of 32 positions
 // and up values of 32 positions, [32][32 columns] f32 each
 constexpr int TC_OFF_STG = TC_STAGES * TC_STAGE_BYTES;
@@ -91,9 +99,8 @@ struct TcArgs {
     int rows_per_expert;  // 2 ff (gate/up) or n_embd (down)
     int row_tiles;        // row tiles per position tile (rows_per_expert / TC_M)
     int row_base;         // first weight row of row tile 0 (0; another row tile for the debug check)
-    int nblk;             // K blocks (n_embd / 32 or ff / 32)
-    const uint8_t *nib;   // weight nibbles [E][rows][nblk][16 B] (packed plane, pack.cuh)
-    const uint16_t *scl;  // weight scales [E][rows][nblk] f16 bits
+    int nblk;             // K blocks (n_embd / 32 or ff / 32), even
+    const float *dwp;     // weight scales, tile-major [E * rows / 128][nblk][128] f32 (pack.cuh)
     int nh;               // (gate/up) h blocks per pair (ff / 32)
     uint8_t *hrec;        // (gate/up) out: h quants (pf_rec_bytes per plan position)
     float *hsc;           // (gate/up) out: h block scales, block-major [nh][ppad] f32
@@ -126,6 +133,16 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
+}
+
+// The same for a K-major operand in the 128-byte swizzle layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 B (64 f16 of K), 16-byte chunk c of row r stored at
+// chunk c ^ (r & 7), 8-row atoms 1024 B apart (sbo), atoms 1024-byte aligned (base offset 0);
+// the K step of an MMA inside the row advances the start address by 32 B (layout type 2 at
+// bits 61-63; lbo unused, 16 B).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
 // Instruction descriptor of kind::f16: f32 accumulator (bits 4-5 = 1), A and B f16 (bits 7-9 and
@@ -228,6 +245,21 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         "[%5];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            int c4, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+        "%6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
+        : "memory");
+}
+// Contiguous global -> shared copy (16-byte aligned addresses, a multiple of 16 bytes).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 // ------------------------------------------------------------------ f32x2 arithmetic
@@ -354,11 +386,12 @@ __device__ __forceinline__ bool tc_tile(const TcArgs &a, int L, int &e, int &nt,
 // ------------------------------------------------------------------ the kernel
 template <int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_constant__ CUtensorMap map_act,
-                                                              const __grid_constant__ CUtensorMap map_dx, TcArgs a) {
+                                                              const __grid_constant__ CUtensorMap map_dx,
+                                                              const __grid_constant__ CUtensorMap map_nib, TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base, as an offset from the shared array (keeps shared addressing)
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __shared__ uint64_t full[TC_STAGES], afull[TC_STAGES], empty[TC_STAGES];
+    __shared__ uint64_t full[TC_STAGES], wfull[TC_STAGES], afull[TC_STAGES], empty[TC_STAGES];
     __shared__ uint64_t tfull[TC_TBUF], tempty[TC_TBUF], drain;
     __shared__ int epi_ok;  // the epilogue leader's wait outcome, read by all epilogue warps after bar.sync
     __shared__ uint32_t taddr_s;
@@ -374,6 +407,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
     if (tid == 32) {
         for (int s = 0; s < TC_STAGES; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&wfull[s], 1);
             mbar_init(&afull[s], 2);                     // the two unpack warps
             mbar_init(&empty[s], 1 + TC_EPI_WARPS);      // the MMAs' commit and every epilogue warp
         }
@@ -403,15 +437,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                         break;
                     TC_TRACE(6, sc, 0);
                     const uint32_t base = sbase + s * TC_STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[s], TC_TMA_BYTES);
-                    tma_load_3d(base + TC_OFF_B, &map_act, 0, p0, 4 * st * TC_KB, &full[s]);
+                    // weight nibbles first (the unpack warps wait for these alone): stored pair
+                    // st ^ k of the rows with key pair k, or pair st past the complete 8-block groups
+                    const int g0 = (e * a.rows_per_expert + row0) >> 3;
+                    const bool swz = 2 * st < (nblk & ~7);
+                    mbar_arrive_expect_tx(&wfull[s], TC_NIB_BYTES);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        tma_load_5d(base + TC_OFF_NIB + k * (TC_NIB_BYTES / 4), &map_nib, 0, swz ? (st ^ k) : st, 0, k, g0,
+                                    &wfull[s]);
+                    mbar_arrive_expect_tx(&full[s], TC_FULL_BYTES);
+                    tma_load_2d(base + TC_OFF_B, &map_act, st * TC_KB * 64, p0, &full[s]);
                     tma_load_2d(base + TC_OFF_DX, &map_dx, p0, st * TC_KB, &full[s]);
+                    const float *dws = a.dwp + ((size_t)((e * a.rows_per_expert + row0) / TC_M) * nblk + st * TC_KB) * TC_M;
+                    bulk_load(base + TC_OFF_DW, dws, TC_KB * TC_M * 4, &full[s]);
                 }
             }
             // copies still in flight after an abort: wait (bounded) for the last stages issued
             if (!ok)
-                for (int k = sc - 1; k >= 0 && k >= sc - TC_STAGES; --k)
+                for (int k = sc - 1; k >= 0 && k >= sc - TC_STAGES; --k) {
+                    fd_mbar_wait(&wfull[k % TC_STAGES], (uint32_t)((k / TC_STAGES) & 1), nullptr);
                     fd_mbar_wait(&full[k % TC_STAGES], (uint32_t)((k / TC_STAGES) & 1), nullptr);
+                }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issue (whole warp)
@@ -439,10 +486,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                         break;
                     tc_fence_after();
                     // block j: K chunks 0, 1 then 2, 3 of the weight (A) and activation (B) operands
-                    const uint32_t ab = base + TC_OFF_A + j * TC_BLK_BYTES, bb = base + TC_OFF_B + j * TC_BLK_BYTES;
+                    const uint32_t ab = base + TC_OFF_A + j * TC_BLK_BYTES, bb = base + TC_OFF_B + j * 64;
                     const uint32_t d = tmem + (uint32_t)(tb * TC_N);
-                    mma_f16_elect<false>(d, umma_desc(ab, 2048, 128), umma_desc(bb, 2048, 128), idesc);
-                    mma_f16_elect<true>(d, umma_desc(ab + 4096, 2048, 128), umma_desc(bb + 4096, 2048, 128), idesc);
+                    mma_f16_elect<false>(d, umma_desc(ab, 2048, 128), umma_desc_sw128(bb), idesc);
+                    mma_f16_elect<true>(d, umma_desc(ab + 4096, 2048, 128), umma_desc_sw128(bb + 32), idesc);
                     mma_commit_elect(&tfull[tb]);
                     if (lane == 0) TC_TRACE(5, bc, 1);
 #ifdef RVC_TC_TRACE_MMA_DONE
@@ -462,75 +509,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
         fd_mbar_wait(&drain, 0, a.status);
     } else if (warp < 4) {
         // ---------------------------------------------------------- weight unpack (rows r, r + 64)
-        // Each row's nibbles (from global, one stage ahead) become f16 n - 8 in the MMA's A layout,
-        // and its f16 scales f32 values in the stage's scale table.
+        // Each row's nibbles (copied into the stage by TMA) become f16 n - 8 in the MMA's A layout.
         const int r0 = tid - 64;
         int sc = 0;
         bool ok = true;
         for (int L = blockIdx.x; L < total && ok; L += gridDim.x) {
             int e, nt, p0, row0;
             if (!tc_tile(a, L, e, nt, p0, row0)) continue;
-            const size_t grow0 = (size_t)e * a.rows_per_expert + row0;  // a multiple of 8: swizzle key = r & 7
-            uint4 wn[2][TC_KB];
-            uint32_t dn[2][TC_KB / 2];
-            auto ld_stage = [&](int st) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = r0 + 64 * h;
-                    const uint4 *nrow = reinterpret_cast<const uint4 *>(a.nib + (grow0 + r) * nblk * 16);
-                    const uint32_t *srow = reinterpret_cast<const uint32_t *>(a.scl + (grow0 + r) * nblk);
-#pragma unroll
-                    for (int j = 0; j < TC_KB; ++j) {
-                        const int b = st * TC_KB + j;
-                        wn[h][j] = b < nblk ? __ldg(nrow + nib_pos(b, nblk, r & 7)) : make_uint4(0u, 0u, 0u, 0u);
-                    }
-                    // TC_KB f16 scales = TC_KB / 2 32-bit words (a row of the plane is 4-byte aligned;
-                    // words past the row's last block are not read)
-#pragma unroll
-                    for (int k = 0; k < TC_KB / 2; ++k)
-                        dn[h][k] = st * TC_KB + 2 * k < nblk ? __ldg(srow + (TC_KB / 2) * st + k) : 0u;
-                }
-            };
-            ld_stage(0);
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
-                uint4 wc[2][TC_KB];
-                uint32_t dc[2][TC_KB / 2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                    for (int j = 0; j < TC_KB; ++j) wc[h][j] = wn[h][j];
-#pragma unroll
-                    for (int k = 0; k < TC_KB / 2; ++k) dc[h][k] = dn[h][k];
-                }
-                if (st + 1 < nst) ld_stage(st + 1);  // lands during this stage
-                // the stage's buffers are free once its copies have been issued again (full[s])
-                if (!(ok = tc_wait_warp(&full[s], (uint32_t)((sc / TC_STAGES) & 1), abort, a.status, true))) break;
+                if (!(ok = tc_wait_warp(&wfull[s], (uint32_t)((sc / TC_STAGES) & 1), abort, a.status, true))) break;
                 if (tid == 64) TC_TRACE(6, sc, 1);
                 uint8_t *base = smem + s * TC_STAGE_BYTES;
-                const int kn = min(TC_KB, nblk - st * TC_KB);
+                const uint32_t flip = 2 * st < (nblk & ~7) ? 1u : 0u;  // blocks of a swizzled pair in order i ^ j
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int r = r0 + 64 * h;
-                    float *dws = reinterpret_cast<float *>(base + TC_OFF_DW) + r;
+                    const int g = r >> 3, k = (r >> 1) & 3, jr = r & 1;
+                    const uint8_t *nrow = base + TC_OFF_NIB + k * (TC_NIB_BYTES / 4) + g * 64 + jr * 32;
 #pragma unroll
                     for (int j = 0; j < TC_KB; ++j) {
-                        if (j < kn) {
-                            // chunk 0: low nibbles of bytes 0..7 (elements 0..7), 1: of bytes 8..15,
-                            // 2: high nibbles of bytes 0..7 (elements 16..23), 3: of bytes 8..15
-                            const uint4 w = wc[h][j];
-                            uint4 *ablk = reinterpret_cast<uint4 *>(base + TC_OFF_A + j * TC_BLK_BYTES) + r;
-                            const uint2 c0a = nib_f16x4(w.x & 0x0F0F0F0Fu), c0b = nib_f16x4(w.y & 0x0F0F0F0Fu);
-                            const uint2 c1a = nib_f16x4(w.z & 0x0F0F0F0Fu), c1b = nib_f16x4(w.w & 0x0F0F0F0Fu);
-                            const uint2 c2a = nib_f16x4((w.x >> 4) & 0x0F0F0F0Fu), c2b = nib_f16x4((w.y >> 4) & 0x0F0F0F0Fu);
-                            const uint2 c3a = nib_f16x4((w.z >> 4) & 0x0F0F0F0Fu), c3b = nib_f16x4((w.w >> 4) & 0x0F0F0F0Fu);
-                            ablk[0 * TC_M] = make_uint4(c0a.x, c0a.y, c0b.x, c0b.y);
-                            ablk[1 * TC_M] = make_uint4(c1a.x, c1a.y, c1b.x, c1b.y);
-                            ablk[2 * TC_M] = make_uint4(c2a.x, c2a.y, c2b.x, c2b.y);
-                            ablk[3 * TC_M] = make_uint4(c3a.x, c3a.y, c3b.x, c3b.y);
-                            const uint32_t hw = dc[h][j >> 1];
-                            dws[j * TC_M] = f16_bits_to_f32((uint16_t)((j & 1) ? (hw >> 16) : (hw & 0xFFFFu)));
-                        }
+                        // chunk 0: low nibbles of bytes 0..7 (elements 0..7), 1: of bytes 8..15,
+                        // 2: high nibbles of bytes 0..7 (elements 16..23), 3: of bytes 8..15
+                        const uint4 w = *reinterpret_cast<const uint4 *>(nrow + ((uint32_t)j ^ (flip & (uint32_t)jr)) * 16);
+                        uint4 *ablk = reinterpret_cast<uint4 *>(base + TC_OFF_A + j * TC_BLK_BYTES) + r;
+                        const uint2 c0a = nib_f16x4(w.x & 0x0F0F0F0Fu), c0b = nib_f16x4(w.y & 0x0F0F0F0Fu);
+                        const uint2 c1a = nib_f16x4(w.z & 0x0F0F0F0Fu), c1b = nib_f16x4(w.w & 0x0F0F0F0Fu);
+                        const uint2 c2a = nib_f16x4((w.x >> 4) & 0x0F0F0F0Fu), c2b = nib_f16x4((w.y >> 4) & 0x0F0F0F0Fu);
+                        const uint2 c3a = nib_f16x4((w.z >> 4) & 0x0F0F0F0Fu), c3b = nib_f16x4((w.w >> 4) & 0x0F0F0F0Fu);
+                        ablk[0 * TC_M] = make_uint4(c0a.x, c0a.y, c0b.x, c0b.y);
+                        ablk[1 * TC_M] = make_uint4(c1a.x, c1a.y, c1b.x, c1b.y);
+                        ablk[2 * TC_M] = make_uint4(c2a.x, c2a.y, c2b.x, c2b.y);
+                        ablk[3 * TC_M] = make_uint4(c3a.x, c3a.y, c3b.x, c3b.y);
                     }
                 }
                 fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads

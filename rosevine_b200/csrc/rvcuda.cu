@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "decode_fused.cuh"
+#include "norm.cuh"
 #include "pack.cuh"
 #include "prefill.cuh"
 #include "prefill_tc.cuh"
@@ -41,15 +42,21 @@ bool dims_ok(const rvc_moe_weights *w) {
 }
 
 // Byte offsets of the packed planes inside the packed buffer.
+// The f32 tile-major scale planes exist for shapes the prefill GEMM takes (rows per expert
+// multiples of DW_TILE: 2 ff and n_embd), and are empty otherwise.
 struct PackedLayout {
-    size_t gu_nib, gu_scl, dn_nib, dn_scl, total;
+    size_t gu_nib, gu_scl, dn_nib, dn_scl, gu_dw, dn_dw, total;
+    bool has_dw;
     PackedLayout(int ne, int n_embd, int ff) {
         const size_t nb = n_embd / QK, nbh = ff / QK;
+        has_dw = (2 * ff) % DW_TILE == 0 && n_embd % DW_TILE == 0;
         size_t o = 0;
         gu_nib = o, o = align256(o + (size_t)ne * 2 * ff * nb * 16);
         gu_scl = o, o = align256(o + (size_t)ne * 2 * ff * nb * 2);
         dn_nib = o, o = align256(o + (size_t)ne * n_embd * nbh * 16);
         dn_scl = o, o = align256(o + (size_t)ne * n_embd * nbh * 2);
+        gu_dw = o, o = align256(o + (has_dw ? (size_t)ne * 2 * ff * nb * 4 : 0));
+        dn_dw = o, o = align256(o + (has_dw ? (size_t)ne * n_embd * nbh * 4 : 0));
         total = o;
     }
 };
@@ -58,7 +65,8 @@ PackedView packed_view(const rvc_moe_weights *w) {
     PackedLayout L(w->n_experts, w->n_embd, w->ff);
     const uint8_t *b = static_cast<const uint8_t *>(w->packed);
     return PackedView{b + L.gu_nib, reinterpret_cast<const uint16_t *>(b + L.gu_scl), b + L.dn_nib,
-                      reinterpret_cast<const uint16_t *>(b + L.dn_scl)};
+                      reinterpret_cast<const uint16_t *>(b + L.dn_scl), reinterpret_cast<const float *>(b + L.gu_dw),
+                      reinterpret_cast<const float *>(b + L.dn_dw)};
 }
 
 // Batches above PF_MIN_TOK tokens take the prefill kernels (grouped GEMMs), smaller ones the
@@ -439,43 +447,48 @@ int tensor_map_encode() {
 // A 2-D tensor map of bytes or f32 (d0 innermost, in elements; stride of dim 1 in bytes), box
 // b0 x b1 elements, no swizzle, out-of-range elements read as zero.
 int map2d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t s1, uint32_t b0, uint32_t b1,
-          CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
+          CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8,
+          CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE) {
     const cuuint64_t dims[2] = {d0, d1};
     const cuuint64_t strides[1] = {s1};
     const cuuint32_t box[2] = {b0, b1};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = g_encode(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+// The packed nibble plane [E * rows][nblk][16 B] viewed as [g][k][j][pair][32 B] (row = 8 g + 2 k
+// + j, blocks 2 pair and 2 pair + 1): a packed reshape, so every stride is the product of the
+// extents inside it. Box: one pair of 16 groups' rows with key pair k (16 x 2 rows x 32 B).
+int map_nibbles(CUtensorMap *m, const uint8_t *nib, uint64_t n_rows, int nblk) {
+    const uint64_t row = (uint64_t)nblk * 16;
+    const cuuint64_t dims[5] = {32, (cuuint64_t)nblk / 2, 2, 4, n_rows / 8};
+    const cuuint64_t strides[4] = {32, row, 2 * row, 8 * row};
+    const cuuint32_t box[5] = {32, 1, 2, 1, 16};
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<uint8_t *>(nib), dims, strides, box, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-// A 3-D byte tensor map (dims d0 innermost; strides of dims 1 and 2 in bytes), box b0 x b1 x b2,
-// no swizzle, out-of-range elements read as zero.
-int map3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
-          uint32_t b0, uint32_t b1, uint32_t b2) {
-    const cuuint64_t dims[3] = {d0, d1, d2};
-    const cuuint64_t strides[2] = {s1, s2};
-    const cuuint32_t box[3] = {b0, b1, b2};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
-}
-
-// The grouped GEMM's tensor maps: activation operands as [16-byte K chunks][positions][16 B] (a
-// tile's positions contiguous per chunk: the MMA's K-major B layout; rec_bytes apart per
-// position); activation block scales [blocks][positions] f32.
+// The grouped GEMM's tensor maps: activation operands [positions][rec_bytes] in boxes of 128
+// positions x 128 B (two blocks of f16 quants) with the 128-byte swizzle (the MMA's K-major B
+// layout); activation block scales [blocks][positions] f32; the weight nibbles (map_nibbles).
 struct TcMaps {
-    CUtensorMap act, dx;
+    CUtensorMap act, dx, nib;
 };
 
-int tc_maps(TcMaps *m, const uint8_t *rec, int rec_bytes, int nblk, int ppos, const float *scales, int ppad) {
+int tc_maps(TcMaps *m, const uint8_t *rec, int rec_bytes, int nblk, int ppos, const float *scales, int ppad,
+            const uint8_t *nib, uint64_t n_rows) {
     int rc;
-    if ((rc = map3d(&m->act, rec, 16, ppos, 4 * (uint64_t)nblk, rec_bytes, 16, 16, TC_N, 4 * TC_KB)) ||
+    if ((rc = map2d(&m->act, rec, (uint64_t)rec_bytes, ppos, rec_bytes, TC_KB * 64, TC_N, CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                    CU_TENSOR_MAP_SWIZZLE_128B)) ||
         (rc = map2d(&m->dx, scales, (uint64_t)ppad, nblk, (uint64_t)ppad * 4, TC_N, TC_KB,
-                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
+        (rc = map_nibbles(&m->nib, nib, n_rows, nblk)))
         return rc;
     return 0;
 }
@@ -487,7 +500,7 @@ int launch_tc(const TcMaps &m, const TcArgs &g, int max_units, cudaStream_t st) 
     if ((rc = fd_smem_max(k_pf_gemm_tc<MODE>, &smax))) return rc;
     if (smax < (size_t)TC_SMEM_BYTES) return RVC_ERR_UNSUPPORTED;
     const int grid = std::max(1, std::min(num_sms(), max_units));  // persistent: one CTA per SM
-    k_pf_gemm_tc<MODE><<<grid, TC_THREADS, TC_SMEM_BYTES, st>>>(m.act, m.dx, g);
+    k_pf_gemm_tc<MODE><<<grid, TC_THREADS, TC_SMEM_BYTES, st>>>(m.act, m.dx, m.nib, g);
     return launched();
 }
 
@@ -501,26 +514,27 @@ int pf_gemms(const rvc_moe_weights *w, const Workspace &L, void *ws, int n_pairs
     float *xsc = at<float>(ws, L.xd), *hsc = at<float>(ws, L.hd);
     const int ppos = (int)L.ppos, ppad = (int)L.ppad;
     TcMaps mg, md;
-    if ((rc = tc_maps(&mg, xperm, pf_rec_bytes(nb), nb, ppos, xsc, ppad)) ||
-        (rc = tc_maps(&md, hrec, pf_rec_bytes(nbh), nbh, ppos, hsc, ppad)))
+    if ((rc = tc_maps(&mg, xperm, pf_rec_bytes(nb), nb, ppos, xsc, ppad, pk.gu_nib, (uint64_t)ne * 2 * w->ff)) ||
+        (rc = tc_maps(&md, hrec, pf_rec_bytes(nbh), nbh, ppos, hsc, ppad, pk.dn_nib, (uint64_t)ne * w->n_embd)))
         return rc;
     const int tiles_max = n_pairs / TC_N + 1 + ne;  // an upper bound on the (expert, position tile) count
     TcArgs g{};
     g.tiles = at<int2>(ws, L.tiles), g.n_tiles = at<int32_t>(ws, L.n_tiles), g.max_tiles = tiles_max;
     g.n_experts = ne, g.ppos = ppos, g.ppad = ppad, g.n_embd = w->n_embd, g.status = at<int>(ws, L.status);
-    g.rows_per_expert = 2 * w->ff, g.row_tiles = 2 * w->ff / TC_M, g.nblk = nb, g.nib = pk.gu_nib, g.scl = pk.gu_scl;
+    g.rows_per_expert = 2 * w->ff, g.row_tiles = 2 * w->ff / TC_M, g.nblk = nb, g.dwp = pk.gu_dw;
     g.nh = nbh, g.hrec = hrec, g.hsc = hsc;
     g.negzero2 = 0x8000000080000000ull;
     if ((rc = launch_tc<PF_GU>(mg, g, tiles_max * g.row_tiles, st))) return rc;
     TcArgs d = g;
-    d.rows_per_expert = w->n_embd, d.row_tiles = w->n_embd / TC_M, d.nblk = nbh, d.nib = pk.dn_nib, d.scl = pk.dn_scl;
+    d.rows_per_expert = w->n_embd, d.row_tiles = w->n_embd / TC_M, d.nblk = nbh, d.dwp = pk.dn_dw;
     d.hrec = nullptr, d.hsc = nullptr, d.y = at<float>(ws, L.ybuf);
     return launch_tc<PF_DN>(md, d, tiles_max * d.row_tiles, st);
 }
 
 int pf_supported(const rvc_moe_weights *w) {
-    const int nb = w->n_embd / QK;
-    if (nb % TC_KB || (2 * w->ff) % TC_M || w->n_embd % TC_M || w->n_experts > MAX_EXPERTS || w->used > MAX_USED)
+    const int nb = w->n_embd / QK, nbh = w->ff / QK;
+    if (nb % TC_KB || nbh % TC_KB || (2 * w->ff) % TC_M || w->n_embd % TC_M || w->n_experts > MAX_EXPERTS ||
+        w->used > MAX_USED)
         return RVC_ERR_UNSUPPORTED;
     return tensor_map_encode();
 }
@@ -755,6 +769,12 @@ int rvc_pack_experts(const void *gate_up_q4, const void *down_q4, int n_experts,
     if (rc) return rc;
     k_pack_q4<<<4 * 148, 256, 0, S(stream)>>>((const uint8_t *)down_q4, n_experts, n_embd, ff / QK, false, ff,
                                                b + L.dn_nib, reinterpret_cast<uint16_t *>(b + L.dn_scl));
+    if ((rc = launched()) || !L.has_dw) return rc;
+    k_pack_dw<<<4 * 148, 256, 0, S(stream)>>>(reinterpret_cast<const uint16_t *>(b + L.gu_scl),
+                                               (size_t)n_experts * 2 * ff, n_embd / QK, reinterpret_cast<float *>(b + L.gu_dw));
+    if ((rc = launched())) return rc;
+    k_pack_dw<<<4 * 148, 256, 0, S(stream)>>>(reinterpret_cast<const uint16_t *>(b + L.dn_scl),
+                                               (size_t)n_experts * n_embd, ff / QK, reinterpret_cast<float *>(b + L.dn_dw));
     return launched();
 }
 
@@ -921,6 +941,19 @@ int rvc_ep_reduce(const float *back, const int32_t *owner_map, int n_tok, int wo
     return launched();
 }
 
+int rvc_rms_norm(const float *x, float *out, const float *weight, int rows, int width, float eps, float post,
+                 void *stream) {
+    if (!x || !out || rows <= 0 || width <= 0 || !aligned(x, 4) || !aligned(out, 4) || (weight && !aligned(weight, 4)))
+        return (int)cudaErrorInvalidValue;
+    const bool vec = width % 4 == 0 && aligned(x, 16) && aligned(out, 16) && (!weight || aligned(weight, 16));
+    const int grid = (rows + NORM_WARPS - 1) / NORM_WARPS;
+    if (vec)
+        k_rms_norm<true><<<grid, NORM_WARPS * 32, 0, S(stream)>>>(x, out, weight, rows, width, eps, post);
+    else
+        k_rms_norm<false><<<grid, NORM_WARPS * 32, 0, S(stream)>>>(x, out, weight, rows, width, eps, post);
+    return launched();
+}
+
 int rvc_status(void *workspace, void *stream) {
     if (!workspace) return (int)cudaErrorInvalidValue;
     int rc = (int)cudaStreamSynchronize(S(stream));
@@ -957,14 +990,15 @@ int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, i
     const PackedView pk = packed_view(w);
     TcMaps m;
     if ((rc = tc_maps(&m, (const uint8_t *)records, pf_rec_bytes(nblk), nblk, n,
-                      reinterpret_cast<const float *>(static_cast<uint8_t *>(scratch) + 256), ppad)))
+                      reinterpret_cast<const float *>(static_cast<uint8_t *>(scratch) + 256), ppad,
+                      which == 0 ? pk.gu_nib : pk.dn_nib, (uint64_t)w->n_experts * rows)))
         return rc;
     TcArgs g{};
     g.tiles = static_cast<const int2 *>(scratch), g.n_tiles = static_cast<const int *>(scratch) + 2, g.max_tiles = 1;
     g.n_experts = w->n_experts, g.ppos = n, g.ppad = ppad, g.n_embd = w->n_embd;
     g.status = static_cast<int *>(scratch) + 3;
     g.rows_per_expert = rows, g.row_tiles = 1, g.row_base = row_tile * TC_M, g.nblk = nblk;
-    g.nib = which == 0 ? pk.gu_nib : pk.dn_nib, g.scl = which == 0 ? pk.gu_scl : pk.dn_scl;
+    g.dwp = which == 0 ? pk.gu_dw : pk.dn_dw;
     g.y = reinterpret_cast<float *>(out);
     return launch_tc<PF_RAW>(m, g, 1, st);
 }

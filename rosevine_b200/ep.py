@@ -181,15 +181,18 @@ class EpMoeLayer:
     """One rank of the expert-parallel layer. `backend` does the compute on this rank's device;
     `group` is the process group of the N ranks (rank r holds experts [r E/N, (r + 1) E/N)).
     With timing=True each forward records CUDA events between its phases (no synchronisation);
-    phase_times() reads them once the caller has synchronised."""
+    phase_times() reads them once the caller has synchronised. With `health` (an
+    ep_health.EpHealth) every forward first checks, on the host, that all peers reached the same
+    step, and raises ep_health.PeerLost instead of entering an exchange a lost peer would stall."""
 
     def __init__(self, backend, rank: int, world: int, n_experts: int = synth.N_EXPERTS, group=None,
-                 timing: bool = False):
+                 timing: bool = False, health=None):
         if n_experts % world:
             raise ValueError("experts must divide evenly over the ranks")
         self.be, self.rank, self.world, self.group = backend, rank, world, group
         self.n_local = n_experts // world
         self.timing = timing
+        self.health, self.step = health, 0
         self.marks = []
         self.stats = EpStats()
 
@@ -203,6 +206,9 @@ class EpMoeLayer:
         be = self.be
         dev = x.device
         marks = []
+        if self.health is not None:
+            self.health.begin_step(self.step)  # raises PeerLost before any collective of this step
+        self.step += 1
 
         def mark(name):  # device timestamps between the phases (CUDA, timing=True only)
             if self.timing and dev.type == "cuda":

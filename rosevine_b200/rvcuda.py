@@ -32,7 +32,7 @@ EXPORTS = [
     "rvc_packed_bytes", "rvc_pack_experts", "rvc_moe_workspace_bytes", "rvc_moe_router", "rvc_moe_experts",
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
     "rvc_debug_gemm_block_dots", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
-    "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms",
+    "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms", "rvc_rms_norm",
 ]
 
 
@@ -95,6 +95,7 @@ def lib() -> ctypes.CDLL:
             "rvc_moe_forward": ([W, P, P, I, P, I, I, P, P, P, P, Z, P], I),
             "rvc_workspace_reset": ([P, P], I),
             "rvc_status": ([P, P], I),
+            "rvc_rms_norm": ([P, P, P, I, I, F, F, P], I),
             "rvc_debug_block_sums": ([W, I, I, P, I, P, I, P, P], I),
             "rvc_moe_forward_noalloc": ([W, P, P, I, P, I, I, P, P, P, P], I),
             "rvc_debug_gemm_block_dots": ([W, I, I, I, P, I, P, P, Z, P], I),
@@ -329,6 +330,13 @@ def ep_row_bytes(n_embd: int, used: int) -> int:
 
 def ep_workspace_bytes(max_rows: int, used: int, n_embd: int, ff: int, n_experts: int) -> int:
     return lib().rvc_ep_workspace_bytes(max_rows, used, n_embd, ff, n_experts)
+
+
+def rms_norm(x, out, weight, rows: int, width: int, eps: float, post: float = 1.0,
+             stream: int | None = None) -> None:
+    """rvc_rms_norm: out [rows, width] f32 = RMS-normalised x (out may be x)."""
+    nb = rows * width * 4
+    check(lib().rvc_rms_norm(_ptr(x, nb), _ptr(out, nb), _ptr(weight, width * 4), rows, width, eps, post, stream))
 
 
 def quant_q8_rows(x, x_dtype: int, n_rows: int, n_embd: int, records, stream: int | None = None) -> None:

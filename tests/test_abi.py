@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_host_size_queries(lib):
-    assert rc.packed_bytes(128, 2816, 704) == 428212224
+    assert rc.packed_bytes(128, 2816, 704) == 523370496  # 428,212,224 GGUF bytes + f32 scale tiles
     assert rc.packed_bytes(128, 2816, 700) == 0
     assert rc.workspace_bytes(64, 2816, 704, 128, 8) > 0
     assert rc.workspace_bytes(0, 2816, 704, 128, 8) == 0
@@ -99,3 +99,15 @@ def test_checked_views_refuse_out_of_range():
     assert v.need(100) == 1 << 20
     with pytest.raises(ValueError):
         v.need(101)
+
+
+def test_integration_names_only_declared_symbols():
+    """Every library entry INTEGRATION.md's bindings call (rvc_* names and the cuda:: wrappers,
+    each a thin shim over rvc_<name>) is declared in include/rvcuda.h."""
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    declared = declared_symbols()
+    named = set(re.findall(r"\b(rvc_\w+)\b", text)) - {"rvc_moe_weights"}
+    wrapped = {"rvc_" + n for n in re.findall(r"\bcuda::(\w+)\s*\(", text)}
+    assert named, "no rvc_ names found"
+    assert named <= declared, named - declared
+    assert wrapped <= declared, wrapped - declared
