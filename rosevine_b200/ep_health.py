@@ -111,23 +111,35 @@ class EpHealth:
             if n_left:
                 left = [r for r in peers if self.store.check([self._left(r)])]
                 if left:
+                    # a peer that gave up on a stalled rank names it: every healthy rank then
+                    # reports the same cause, whichever of them ran out of time first
+                    stalled = sorted({s for r in left for s in self._stalled(r)} - {self.rank})
+                    if stalled and not any(self.rank in self._stalled(r) for r in left):
+                        self.leave(stalled)
+                        raise PeerLost(stalled, "timeout", step)
                     self.leave()
                     raise PeerLost(left, "left", step)
             if time.monotonic() > deadline:
                 missing = [r for r in peers if not self.store.check([self._key(step, r)])]
-                self.leave()
+                self.leave(missing)
                 raise PeerLost(missing, "timeout", step)
             time.sleep(self.poll_s)
 
     def _nleft(self) -> str:
         return f"{self.prefix}/n_left"
 
-    def leave(self) -> None:
+    def _stalled(self, r: int) -> list[int]:
+        """The ranks that peer r gave up waiting on when it left (empty: it left of its own accord)."""
+        v = self.store.get(self._left(r)).decode()
+        return [int(t) for t in v[2:].split(",")] if v.startswith("t:") else []
+
+    def leave(self, stalled=()) -> None:
         """Announce that this rank takes no further steps (between steps; begin_step does it
-        itself before raising PeerLost). Idempotent."""
+        itself before raising PeerLost, naming the ranks it timed out on). Idempotent."""
         try:
             if not self.store.check([self._left(self.rank)]):
-                self.store.set(self._left(self.rank), b"1")
+                mark = "t:" + ",".join(str(r) for r in stalled) if stalled else "x"
+                self.store.set(self._left(self.rank), mark.encode())
                 self.store.add(self._nleft(), 1)
         except Exception:  # noqa: BLE001 - nobody is left to tell
             pass

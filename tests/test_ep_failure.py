@@ -134,7 +134,9 @@ def test_stalled_rank_is_reported_after_the_timeout():
     for r in (recs[0], recs[2]):
         assert r["steps"] == 2 and r["error"] == "PeerLost" and r["why"] == "timeout", r
         assert r["ranks"] == [1], r
-        assert HEALTH_S <= r["t_detect"] < HEALTH_S + 5, r
+        # the first rank to run out of time tells the other, whose own wait started within
+        # the previous step's exchange of it
+        assert HEALTH_S - 0.5 <= r["t_detect"] < HEALTH_S + 5, r
     # the stalled rank comes back to peers that gave up: told (their leave notice, or the store
     # gone with rank 0), not left waiting in an all-to-all
     assert recs[1]["error"] == "PeerLost" and recs[1]["why"] in ("left", "unreachable"), recs[1]
