@@ -194,7 +194,7 @@ int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, cons
 
 /* Measurement hook (no counterpart in the reference): enqueue on `stream`, again, the two
  * grouped expert GEMMs (gate/up with GELU and h quantisation, then down) of the last
- * rvc_moe_forward call of more than 16 tokens enqueued with this workspace and these weights,
+ * rvc_moe_forward call of more than 48 tokens enqueued with this workspace and these weights,
  * on the plan, records and scale planes that call left in the workspace. The GEMMs rewrite the
  * same h records and y, so the layer's outputs stay as they were. Lets a caller time the
  * layer's dominant kernels alone with events on `stream`. Returns cudaErrorInvalidValue if no

@@ -70,9 +70,9 @@ PackedView packed_view(const rvc_moe_weights *w) {
 }
 
 // Batches above PF_MIN_TOK tokens take the prefill kernels (grouped GEMMs), smaller ones the
-// decode kernels (measured on B200: at 24 tokens the grouped GEMMs run the layer in 376 us, the
-// decode kernels in 552 us; at 16 tokens 357 against 316 us).
-constexpr int PF_MIN_TOK = 16;
+// decode kernels (measured on B200, L2 flushed before each call, layer us decode / prefill
+// kernels: 24 tokens 434 / 744, 32 tokens 596 / 853, 48 tokens 821 / 927, 64 tokens 967 / 934).
+constexpr int PF_MIN_TOK = 48;
 
 // Workspace carve-up for calls of up to max_tok tokens.
 struct Workspace {
