@@ -39,6 +39,7 @@ extern "C" {
 #define RVC_ERR_DEVICE_INDEX 10002   /* a device-side index check failed (status word) */
 #define RVC_ERR_UNSUPPORTED 10003    /* shape outside what the kernels support */
 #define RVC_ERR_WORKSPACE 10004      /* workspace too small for this call */
+#define RVC_ERR_GGUF 10100           /* + a reason: malformed or unusable GGUF file (rvc_error_string) */
 
 /* ---------------------------------------------------------------- runtime
  * 1:1 with runtime/hip/rvhip.h:22-38 (rvh_init ... rvh_event_elapsed). */
@@ -222,6 +223,39 @@ int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const 
  * 256 + nblk * 4 * round_up(n, 4) bytes; its int at byte 12 receives the kernel's status bits. */
 int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, int row_tile, const void *records,
                               int n, int32_t *out, void *scratch, size_t scratch_bytes, void *stream);
+
+/* ---------------------------------------------------------------- GGUF weights (host only)
+ * The reference reads the model with its own GGUF parser (runtime/src/gguf.rs, Gguf::parse) and
+ * binds tensors by name (runtime/src/model.rs:61-107, Weights::bind). These calls do the same for
+ * the MoE layer: the file is mapped read-only, validated with the reference parser's checks
+ * (a file it rejects is rejected here, the reason as its message: rvc_error_string of the
+ * RVC_ERR_GGUF + reason code), and tensors are views into the mapping, valid until
+ * rvc_gguf_close. Tensor types: F32 and Q4_0, as the reference accepts. */
+typedef struct rvc_gguf rvc_gguf;
+
+/* Map and validate a GGUF v3 file (gguf.rs:272-383 replaces). */
+int rvc_gguf_open(const char *path, rvc_gguf **out);
+/* The same over a caller's buffer (not copied: it must outlive the handle). */
+int rvc_gguf_parse(const void *buf, size_t len, rvc_gguf **out);
+void rvc_gguf_close(rvc_gguf *g);
+/* A tensor by name (gguf.rs, Gguf::tensor): ggml type (0 F32, 2 Q4_0), rank, shape[4] (ggml
+ * order: shape[0] is the innermost dimension; unused dimensions 1), its bytes in the mapping. */
+int rvc_gguf_tensor(const rvc_gguf *g, const char *name, int *dtype, int *n_dims, uint64_t *shape, const void **data,
+                    uint64_t *bytes);
+
+/* Host views of one layer's MoE tensors, each checked against the target contract's shape and
+ * type (runtime/src/contract.rs:42-51, 66-70): gate_up and down are rvc_pack_experts' inputs. */
+typedef struct {
+    const void *gate_up;          /* Q4_0 ggml [n_embd, 2 ff, n_experts]: blk.L.ffn_gate_up_exps.weight */
+    const void *down;             /* Q4_0 ggml [ff, n_embd, n_experts]: blk.L.ffn_down_exps.weight */
+    const float *router;          /* F32 [n_experts][n_embd]: blk.L.ffn_gate_inp.weight */
+    const float *down_scale;      /* [n_experts]: blk.L.ffn_down_exps.scale */
+    const float *gate_inp_scale;  /* [n_embd]: blk.L.ffn_gate_inp.scale (router input norm) */
+    const float *pre_norm;        /* [n_embd]: blk.L.pre_ffw_norm_2.weight (expert input norm) */
+    const float *post_norm;       /* [n_embd]: blk.L.post_ffw_norm_2.weight (output norm) */
+} rvc_gguf_moe;
+/* model.rs:61-107 (Weights::bind) for one layer's MoE branch. */
+int rvc_gguf_moe_layer(const rvc_gguf *g, int layer, int n_embd, int ff, int n_experts, rvc_gguf_moe *out);
 
 #ifdef __cplusplus
 }

@@ -12,8 +12,14 @@
 #include <cstdio>
 #include <mutex>
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include "common.cuh"
 #include "decode_fused.cuh"
+#include "gguf.h"
 #include "norm.cuh"
 #include "pack.cuh"
 #include "prefill.cuh"
@@ -706,7 +712,10 @@ const char *rvc_error_string(int code) {
         case RVC_ERR_DEVICE_INDEX: return "rvcuda: a device-side index check failed";
         case RVC_ERR_UNSUPPORTED: return "rvcuda: shape not supported by the kernels";
         case RVC_ERR_WORKSPACE: return "rvcuda: workspace too small for this call";
-        default: return cudaGetErrorString((cudaError_t)code);
+        default:
+            if (code >= RVC_ERR_GGUF && code < RVC_ERR_GGUF + rvc::gguf::kReasons)
+                return rvc::gguf::reason(code - RVC_ERR_GGUF);
+            return cudaGetErrorString((cudaError_t)code);
     }
 }
 
@@ -1011,6 +1020,108 @@ int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const 
     k_debug_block_sums<<<592, 256, 0, S(stream)>>>(packed_view(w), which, expert, w->n_embd, w->ff, rows, n_rows,
                                                    (const uint8_t *)xq8, n_in, out);
     return launched();
+}
+
+// ------------------------------------------------------------------ GGUF weights (host only)
+struct rvc_gguf {
+    rvc::gguf::File f;
+};
+
+int rvc_gguf_parse(const void *buf, size_t len, rvc_gguf **out) {
+    if (!out || (!buf && len)) return (int)cudaErrorInvalidValue;
+    *out = nullptr;
+    rvc_gguf *g = new (std::nothrow) rvc_gguf();
+    if (!g) return (int)cudaErrorMemoryAllocation;
+    const int r = rvc::gguf::parse(static_cast<const uint8_t *>(buf), len, &g->f);
+    if (r) {
+        delete g;
+        return RVC_ERR_GGUF + r;
+    }
+    *out = g;
+    return 0;
+}
+
+int rvc_gguf_open(const char *path, rvc_gguf **out) {
+    if (!path || !out) return (int)cudaErrorInvalidValue;
+    *out = nullptr;
+    const int fd = open(path, O_RDONLY | O_CLOEXEC);
+    if (fd < 0) return RVC_ERR_GGUF + rvc::gguf::kIo;
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+        close(fd);
+        return RVC_ERR_GGUF + (st.st_size == 0 ? rvc::gguf::kTruncated : rvc::gguf::kIo);
+    }
+    const size_t len = (size_t)st.st_size;
+    void *m = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (m == MAP_FAILED) return RVC_ERR_GGUF + rvc::gguf::kIo;
+    rvc_gguf *g = nullptr;
+    const int r = rvc_gguf_parse(m, len, &g);
+    if (r) {
+        munmap(m, len);
+        return r;
+    }
+    g->f.map = m, g->f.map_len = len;
+    *out = g;
+    return 0;
+}
+
+void rvc_gguf_close(rvc_gguf *g) {
+    if (!g) return;
+    if (g->f.map) munmap(g->f.map, g->f.map_len);
+    delete g;
+}
+
+int rvc_gguf_tensor(const rvc_gguf *g, const char *name, int *dtype, int *n_dims, uint64_t *shape, const void **data,
+                    uint64_t *bytes) {
+    if (!g || !name) return (int)cudaErrorInvalidValue;
+    const rvc::gguf::Tensor *t = g->f.find(name);
+    if (!t) return RVC_ERR_GGUF + rvc::gguf::kMissing;
+    if (dtype) *dtype = t->dtype;
+    if (n_dims) *n_dims = t->n_dims;
+    if (shape)
+        for (int d = 0; d < 4; ++d) shape[d] = t->shape[d];
+    if (data) *data = t->data;
+    if (bytes) *bytes = t->bytes;
+    return 0;
+}
+
+int rvc_gguf_moe_layer(const rvc_gguf *g, int layer, int n_embd, int ff, int n_experts, rvc_gguf_moe *out) {
+    using namespace rvc::gguf;
+    if (!g || !out || layer < 0 || n_embd <= 0 || ff <= 0 || n_experts <= 0) return (int)cudaErrorInvalidValue;
+    const uint64_t E = (uint64_t)n_embd, F = (uint64_t)ff, N = (uint64_t)n_experts;
+    struct Want {
+        const char *suffix;
+        int dtype, n_dims;
+        uint64_t s[3];
+        const void **dst;
+    };
+    const void *gu, *dn, *router, *dscale, *giscale, *pre, *post;
+    const Want want[] = {
+        {"ffn_gate_up_exps.weight", kQ4_0, 3, {E, 2 * F, N}, &gu},  // contract.rs:69
+        {"ffn_down_exps.weight", kQ4_0, 3, {F, E, N}, &dn},         // contract.rs:70
+        {"ffn_gate_inp.weight", kF32, 2, {E, N, 0}, &router},       // contract.rs:66
+        {"ffn_down_exps.scale", kF32, 1, {N, 0, 0}, &dscale},       // contract.rs:68
+        {"ffn_gate_inp.scale", kF32, 1, {E, 0, 0}, &giscale},       // contract.rs:67
+        {"pre_ffw_norm_2.weight", kF32, 1, {E, 0, 0}, &pre},        // contract.rs:42-51
+        {"post_ffw_norm_2.weight", kF32, 1, {E, 0, 0}, &post},
+    };
+    for (const Want &w : want) {
+        const std::string name = "blk." + std::to_string(layer) + "." + w.suffix;
+        const Tensor *t = g->f.find(name.c_str());
+        if (!t) return RVC_ERR_GGUF + kMissing;
+        bool ok = t->dtype == w.dtype && t->n_dims == w.n_dims;
+        for (int d = 0; ok && d < w.n_dims; ++d) ok = t->shape[d] == w.s[d];
+        if (!ok) return RVC_ERR_GGUF + kContract;
+        *w.dst = t->data;
+    }
+    out->gate_up = gu, out->down = dn;
+    out->router = static_cast<const float *>(router);
+    out->down_scale = static_cast<const float *>(dscale);
+    out->gate_inp_scale = static_cast<const float *>(giscale);
+    out->pre_norm = static_cast<const float *>(pre);
+    out->post_norm = static_cast<const float *>(post);
+    return 0;
 }
 
 }  // extern "C"

@@ -59,6 +59,19 @@ class MoeLayer:
         self.w = rc.weights_struct(n_embd, ff, self.n_experts, used, self.router_dtype, self.router_w, self.packed,
                                    self.down_scale)
 
+    @classmethod
+    def from_gguf(cls, path: str, layer: int, max_tok: int = 64, device: int = 0, n_embd: int = synth.N_EMBD,
+                  ff: int = synth.FF, n_experts: int = synth.N_EXPERTS, used: int = synth.USED) -> "MoeLayer":
+        """The MoE layer of block `layer` of a GGUF model file (runtime/src/model.rs:61-107 binds the
+        same tensors): F32 router, Q4_0 experts packed on the device, the experts' down scales. The
+        branch's norm weights are kept as `norms` (gate_inp_scale, pre_norm, post_norm: host f32)."""
+        with rc.GgufFile(path) as g:
+            t = g.moe_layer(layer, n_embd, ff, n_experts)
+            lyr = cls(t["router"], t["gate_up"], t["down"], down_scale=t["down_scale"], max_tok=max_tok,
+                      device=device, n_embd=n_embd, ff=ff, used=used)
+            lyr.norms = {k: np.array(t[k]) for k in ("gate_inp_scale", "pre_norm", "post_norm")}
+        return lyr
+
     @staticmethod
     def x_dtype(x: torch.Tensor) -> int:
         if x.dtype == torch.bfloat16:

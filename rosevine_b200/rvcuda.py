@@ -33,7 +33,9 @@ EXPORTS = [
     "rvc_moe_forward", "rvc_workspace_reset", "rvc_status", "rvc_debug_block_sums", "rvc_moe_forward_noalloc",
     "rvc_debug_gemm_block_dots", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
     "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms", "rvc_rms_norm",
+    "rvc_gguf_open", "rvc_gguf_parse", "rvc_gguf_close", "rvc_gguf_tensor", "rvc_gguf_moe_layer",
 ]
+ERR_GGUF = 10100  # + a reason (rvc_error_string gives the reference parser's wording)
 
 
 class DeviceError(RuntimeError):
@@ -54,6 +56,12 @@ class MoeWeights(ctypes.Structure):
         ("packed", ctypes.c_void_p),
         ("down_scale", ctypes.c_void_p),
     ]
+
+
+class GgufMoe(ctypes.Structure):
+    """rvc_gguf_moe (include/rvcuda.h): host views of one layer's MoE tensors."""
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("gate_up", "down", "router", "down_scale", "gate_inp_scale", "pre_norm", "post_norm")]
 
 
 _lib = None
@@ -107,6 +115,12 @@ def lib() -> ctypes.CDLL:
             "rvc_ep_experts": ([W, P, I, I, P, P, Z, P], I),
             "rvc_ep_reduce": ([P, P, I, I, I, P, P], I),
             "rvc_prefill_gemms": ([W, P, Z, P], I),
+            "rvc_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(P)], I),
+            "rvc_gguf_parse": ([P, Z, ctypes.POINTER(P)], I),
+            "rvc_gguf_close": ([P], None),
+            "rvc_gguf_tensor": ([P, ctypes.c_char_p, ctypes.POINTER(I), ctypes.POINTER(I),
+                                 ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(P), ctypes.POINTER(ctypes.c_uint64)], I),
+            "rvc_gguf_moe_layer": ([P, I, I, I, I, ctypes.POINTER(GgufMoe)], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -363,3 +377,67 @@ def ep_reduce(back, n_back: int, owner_map, n_tok: int, world: int, n_embd: int,
               stream: int | None = None) -> None:
     check(lib().rvc_ep_reduce(_ptr(back, n_back * n_embd * 4), _ptr(owner_map, n_tok * world * 4), n_tok, world,
                               n_embd, _ptr(out, n_tok * n_embd * 4), stream))
+
+
+class GgufFile:
+    """A GGUF v3 file mapped and validated by the library (rvc_gguf_open / rvc_gguf_parse): the
+    checks of the reference's parser (runtime/src/gguf.rs, Gguf::parse). Tensors are numpy views
+    into the mapping, valid until close()."""
+
+    def __init__(self, path: str | None = None, data: bytes | None = None):
+        h = ctypes.c_void_p()
+        if path is not None:
+            check(lib().rvc_gguf_open(os.fsencode(path), ctypes.byref(h)))
+            self._buf = None
+        else:
+            self._buf = ctypes.create_string_buffer(bytes(data), len(data)) if data else None
+            check(lib().rvc_gguf_parse(self._buf, len(data) if data else 0, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            lib().rvc_gguf_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    def tensor(self, name: str):
+        """(ggml type, shape in ggml order, uint8 view of the tensor's bytes)."""
+        dt, nd = ctypes.c_int(), ctypes.c_int()
+        shape = (ctypes.c_uint64 * 4)()
+        data, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        check(lib().rvc_gguf_tensor(self._h, name.encode(), ctypes.byref(dt), ctypes.byref(nd), shape,
+                                    ctypes.byref(data), ctypes.byref(nbytes)))
+        return dt.value, tuple(shape[:nd.value]), _host_view(data.value, nbytes.value)
+
+    def moe_layer(self, layer: int, n_embd: int, ff: int, n_experts: int) -> dict:
+        """Views of one layer's MoE tensors, shapes and types checked (rvc_gguf_moe_layer)."""
+        m = GgufMoe()
+        check(lib().rvc_gguf_moe_layer(self._h, layer, n_embd, ff, n_experts, ctypes.byref(m)))
+        nb, nh = n_embd // 32, ff // 32
+        f32 = lambda p, n: _host_view(p, 4 * n).view(np.float32)  # noqa: E731
+        return {
+            "gate_up": _host_view(m.gate_up, n_experts * 2 * ff * nb * 18).reshape(n_experts, 2 * ff, nb * 18),
+            "down": _host_view(m.down, n_experts * n_embd * nh * 18).reshape(n_experts, n_embd, nh * 18),
+            "router": f32(m.router, n_experts * n_embd).reshape(n_experts, n_embd),
+            "down_scale": f32(m.down_scale, n_experts),
+            "gate_inp_scale": f32(m.gate_inp_scale, n_embd),
+            "pre_norm": f32(m.pre_norm, n_embd),
+            "post_norm": f32(m.post_norm, n_embd),
+        }
+
+
+def _host_view(ptr: int, nbytes: int) -> np.ndarray:
+    if nbytes == 0:
+        return np.zeros(0, np.uint8)
+    return np.ctypeslib.as_array((ctypes.c_uint8 * nbytes).from_address(ptr))
