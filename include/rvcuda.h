@@ -224,6 +224,28 @@ int rvc_debug_block_sums(const rvc_moe_weights *w, int which, int expert, const 
 int rvc_debug_gemm_block_dots(const rvc_moe_weights *w, int which, int expert, int row_tile, const void *records,
                               int n, int32_t *out, void *scratch, size_t scratch_bytes, void *stream);
 
+/* ---------------------------------------------------------------- shared dense MLP
+ * The layer's dense gated MLP beside the experts (runtime/src/exec.rs:438-453 on the CPU,
+ * runtime/src/hip_exec.rs:770-778 on the device), Q4_0 weights in the GGUF layout as bound by
+ * runtime/src/model.rs:30-32 (ffn_gate / ffn_up [ff rows][n_embd/32 blocks of 18 B], ffn_down
+ * [n_embd rows][ff/32 blocks]) and F32 activations. Every dot is the CPU reference's sequential
+ * f32 sum of rounded products (ops.rs:249-266), so results equal the CPU reference's bit for bit
+ * and do not depend on the batch. */
+
+/* y[t][r] = W[r] . x[t]; W Q4_0 n_out x k (k a multiple of 32), x n_in x k (16-byte aligned).
+ * rvhip.h:45 (rvh_q4_mm) with a stream. */
+int rvc_q4_mm(const void *w, const float *x, float *y, int n_out, int k, int n_in, void *stream);
+/* out[i] = gelu(g[i]) * u[i] (rvhip.h:65, rvh_geglu). */
+int rvc_geglu(const float *g, const float *u, float *out, int n, void *stream);
+/* Workspace of rvc_shared_mlp calls of up to max_tok tokens. */
+size_t rvc_shared_mlp_workspace_bytes(int max_tok, int n_embd, int ff);
+/* out = rms_norm(Wd . (gelu(Wg . c) * (Wu . c))) * post_norm with c = rms_norm(x) * ffn_norm
+ * (exec.rs:438-453): x, out [n_tok][n_embd] f32 (out 16-byte aligned); gate and up fused in
+ * one kernel with the GELU product. Four launches on `stream`. */
+int rvc_shared_mlp(const void *w_gate, const void *w_up, const void *w_down, const float *ffn_norm,
+                   const float *post_norm, const float *x, float *out, int n_tok, int n_embd, int ff, float eps,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------- GGUF weights (host only)
  * The reference reads the model with its own GGUF parser (runtime/src/gguf.rs, Gguf::parse) and
  * binds tensors by name (runtime/src/model.rs:61-107, Weights::bind). These calls do the same for

@@ -44,6 +44,8 @@ def lib() -> ctypes.CDLL:
         L.rvo_gelu.argtypes, L.rvo_gelu.restype = [F], F
         L.rvo_softmax.argtypes, L.rvo_softmax.restype = [P, I], None
         L.rvo_rms_norm.argtypes, L.rvo_rms_norm.restype = [P, P, P, I, I, F, F], None
+        L.rvo_matmul_q4_0.argtypes, L.rvo_matmul_q4_0.restype = [P, I, P, I, P, I], None
+        L.rvo_shared_mlp.argtypes, L.rvo_shared_mlp.restype = [P, P, P, P, P, P, I, I, I, F, P], None
         L.rvo_top_k.argtypes, L.rvo_top_k.restype = [P, I, I, P], None
         L.rvo_router_logits.argtypes = [P, I, P, I, P, I, I, I, I, P]
         L.rvo_router_logits.restype = None
@@ -104,6 +106,28 @@ def rms_norm(x: np.ndarray, weight: np.ndarray | None = None, eps: float = 1e-6,
     out = np.empty_like(x)
     w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
     lib().rvo_rms_norm(_p(x), _p(out), _p(w), rows, width, eps, post)
+    return out
+
+
+def matmul_q4_0(w: np.ndarray, x: np.ndarray, n_out: int) -> np.ndarray:
+    """rvo_matmul_q4_0: y [n_in, n_out] = dequant(W) . x for Q4_0 rows w (bytes) and x [n_in, k] f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w).view(np.uint8)
+    n_in, k = x.shape
+    assert w.size == n_out * (k // 32) * 18
+    y = np.empty((n_in, n_out), np.float32)
+    lib().rvo_matmul_q4_0(_p(w), k, _p(x), n_in, _p(y), n_out)
+    return y
+
+
+def shared_mlp(gate, up, down, ffn_norm, post_norm, x, ff: int, eps: float = 1e-6) -> np.ndarray:
+    """rvo_shared_mlp: the dense MLP with its norms on x [n_tok, n_embd] f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n_tok, n_embd = x.shape
+    gate, up, down = (np.ascontiguousarray(a).view(np.uint8) for a in (gate, up, down))
+    fn, pn = (np.ascontiguousarray(a, dtype=np.float32) for a in (ffn_norm, post_norm))
+    out = np.empty_like(x)
+    lib().rvo_shared_mlp(_p(gate), _p(up), _p(down), _p(fn), _p(pn), _p(x), n_tok, n_embd, ff, eps, _p(out))
     return out
 
 

@@ -143,6 +143,56 @@ void rvo_rms_norm(const float *x, float *out, const float *weight, int rows, int
     }
 }
 
+/* ops.rs:83-92 (dequant_q4_0) then ops.rs:249-266 (matmul_q4_0): each row dequantised to f32,
+ * (q - 8) * d, and each (token, row) dot the sequential sum of the rounded products, starting
+ * from -0 as Rust's f32 sum does. */
+void rvo_matmul_q4_0(const uint8_t *w, int k, const float *x, int n_in, float *y, int n_out) {
+    const int nb = k / 32;
+    float *row = (float *)malloc(sizeof(float) * (size_t)k);
+    if (!row) return;
+    for (int r = 0; r < n_out; ++r) {
+        const uint8_t *wr = w + (size_t)r * nb * 18;
+        for (int b = 0; b < nb; ++b) {
+            const float d = ld_f16(wr + 18 * b);
+            for (int j = 0; j < 16; ++j) {
+                const uint8_t q = wr[18 * b + 2 + j];
+                row[32 * b + j] = (float)((int)(q & 15) - 8) * d;
+                row[32 * b + j + 16] = (float)((int)(q >> 4) - 8) * d;
+            }
+        }
+        for (int t = 0; t < n_in; ++t) {
+            const float *xt = x + (size_t)t * k;
+            float s = -0.0f;
+            for (int i = 0; i < k; ++i) {
+                const float p = row[i] * xt[i];
+                s = s + p;
+            }
+            y[(size_t)t * n_out + r] = s;
+        }
+    }
+    free(row);
+}
+
+/* The shared dense MLP of exec.rs:438-453: cur = rms_norm(x) * ffn_norm; gate, up =
+ * matmul_q4_0(cur); mlp = gelu(gate) * up; out = rms_norm(matmul_q4_0(down, mlp)) * post_norm. */
+void rvo_shared_mlp(const uint8_t *gate, const uint8_t *up, const uint8_t *down, const float *ffn_norm,
+                    const float *post_norm, const float *x, int n_tok, int n_embd, int ff, float eps, float *out) {
+    float *cur = (float *)malloc(sizeof(float) * (size_t)n_tok * n_embd);
+    float *g = (float *)malloc(sizeof(float) * (size_t)n_tok * ff);
+    float *u = (float *)malloc(sizeof(float) * (size_t)n_tok * ff);
+    if (cur && g && u) {
+        rvo_rms_norm(x, cur, ffn_norm, n_tok, n_embd, eps, 1.0f);
+        rvo_matmul_q4_0(gate, n_embd, cur, n_tok, g, ff);
+        rvo_matmul_q4_0(up, n_embd, cur, n_tok, u, ff);
+        for (size_t i = 0; i < (size_t)n_tok * ff; ++i) g[i] = rvo_gelu(g[i]) * u[i];
+        rvo_matmul_q4_0(down, ff, g, n_tok, out, n_embd);
+        rvo_rms_norm(out, out, post_norm, n_tok, n_embd, eps, 1.0f);
+    }
+    free(cur);
+    free(g);
+    free(u);
+}
+
 /* Softmax with f32 exp and an f64 sum, scaled by (1/sum) rounded to f32 (ops.rs:170-179). */
 void rvo_softmax(float *x, int n) {
     float mx = -INFINITY;

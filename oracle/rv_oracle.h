@@ -60,6 +60,12 @@ void rvo_router_logits(const void *x, int x_dtype, const void *w, int w_dtype, c
  * mean rounded to f32, scale = 1 / sqrt(mean + eps) in f32, out = x * scale (* post when
  * post != 1) (* weight[i] when weight is given), each product rounded. out may equal x. */
 void rvo_rms_norm(const float *x, float *out, const float *weight, int rows, int width, float eps, float post);
+/* ops.rs:249-266 (matmul_q4_0): y[t][r] = dequant(W[r]) . x[t], Q4_0 rows of k, F32 x, each
+ * dot the sequential f32 sum of rounded products from -0. */
+void rvo_matmul_q4_0(const uint8_t *w, int k, const float *x, int n_in, float *y, int n_out);
+/* exec.rs:438-453: the shared dense MLP with its two norms (out [n_tok][n_embd]). */
+void rvo_shared_mlp(const uint8_t *gate, const uint8_t *up, const uint8_t *down, const float *ffn_norm,
+                    const float *post_norm, const float *x, int n_tok, int n_embd, int ff, float eps, float *out);
 /* exec.rs:507-517: softmax, top `used`, renormalise with the 2^-14 clamp.
  * logits are overwritten by probabilities. */
 void rvo_select_experts(float *logits, int n_tok, int n_experts, int used, int32_t *ids, float *weights);

@@ -10,7 +10,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "librvcuda.so")
 SOURCES = ["csrc/rvcuda.cu"]
 HEADERS = ["csrc/common.cuh", "csrc/norm.cuh", "csrc/router.cuh", "csrc/router_fast.cuh", "csrc/decode_fused.cuh", "csrc/pack.cuh",
-           "csrc/prefill.cuh", "csrc/prefill_tc.cuh", "csrc/gguf.h"]
+           "csrc/prefill.cuh", "csrc/prefill_tc.cuh", "csrc/gguf.h", "csrc/dense.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "decode_fused.cuh"
+#include "dense.cuh"
 #include "gguf.h"
 #include "norm.cuh"
 #include "pack.cuh"
@@ -961,6 +962,60 @@ int rvc_rms_norm(const float *x, float *out, const float *weight, int rows, int 
     else
         k_rms_norm<false><<<grid, NORM_WARPS * 32, 0, S(stream)>>>(x, out, weight, rows, width, eps, post);
     return launched();
+}
+
+// ------------------------------------------------------------------ shared dense MLP
+namespace {
+int q4_chains(bool gu, const void *w0, const void *w1, const float *x, float *y, int n_out, int k, int n_tok,
+              cudaStream_t st) {
+    int rc = gu ? set_smem_attr(k_q4_chains<true>, 31) : set_smem_attr(k_q4_chains<false>, 30);
+    if (rc) return rc;
+    const int rpc = gu ? DN_ROWS / 2 : DN_ROWS;
+    const dim3 grid((unsigned)((n_out + rpc - 1) / rpc), (unsigned)((n_tok + DN_T - 1) / DN_T));
+    const DenseArgs a{static_cast<const uint8_t *>(w0), static_cast<const uint8_t *>(w1), x, y, n_out, k, n_tok};
+    if (gu)
+        k_q4_chains<true><<<grid, DN_THREADS, DN_SMEM, st>>>(a);
+    else
+        k_q4_chains<false><<<grid, DN_THREADS, DN_SMEM, st>>>(a);
+    return launched();
+}
+}  // namespace
+
+int rvc_q4_mm(const void *w, const float *x, float *y, int n_out, int k, int n_in, void *stream) {
+    if (!w || !x || !y || n_out <= 0 || k <= 0 || k % QK || n_in <= 0 || n_in > 65535 * DN_T || !aligned(w, 2) ||
+        !aligned(x, 16) || !aligned(y, 4))
+        return (int)cudaErrorInvalidValue;
+    return q4_chains(false, w, nullptr, x, y, n_out, k, n_in, S(stream));
+}
+
+int rvc_geglu(const float *g, const float *u, float *out, int n, void *stream) {
+    if (!g || !u || !out || n < 0) return (int)cudaErrorInvalidValue;
+    if (n == 0) return 0;
+    k_geglu<<<(n + 255) / 256, 256, 0, S(stream)>>>(g, u, out, n);
+    return launched();
+}
+
+size_t rvc_shared_mlp_workspace_bytes(int max_tok, int n_embd, int ff) {
+    if (max_tok <= 0 || n_embd <= 0 || ff <= 0) return 0;
+    return align256((size_t)max_tok * n_embd * 4) + align256((size_t)max_tok * ff * 4);
+}
+
+int rvc_shared_mlp(const void *w_gate, const void *w_up, const void *w_down, const float *ffn_norm,
+                   const float *post_norm, const float *x, float *out, int n_tok, int n_embd, int ff, float eps,
+                   void *workspace, size_t workspace_bytes, void *stream) {
+    if (!w_gate || !w_up || !w_down || !aligned(w_gate, 2) || !aligned(w_up, 2) || !aligned(w_down, 2) || !x ||
+        !out || !workspace || !aligned(workspace, 256) || !aligned(out, 16) || n_tok <= 0 || n_embd <= 0 || ff <= 0 ||
+        n_embd % QK || ff % QK || n_tok > 65535 * DN_T)
+        return (int)cudaErrorInvalidValue;
+    if (workspace_bytes < rvc_shared_mlp_workspace_bytes(n_tok, n_embd, ff)) return RVC_ERR_WORKSPACE;
+    cudaStream_t st = S(stream);
+    float *cur = static_cast<float *>(workspace);
+    float *mlp = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + align256((size_t)n_tok * n_embd * 4));
+    int rc = rvc_rms_norm(x, cur, ffn_norm, n_tok, n_embd, eps, 1.0f, stream);         // exec.rs:440-443
+    if (!rc) rc = q4_chains(true, w_gate, w_up, cur, mlp, ff, n_embd, n_tok, st);      // :444-448
+    if (!rc) rc = q4_chains(false, w_down, nullptr, mlp, out, n_embd, ff, n_tok, st);  // :450
+    if (!rc) rc = rvc_rms_norm(out, out, post_norm, n_tok, n_embd, eps, 1.0f, stream);  // :451-453
+    return rc;
 }
 
 int rvc_status(void *workspace, void *stream) {

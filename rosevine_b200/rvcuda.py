@@ -34,6 +34,7 @@ EXPORTS = [
     "rvc_debug_gemm_block_dots", "rvc_q8_record_bytes", "rvc_ep_row_bytes", "rvc_quant_q8_rows", "rvc_ep_pack",
     "rvc_ep_workspace_bytes", "rvc_ep_experts", "rvc_ep_reduce", "rvc_prefill_gemms", "rvc_rms_norm",
     "rvc_gguf_open", "rvc_gguf_parse", "rvc_gguf_close", "rvc_gguf_tensor", "rvc_gguf_moe_layer",
+    "rvc_q4_mm", "rvc_geglu", "rvc_shared_mlp_workspace_bytes", "rvc_shared_mlp",
 ]
 ERR_GGUF = 10100  # + a reason (rvc_error_string gives the reference parser's wording)
 
@@ -121,6 +122,10 @@ def lib() -> ctypes.CDLL:
             "rvc_gguf_tensor": ([P, ctypes.c_char_p, ctypes.POINTER(I), ctypes.POINTER(I),
                                  ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(P), ctypes.POINTER(ctypes.c_uint64)], I),
             "rvc_gguf_moe_layer": ([P, I, I, I, I, ctypes.POINTER(GgufMoe)], I),
+            "rvc_q4_mm": ([P, P, P, I, I, I, P], I),
+            "rvc_geglu": ([P, P, P, I, P], I),
+            "rvc_shared_mlp_workspace_bytes": ([I, I, I], Z),
+            "rvc_shared_mlp": ([P, P, P, P, P, P, P, I, I, I, F, P, Z, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -377,6 +382,30 @@ def ep_reduce(back, n_back: int, owner_map, n_tok: int, world: int, n_embd: int,
               stream: int | None = None) -> None:
     check(lib().rvc_ep_reduce(_ptr(back, n_back * n_embd * 4), _ptr(owner_map, n_tok * world * 4), n_tok, world,
                               n_embd, _ptr(out, n_tok * n_embd * 4), stream))
+
+
+def q4_mm(w, x, y, n_out: int, k: int, n_in: int, stream: int | None = None) -> None:
+    """rvc_q4_mm: y [n_in][n_out] = W . x, W Q4_0 rows (GGUF layout), x [n_in][k] f32."""
+    check(lib().rvc_q4_mm(_ptr(w, n_out * (k // 32) * 18), _ptr(x, n_in * k * 4), _ptr(y, n_in * n_out * 4),
+                          n_out, k, n_in, stream))
+
+
+def geglu(g, u, out, n: int, stream: int | None = None) -> None:
+    check(lib().rvc_geglu(_ptr(g, 4 * n), _ptr(u, 4 * n), _ptr(out, 4 * n), n, stream))
+
+
+def shared_mlp_workspace_bytes(max_tok: int, n_embd: int, ff: int) -> int:
+    return lib().rvc_shared_mlp_workspace_bytes(max_tok, n_embd, ff)
+
+
+def shared_mlp(w_gate, w_up, w_down, ffn_norm, post_norm, x, out, n_tok: int, n_embd: int, ff: int, eps: float,
+               workspace, stream: int | None = None) -> None:
+    """rvc_shared_mlp: the layer's dense MLP with its two norms (exec.rs:438-453)."""
+    wb_gu, wb_dn = ff * (n_embd // 32) * 18, n_embd * (ff // 32) * 18
+    ws = view_of(workspace)
+    check(lib().rvc_shared_mlp(_ptr(w_gate, wb_gu), _ptr(w_up, wb_gu), _ptr(w_down, wb_dn), _ptr(ffn_norm, 4 * n_embd),
+                               _ptr(post_norm, 4 * n_embd), _ptr(x, 4 * n_tok * n_embd), _ptr(out, 4 * n_tok * n_embd),
+                               n_tok, n_embd, ff, eps, ws.ptr, ws.nbytes, stream))
 
 
 class GgufFile:
