@@ -17,7 +17,7 @@
 //
 // Build and run (on a B200):
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -o tc_probe tc_probe.cu
-//   ./tc_probe
+//   stdbuf -o0 ./tc_probe          (one JSON line per probe; about 3 s)
 // Every mbarrier wait is bounded; a wait that runs out sets a flag the host reports.
 #include <cuda_runtime.h>
 
@@ -1356,6 +1356,16 @@ int main() {
     CK(cudaFuncSetAttribute(k_ring, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     CK(cudaFuncSetAttribute(k_ring2, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     CK(cudaFuncSetAttribute(k_contend, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    CK(cudaFuncSetAttribute(k_ring3, cudaFuncAttributeMaxDynamicSharedMemorySize, 5 * 34816 + 2048));
+    // MMA issue: back to back, a commit after every MMA (style 2) or every fourth (style 3)
+    for (int st : {0, 1, 2, 3, 4}) run_issue(st, 4000, flag);
+    // tensor-memory loads alone (1, 4, 8 warps), and beside a stream of MMAs on other columns
+    for (int nw : {1, 4, 8}) run_tmem(2, 128, nw, 2000, flag);
+    for (int nw : {4, 8}) run_tmem(3, 128, nw, 2000, flag);
+    // the GEMM's skeleton factor by factor (writers only with rotating stages: flags 8 and 12
+    // without rotation do not pair the writers' stages with the MMAs' and are not run)
+    for (int f : {0, 1, 3, 5, 7, 11, 15}) run_ring3(f, 4000, flag);
+    // an MMA stream with tensor-memory or shared-memory loads beside it
     for (int mode : {0, 1, 2}) run_contend(mode, 4000, flag);
     CK(cudaFree(flag));
     return 0;
