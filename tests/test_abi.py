@@ -118,7 +118,10 @@ def test_integration_names_only_declared_symbols():
     each a thin shim over rvc_<name>) is declared in include/rvcuda.h."""
     text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
     declared = declared_symbols()
-    named = set(re.findall(r"\b(rvc_\w+)\b", text)) - {"rvc_moe_weights"}
+    header = open(os.path.join(ROOT, "include", "rvcuda.h")).read()
+    types = {a or b for a, b in re.findall(r"typedef struct \w+ (rvc_\w+);|\}\s*(rvc_\w+);", header)}
+    assert {"rvc_moe_weights", "rvc_gguf", "rvc_gguf_moe"} <= types, types
+    named = set(re.findall(r"\b(rvc_\w+)\b", text)) - types
     wrapped = {"rvc_" + n for n in re.findall(r"\bcuda::(\w+)\s*\(", text)}
     assert named, "no rvc_ names found"
     assert named <= declared, named - declared
