@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base, as an offset from the shared array (keeps shared addressing)
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    __shared__ uint64_t full[TC_STAGES], wfull[TC_STAGES], afull[TC_STAGES], empty[TC_STAGES];
+    __shared__ uint64_t full[TC_STAGES], wfull[TC_STAGES], empty[TC_STAGES];
     __shared__ uint64_t tfull[TC_TBUF], tempty[TC_TBUF], drain;
     __shared__ int epi_ok;  // the epilogue leader's wait outcome, read by all epilogue warps after bar.sync
     __shared__ uint32_t taddr_s;
@@ -406,9 +406,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
     }
     if (tid == 32) {
         for (int s = 0; s < TC_STAGES; ++s) {
-            mbar_init(&full[s], 1);
+            // a stage is ready once its copies have landed and both unpack warps are done: one
+            // barrier, so that the MMA warp, whose loop is the GEMM's critical path, waits once
+            mbar_init(&full[s], 3);                      // the copies' expect_tx arrival + the two unpack warps
             mbar_init(&wfull[s], 1);
-            mbar_init(&afull[s], 2);                     // the two unpack warps
             mbar_init(&empty[s], 1 + TC_EPI_WARPS);      // the MMAs' commit and every epilogue warp
         }
         for (int b = 0; b < TC_TBUF; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], TC_EPI_WARPS);
@@ -453,10 +454,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                     bulk_load(base + TC_OFF_DW, dws, TC_KB * TC_M * 4, &full[s]);
                 }
             }
-            // copies still in flight after an abort: wait (bounded) for the last stages issued
+            // copies still in flight after an abort: wait (bounded) for the last stages issued. The
+            // unpack warps may have stopped before arriving on those stages: arrive for them, so
+            // that only the copies' bytes are waited for (an arrival beyond a phase's count lands
+            // in the next phase, which no role uses after an abort)
             if (!ok)
                 for (int k = sc - 1; k >= 0 && k >= sc - TC_STAGES; --k) {
                     fd_mbar_wait(&wfull[k % TC_STAGES], (uint32_t)((k / TC_STAGES) & 1), nullptr);
+                    mbar_arrive(&full[k % TC_STAGES]);
+                    mbar_arrive(&full[k % TC_STAGES]);
                     fd_mbar_wait(&full[k % TC_STAGES], (uint32_t)((k / TC_STAGES) & 1), nullptr);
                 }
         }
@@ -471,9 +477,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
                 const uint32_t par = (uint32_t)((sc / TC_STAGES) & 1);
-                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status, true) &&
-                           tc_wait_warp(&afull[s], par, abort, a.status, true)))
-                    break;
+                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status, true))) break;
                 if (lane == 0) TC_TRACE(6, sc, 3);
                 tc_fence_after();
                 const uint32_t base = sbase + s * TC_STAGE_BYTES;
@@ -545,7 +549,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                 }
                 fence_proxy_async_smem();  // generic-proxy writes -> the tensor core's reads
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&afull[s]);
+                if (lane == 0) mbar_arrive(&full[s]);  // the stage's A operand is ready
                 if (tid == 64) TC_TRACE(6, sc, 2);
             }
         }
@@ -583,7 +587,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
             for (int st = 0; st < nst && ok; ++st, ++sc) {
                 const int s = sc % TC_STAGES;
                 const uint32_t par = (uint32_t)((sc / TC_STAGES) & 1);
-                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status) && tc_wait_warp(&afull[s], par, abort, a.status)))
+                if (!(ok = tc_wait_warp(&full[s], par, abort, a.status)))
                     break;
                 const uint32_t sdx = sbase + s * TC_STAGE_BYTES + TC_OFF_DX + 4 * pb;  // this warp's positions
                 const uint32_t sdw = sbase + s * TC_STAGE_BYTES + TC_OFF_DW + 4 * r;   // this row's scales
