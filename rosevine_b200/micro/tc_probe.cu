@@ -1122,6 +1122,160 @@ __global__ void __launch_bounds__(18 * 32, 1) k_contend(int mode, int blocks, Pr
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
 }
 
+// The production GEMM's synchronisation without its data movement: a producer warp that marks
+// stages ready (no copies), two warps that mark the stages' operands ready (no unpacking), the MMA
+// warp (two f16 MMAs per block into 4 tensor-memory buffers, a commit per block and per stage),
+// and 16 epilogue warps (load, hand back, optional exact scaling), over S stages of two blocks.
+// Knobs (compile time): MATH the epilogue's arithmetic; SLEEP the MMA, producer and marker warps
+// back off with __nanosleep between polls (32 ns doubling to 512 ns) as the production kernel's
+// do; EWAIT the epilogue also waits for each stage's two barriers. The figure to compare is
+// cycles per block against ring4 (the same MMAs and loads with a buffer ring only).
+__device__ __forceinline__ bool pwait(uint64_t *b, uint32_t par, bool sleep, int *flag) {
+    uint32_t ns = 32;
+    for (long long i = 0; i < (1ll << 22); ++i) {
+        if (mbar_try(b, par)) return true;
+        if (sleep) {
+            __nanosleep(ns);
+            ns = ns < 512 ? 2 * ns : 512;
+        }
+    }
+    atomicOr(flag, 1);
+    return false;
+}
+// PROTO 0: no stage protocol at all (the buffer ring alone, as ring4); 1: the MMA warp commits each
+// stage's release and the epilogue arrives on it, the producer recycles stages, but the MMA warp
+// does not wait for stages; 2: the whole protocol.
+template <bool MATH, bool SLEEP, bool EWAIT, int S, int PROTO = 2>
+__global__ void __launch_bounds__(20 * 32, 1) k_ring5(int iters, ProbeOut *out, int *flag) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    __shared__ uint64_t tfull[4], tempty[4], full[S], afull[S], empty[S], done;
+    __shared__ uint32_t taddr_s;
+    __shared__ __align__(16) float dx_s[128];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < 24576 / 4; i += blockDim.x) reinterpret_cast<uint32_t *>(smem)[i] = 0x3C003C00u;
+    for (int i = tid; i < 128; i += blockDim.x) dx_s[i] = 1.0f + i * 0.001f;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < 4; ++b) mbar_init(&tfull[b], 1), mbar_init(&tempty[b], 16);
+        for (int b = 0; b < S; ++b) mbar_init(&full[b], 1), mbar_init(&afull[b], 2), mbar_init(&empty[b], 17);
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t taddr = taddr_s;
+    const int nst = iters / 2;  // stages of two blocks
+    long long cyc = 0;
+    if (warp == 0) {  // producer: stage sc ready once its slot is free
+        if (lane == 0 && PROTO >= 1)
+            for (int sc = 0; sc < nst; ++sc) {
+                const int st = sc % S;
+                if (sc >= S && !pwait(&empty[st], (uint32_t)((sc / S - 1) & 1), SLEEP, flag)) break;
+                mbar_arrive(&full[st]);
+            }
+    } else if (warp == 2 || warp == 3) {  // operand markers: after the stage's copies
+        for (int sc = 0; sc < nst && PROTO >= 1; ++sc) {
+            const int st = sc % S;
+            if (!__all_sync(0xffffffffu, pwait(&full[st], (uint32_t)((sc / S) & 1), SLEEP, flag))) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[st]);
+        }
+    } else if (warp == 1) {
+        const uint32_t id = idesc_f16(128, 128);
+        const uint64_t da = desc_l(smem, 128 * 16, 128, 0), db = desc_l(smem + 8192, 128 * 16, 128, 0);
+        const long long c0 = clock64();
+        bool ok = true;
+        int bc = 0;
+        for (int sc = 0; sc < nst && ok; ++sc) {
+            const int st = sc % S;
+            const uint32_t par = (uint32_t)((sc / S) & 1);
+            if (PROTO >= 2)
+                ok = __all_sync(0xffffffffu, pwait(&full[st], par, SLEEP, flag)) &&
+                     __all_sync(0xffffffffu, pwait(&afull[st], par, SLEEP, flag));
+            tc_after();
+            for (int j = 0; j < 2 && ok; ++j, ++bc) {
+                const int b = bc & 3;
+                if (bc >= 4) ok = __all_sync(0xffffffffu, pwait(&tempty[b], (uint32_t)((bc / 4 - 1) & 1), SLEEP, flag));
+                tc_after();
+                const uint32_t d = taddr + (uint32_t)(b * 128);
+                mma_f16_k<false>(d, da, db, id);
+                mma_f16_k<true>(d, da + 256, db + 256, id);
+                mma_commit_elect(&tfull[b]);
+            }
+            if (PROTO >= 1) mma_commit_elect(&empty[st]);
+        }
+        mma_commit_elect(&done);
+        mbar_wait(&done, 0, flag);
+        cyc = clock64() - c0;
+    } else {
+        const int q = warp & 3, cg = (warp - 4) >> 2;
+        const uint32_t tcol = taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * cg);
+        const uint64_t nz2 = 0x8000000080000000ull;
+        const uint64_t dw2 = pack2(0.5f + lane * 0.002f, 0.5f + lane * 0.002f);
+        const uint32_t sdx = smem_u32(dx_s) + 128 * cg;
+        uint64_t acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc[m] = 0ull;
+        uint32_t x = 0;
+        bool ok = true;
+        int bc = 0;
+        for (int sc = 0; sc < nst && ok; ++sc) {
+            const int st = sc % S;
+            const uint32_t par = (uint32_t)((sc / S) & 1);
+            if (EWAIT)
+                ok = __all_sync(0xffffffffu, pwait(&full[st], par, false, flag)) &&
+                     __all_sync(0xffffffffu, pwait(&afull[st], par, false, flag));
+            for (int j = 0; j < 2 && ok; ++j, ++bc) {
+                const int b = bc & 3;
+                ok = __all_sync(0xffffffffu, ring_wait(&tfull[b], (uint32_t)((bc / 4) & 1), 0, flag));
+                tc_after();
+                uint32_t v[32];
+                ld32(tcol + (uint32_t)(b * 128), v);
+                ld_wait(v);
+                tc_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+                if (MATH) {
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        float4 d4;
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(d4.x), "=f"(d4.y), "=f"(d4.z), "=f"(d4.w) : "r"(sdx + 16 * m));
+                        const uint64_t t0 = ((uint64_t)v[4 * m + 1] << 32) | v[4 * m];
+                        const uint64_t t1 = ((uint64_t)v[4 * m + 3] << 32) | v[4 * m + 2];
+                        const uint64_t s0 = f2x_mul(dw2, pack2(d4.x, d4.y));
+                        const uint64_t s1 = f2x_mul(dw2, pack2(d4.z, d4.w));
+                        acc[2 * m] = f2x_add(acc[2 * m], f2x_fma(t0, s0, nz2));
+                        acc[2 * m + 1] = f2x_add(acc[2 * m + 1], f2x_fma(t1, s1, nz2));
+                    }
+                } else {
+                    x ^= v[0] ^ v[31];
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && PROTO >= 1) mbar_arrive(&empty[st]);
+        }
+#pragma unroll
+        for (int m = 0; m < 16; ++m) x ^= (uint32_t)acc[m];
+        if (x == 0x12345678u) out[blockIdx.x].pad = 1;
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
+    if (warp == 1 && lane == 0) {
+        out[blockIdx.x].mma_cyc = cyc;
+        out[blockIdx.x].mma_n = iters;
+    }
+}
+
 int g_sms = 148;
 
 double run_simple(void (*k)(int, long long *, int *), int iters, const char *name, double ops_per_thread_iter) {
@@ -1341,6 +1495,31 @@ void run_contend(int mode, int blocks, int *flag) {
     CK(cudaFree(out));
 }
 
+
+template <bool MATH, bool SLEEP, bool EWAIT, int S, int PROTO = 2>
+void run_ring5(int iters, int *flag) {
+    auto kern = k_ring5<MATH, SLEEP, EWAIT, S, PROTO>;
+    const int smem = 1024 + 24576;
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ProbeOut *out;
+    CK(cudaMalloc(&out, g_sms * sizeof(ProbeOut)));
+    CK(cudaMemset(out, 0, g_sms * sizeof(ProbeOut)));
+    kern<<<g_sms, 20 * 32, smem>>>(200, out, flag);
+    CK(cudaDeviceSynchronize());
+    kern<<<g_sms, 20 * 32, smem>>>(iters, out, flag);
+    CK(cudaDeviceSynchronize());
+    ProbeOut h[1024];
+    CK(cudaMemcpy(h, out, g_sms * sizeof(ProbeOut), cudaMemcpyDeviceToHost));
+    int hf = 0;
+    CK(cudaMemcpy(&hf, flag, 4, cudaMemcpyDeviceToHost));
+    double tot = 0;
+    for (int i = 0; i < g_sms; ++i) tot += (double)h[i].mma_cyc / g_sms;
+    printf("{\"probe\": \"ring5\", \"protocol\": %d, \"math\": %d, \"sleep\": %d, \"epilogue_stage_waits\": %d, "
+           "\"stages\": %d, \"cyc_per_block\": %.1f, \"timeout\": %d}\n", PROTO, (int)MATH, (int)SLEEP, (int)EWAIT, S,
+           tot / iters, hf);
+    CK(cudaFree(out));
+}
+
 }  // namespace
 
 int main() {
@@ -1367,6 +1546,16 @@ int main() {
     for (int f : {0, 1, 3, 5, 7, 11, 15}) run_ring3(f, 4000, flag);
     // an MMA stream with tensor-memory or shared-memory loads beside it
     for (int mode : {0, 1, 2}) run_contend(mode, 4000, flag);
+    // the production kernel's synchronisation, knob by knob
+    run_ring5<false, false, false, 5, 0>(4000, flag);
+    run_ring5<false, false, false, 5, 1>(4000, flag);
+    run_ring5<true, false, false, 5, 0>(4000, flag);
+    run_ring5<false, false, false, 5>(4000, flag);
+    run_ring5<false, true, false, 5>(4000, flag);
+    run_ring5<false, false, true, 5>(4000, flag);
+    run_ring5<false, true, true, 5>(4000, flag);
+    run_ring5<true, false, false, 5>(4000, flag);
+    run_ring5<true, true, true, 5>(4000, flag);
     CK(cudaFree(flag));
     return 0;
 }
