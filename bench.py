@@ -46,6 +46,12 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE layer µs/token @B=1 (HBM GB/s) and prefill tokens/s @1/2/4/8 B200"
 SWEEP = [1, 2, 4, 8, 16, 32, 64]
 PREFILL_TOK = 16384
+# --workload: the configuration the prefill step runs (configs[3] unless asked otherwise):
+#   config2  2,048 tokens, router logits plus a Zipf(1.1) per-expert bias (uneven expert groups)
+#   config4  8,192 tokens, 90% of them forced onto experts 0-7 (all held by rank 0 under
+#            expert parallelism: the adversarial hot-expert load)
+WORKLOADS = {"config3": 16384, "config2": 2048, "config4": 8192}
+WORKLOAD = "config3"
 EXPERT_BYTES = 3_345_408
 ROUTER_BYTES = 128 * 2816 * 2
 OPS_PER_TOKEN = 2 * 8 * (1408 * 2816 + 2816 * 704)  # int8 MACs x 2 of the 8 experts' gate/up and down
@@ -183,7 +189,7 @@ def cpu_prefill(budget_s: float, seed: int, threads: int | None = None) -> dict:
     256-token slices of the prefill workload for about budget_s seconds."""
     from oracle import oracle as O
     O.build()
-    weights, x = prefill_inputs(seed, 0, 1)
+    weights, x, _ = prefill_inputs(seed, 0, 1)  # the headline workload (configs[3]) only
     pool = O.Pool(threads)
     try:
         O.moe_layer(pool, x[:64], x[:64], weights["w_router"], weights["gate_up"], weights["down"])  # page in
@@ -205,13 +211,26 @@ def cpu_prefill(budget_s: float, seed: int, threads: int | None = None) -> dict:
 
 # ------------------------------------------------------------------- inputs
 def prefill_inputs(seed: int, rank: int, world: int):
-    """Weights (all experts) and this rank's shard of the prefill tokens."""
+    """Weights (all experts), this rank's shard of the prefill tokens, and its router bias (None,
+    a per-expert [128] Zipf bias, or per-token [n, 128] hot-expert rows) for the workload."""
     from rosevine_b200 import synth
     gu, dn = synth.experts(seed + 2)
     weights = {"gate_up": gu, "down": dn, "w_router": synth.router(seed + 1)}
     x = synth.tokens(PREFILL_TOK, seed + 77)
     n = PREFILL_TOK // world
-    return weights, x[rank * n:(rank + 1) * n]
+    bias = None
+    if WORKLOAD == "config2":
+        bias = synth.zipf_bias(seed + 5)
+    elif WORKLOAD == "config4":
+        bias = synth.hot_expert_bias(seed + 3, PREFILL_TOK, np.arange(8, dtype=np.int64))[rank * n:(rank + 1) * n]
+    return weights, x[rank * n:(rank + 1) * n], bias
+
+
+def bias_rows(bias, a: int, b: int):
+    """The oracle's bias arguments for tokens a .. b - 1 of the workload: (bias, bias_stride)."""
+    if bias is None:
+        return None, 0
+    return (bias, 0) if bias.ndim == 1 else (np.ascontiguousarray(bias[a:b]), bias.shape[1])
 
 
 def make_inputs(seed: int = 0):
@@ -314,9 +333,10 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
     from rosevine_b200.moe import MoeLayer, to_device_x
 
     dev = torch.device("cuda", local_rank)
-    weights, xs = prefill_inputs(args.seed, rank, world)
+    weights, xs, bias_np = prefill_inputs(args.seed, rank, world)
     n = xs.shape[0]
     x = to_device_x(xs, dev)
+    bias = None if bias_np is None else torch.from_numpy(np.ascontiguousarray(bias_np)).to(dev)
     hx = torch.from_numpy(xs.view(np.int16)).pin_memory()
     ho = torch.empty((n, 2816), dtype=torch.float32).pin_memory()
     if world == 1:
@@ -324,7 +344,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
         out = torch.empty((n, 2816), dtype=torch.float32, device=dev)
 
         def fwd():
-            return layer.forward(x, out=out)
+            return layer.forward(x, out=out, bias=bias)
         launches = 7  # k_router_chains4, k_select, k_plan, k_pf_quant, 2 x k_pf_gemm_tc, k_pf_combine
         check = layer.status
     else:
@@ -335,7 +355,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
         layer = EpMoeLayer(be, rank, world)
 
         def fwd():
-            return layer.forward(x)
+            return layer.forward(x, bias=bias)
         # k_router_chains4, k_select, k_quant_rows, k_ep_count, k_ep_pack, k_ep_meta, k_plan, k_ep_scatter,
         # 2 x k_pf_gemm_tc, k_pf_combine, k_ep_reduce (NCCL's and torch's own kernels not counted)
         launches = 12
@@ -408,11 +428,11 @@ def run_prefill(args, rank: int, world: int, local_rank: int, peaks: dict) -> di
         check()
     if world == 1:
         ids_t = torch.empty((n, 8), dtype=torch.int32, device=dev)
-        o = layer.forward(x, ids=ids_t)
+        o = layer.forward(x, ids=ids_t, bias=bias)
     else:
-        o = layer.forward(x)
+        o = layer.forward(x, bias=bias)
         ids_t = layer.last_ids
-    par = prefill_parity(args, o, ids_t, xs, weights, rank, world, dev)
+    par = prefill_parity(args, o, ids_t, xs, weights, rank, world, dev, bias_np)
     t = torch.tensor([step_ms, e2e_ms, disp_ms, comb_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -432,7 +452,7 @@ PARITY_ROWS = 32   # oracle-checked output rows per rank
 PARITY_TOL = 1e-3  # max |gpu - cpu| / max |cpu| per row (the north star's tolerance)
 
 
-def prefill_parity(args, out, ids_t, xs, weights, rank: int, world: int, dev) -> dict:
+def prefill_parity(args, out, ids_t, xs, weights, rank: int, world: int, dev, bias=None) -> dict:
     """A seeded sample of this rank's output rows against the oracle (the reference's scalar
     Q8_0 CPU path): expert ids exact, per-row relative error. Rows whose router has an exact
     tie among the top 9 probabilities would be left out and counted."""
@@ -446,8 +466,10 @@ def prefill_parity(args, out, ids_t, xs, weights, rank: int, world: int, dev) ->
     threads = max(1, (os.cpu_count() or 1) // world)
     pool = O.Pool(threads, kernel=O.KERNEL_SCALAR)
     try:
+        b = None if bias is None else (bias if bias.ndim == 1 else np.ascontiguousarray(bias[rows]))
         want, want_ids, _, lg = O.moe_layer(pool, xs[rows], xs[rows], weights["w_router"], weights["gate_up"],
-                                            weights["down"])
+                                            weights["down"], bias=b,
+                                            bias_stride=0 if b is None or b.ndim == 1 else b.shape[1])
     finally:
         pool.close()
     _, _, probs = O.select_experts(lg, 8)
@@ -496,6 +518,10 @@ def roofline(pf: dict, peaks: dict) -> dict:
     return r
 
 
+WORKLOAD_NAME = {"config3": "configs[3]", "config2": "configs[2] (Zipf(1.1) expert bias)",
+                 "config4": "configs[4] (90% of tokens on experts 0-7)"}
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     torch.cuda.set_device(local_rank)
@@ -508,8 +534,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "metric": METRIC, "value": pf["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": pf["step_ms"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": DTYPE, "data": DATA,
-        "config": {"workload": f"configs[3] at N={world}: prefill of {PREFILL_TOK} tokens through one MoE layer "
-                               f"(2816/704, 128 experts, top-8, Q4_0 experts, bf16 x), "
+        "config": {"workload": f"{WORKLOAD_NAME[WORKLOAD]} at N={world}: prefill of {PREFILL_TOK} tokens through one "
+                               f"MoE layer (2816/704, 128 experts, top-8, Q4_0 experts, bf16 x), "
                                + ("single device" if world == 1 else f"expert-parallel, {128 // world} experts "
                                   f"and {PREFILL_TOK // world} tokens per GPU, NCCL all-to-allv"),
                    "tokens_per_step": PREFILL_TOK, "l2": "inputs and intermediates larger than the 126 MB L2",
@@ -535,19 +561,22 @@ def run_reference(args, rank: int) -> dict | None:
         return None
     from oracle import oracle as O
     O.build()
-    weights, x = prefill_inputs(args.seed, 0, 1)
+    weights, x, bias = prefill_inputs(args.seed, 0, 1)
     pool = O.Pool(None)
     sl = 256
     O.moe_layer(pool, x[:64], x[:64], weights["w_router"], weights["gate_up"], weights["down"])
     for i in range(args.warmup):
         s = x[i * sl:(i + 1) * sl]
-        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"])
+        b, bs = bias_rows(bias, i * sl, (i + 1) * sl)
+        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"], bias=b, bias_stride=bs)
     steps = max(1, min(args.steps, 8))  # bounded: a few minutes of host work at most
     ts = []
     for i in range(steps):
-        s = x[(i * sl) % PREFILL_TOK:(i * sl) % PREFILL_TOK + sl]
+        a0 = (i * sl) % PREFILL_TOK
+        s = x[a0:a0 + sl]
+        b, bs = bias_rows(bias, a0, a0 + sl)
         t0 = time.perf_counter()
-        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"])
+        O.moe_layer(pool, s, s, weights["w_router"], weights["gate_up"], weights["down"], bias=b, bias_stride=bs)
         ts.append(time.perf_counter() - t0)
     threads = pool.threads
     pool.close()
@@ -556,7 +585,7 @@ def run_reference(args, rank: int) -> dict | None:
     return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": DTYPE, "data": DATA, "impl": "reference",
-            "config": {"workload": f"configs[3] prefill workload ({PREFILL_TOK} tokens) on the reference's CPU-experts "
+            "config": {"workload": f"{WORKLOAD_NAME[WORKLOAD]} prefill workload ({PREFILL_TOK} tokens) on the reference's CPU-experts "
                                    f"Q8_0 path (oracle port: the Rust toolchain is absent), {sl}-token slices",
                        "tokens_per_step": sl, "parallelism": "host threads"},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -575,7 +604,14 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
+                    help="prefill configuration (configs[3] is the headline; the others skip the decode "
+                         "sweep and the CPU baseline)")
     args = ap.parse_args()
+    global PREFILL_TOK, WORKLOAD
+    WORKLOAD, PREFILL_TOK = args.workload, WORKLOADS[args.workload]
+    if WORKLOAD != "config3":
+        args.no_decode = args.no_cpu = True
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
