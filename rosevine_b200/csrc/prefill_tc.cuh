@@ -151,22 +151,19 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// D[tmem] = A * B (ACC false) or D += A * B (ACC true), issued by one elected lane of a converged
-// warp (all lanes pass the same, warp-uniform operands). The accumulate flag is an immediate.
-template <bool ACC>
-__device__ __forceinline__ void mma_f16_elect(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc) {
-    if (ACC)
-        asm volatile(
-            "{\n\t.reg .pred e, acc;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 acc, 1, 0;\n\t"
-            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, acc;\n\t}\n" ::"r"(tmem_d),
-            "l"(da), "l"(db), "r"(idesc)
-            : "memory");
-    else
-        asm volatile(
-            "{\n\t.reg .pred e, acc;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 acc, 0, 0;\n\t"
-            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, acc;\n\t}\n" ::"r"(tmem_d),
-            "l"(da), "l"(db), "r"(idesc)
-            : "memory");
+// A block's two MMAs (D = A0 B0, then D += A1 B1) and the commit that arrives on `bar` once they
+// have completed, under one election: the fewest instructions on the MMA warp's loop, which is
+// the GEMM's critical path.
+__device__ __forceinline__ void mma_block_elect(uint32_t tmem_d, uint64_t da0, uint64_t db0, uint64_t da1, uint64_t db1,
+                                                uint32_t idesc, uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .pred e, p0, p1;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p0, 0, 0;\n\t"
+        "setp.ne.b32 p1, 1, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %5, p0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %4, %5, p1;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}\n" ::"r"(tmem_d),
+        "l"(da0), "l"(db0), "l"(da1), "l"(db1), "r"(idesc), "r"(smem_u32(bar))
+        : "memory");
 }
 // Arrive on `bar` once every tcgen05 operation issued before by this thread has completed
 // (elected lane of a converged warp).
@@ -492,9 +489,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_pf_gemm_tc(const __grid_const
                     // block j: K chunks 0, 1 then 2, 3 of the weight (A) and activation (B) operands
                     const uint32_t ab = base + TC_OFF_A + j * TC_BLK_BYTES, bb = base + TC_OFF_B + j * 64;
                     const uint32_t d = tmem + (uint32_t)(tb * TC_N);
-                    mma_f16_elect<false>(d, umma_desc(ab, 2048, 128), umma_desc_sw128(bb), idesc);
-                    mma_f16_elect<true>(d, umma_desc(ab + 4096, 2048, 128), umma_desc_sw128(bb + 32), idesc);
-                    mma_commit_elect(&tfull[tb]);
+                    mma_block_elect(d, umma_desc(ab, 2048, 128), umma_desc_sw128(bb), umma_desc(ab + 4096, 2048, 128),
+                                    umma_desc_sw128(bb + 32), idesc, &tfull[tb]);
                     if (lane == 0) TC_TRACE(5, bc, 1);
 #ifdef RVC_TC_TRACE_MMA_DONE
                     // profiling builds only: the MMA warp itself timestamps the block's completion
