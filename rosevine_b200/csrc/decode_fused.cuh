@@ -817,6 +817,50 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_route(FdArgs a) {
 // exact fallback). Publishes the plan and leaves h records for k_fd_down, whose weight tiles
 // it prefetches into L2. WIDE (batches whose x records do not all fit one buffer): each unit
 // is computed by the whole CTA (fd_gu_wide) instead of a warp per half and token pair.
+// The gate/up units [g0, g1) of CTA c for batches (k_fd_gate<..., true>), called by one whole warp.
+// A unit's time grows with its expert's tokens: each chunk of ax tokens costs a pass over the
+// unit's rows and an h phase, on top of the unit's fixed cost (its stage waits and hand-back),
+// measured at about 3 to 1. Unit weight 1 + 3 * chunks, and CTA c takes the units whose
+// cumulative start weight lies in [c W / G, (c + 1) W / G): every CTA computes the same ranges,
+// which tile [0, n_act * nbh) exactly.
+__device__ __noinline__ int2 fd_unit_range(int c, int G, int n_act, int nbh, int ax, const int32_t *p_cnt,
+                                           const int32_t *p_act) {
+    const int lane = threadIdx.x & 31;
+    constexpr int PL = FD_MAX_EXPERTS / 32;
+    int uw[PL], run = 0;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int x = lane * PL + i;
+        uw[i] = x < n_act ? 1 + 3 * ((p_cnt[p_act[x]] + ax - 1) / ax) : 0;
+        run += uw[i] * nbh;
+    }
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const long long W = __shfl_sync(0xffffffffu, incl, 31);
+    const long long t0 = (long long)c * W / G, t1 = (long long)(c + 1) * W / G;
+    // units whose start weight is below t: in expert x (start S), ceil((t - S) / u) of its nbh
+    int n0 = 0, n1 = 0;
+    long long S = incl - run;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        if (uw[i] > 0) {
+            if (t0 > S) n0 += (int)min((long long)nbh, (t0 - S + uw[i] - 1) / uw[i]);
+            if (t1 > S) n1 += (int)min((long long)nbh, (t1 - S + uw[i] - 1) / uw[i]);
+        }
+        S += (long long)uw[i] * nbh;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        n0 += __shfl_xor_sync(0xffffffffu, n0, o);
+        n1 += __shfl_xor_sync(0xffffffffu, n1, o);
+    }
+    return make_int2(n0, n1);
+}
+
 template <typename XT, typename WT, int NB8, bool WIDE>
 __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -929,9 +973,14 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     RVC_MARK(4, 3);
 
     // ------------------------------------------------------------ stage plan
-    if (tid == 0) {
+    // (expert, 32-column) units: an even split for small batches (every unit has one or two
+    // tokens), split by cost for batches (fd_unit_range)
+    if (WIDE && warp == 0) {
+        const int2 r = fd_unit_range(c, G, n_act, nbh, L.act_x, p_cnt, p_act);
+        if (lane == 0) C.n_act = n_act, C.g0 = r.x, C.n_units = r.y - r.x, C.NS = 2 * (r.y - r.x);
+    } else if (!WIDE && tid == 0) {
+        const int U = n_act * nbh;
         C.n_act = n_act;
-        const int U = n_act * nbh;  // (expert, 32-column) units
         C.g0 = c * U / G;
         C.n_units = (c + 1) * U / G - C.g0;
         C.NS = 2 * C.n_units;
@@ -1018,6 +1067,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
             if (__syncthreads_or(!ok)) goto fail;
         }
         if (u0 == 0) RVC_MARK(4, 4);
+        RVC_TRACE(5, u0, 0);
         const int x_first = (C.g0 + u0) / nbh;
         const int M = resident ? 1 : gu_chunks(x_first);
 #pragma unroll 1
@@ -1035,6 +1085,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                     cur_buf = nbuf, cur_id = id;
                 }
             }
+            RVC_TRACE(5, u0, 1);
             const uint8_t *recs = act0 + (size_t)cur_buf * L.act_bytes;
             if constexpr (WIDE) {  // one unit per wave: warps 0-7 the gate half, 8-15 the up half
                 const int e = p_act[(C.g0 + u0) / nbh], nt = min(AX, p_cnt[e] - m * AX), half = warp >> 3;
@@ -1089,6 +1140,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
             }
             }
             __syncthreads();
+            RVC_TRACE(5, u0, 2);
             int nh = 0;
 #pragma unroll 1
             for (int w = 0; w < nw; ++w) {
@@ -1118,6 +1170,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
         }
         // release the wave's slots
         __syncthreads();
+        RVC_TRACE(5, u0, 3);
 #pragma unroll 1
         for (; j_done < 2 * (u0 + nw); ++j_done)
             if (j_issued < NS) {
