@@ -315,7 +315,7 @@ def run_decode(args, local_rank: int, peaks: dict) -> dict:
     achieved = lay_bytes / (sweep_ms * 1e-3) / 1e9
     ph_gbs = sum(distinct[b] * EXPERT_BYTES for b in SWEEP) / (sum(phase.values()) * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": "decode layer (rvc_moe_forward: k_fd_route, k_fd_gate, k_fd_down up to "
-                                           "48 tokens, the prefill kernels above), algorithmic bytes and device time "
+                                           "64 tokens, the prefill kernels above), algorithmic bytes and device time "
                                            "summed over the B sweep",
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "peak_source": peaks["source"], "b1_frac": rows[0]["frac_of_hbm"],
@@ -323,7 +323,7 @@ def run_decode(args, local_rank: int, peaks: dict) -> dict:
     return {"workload": "configs[1]: batched decode sweep B in {1,2,4,8,16,32,64}, L2 flushed before every call",
             "steps": steps, "b1_us_per_token": per_b[1] * 1e3, "b1_hbm_gbs": rows[0]["hbm_gbs"],
             "sweep_tokens_per_s": sum(SWEEP) / (sweep_ms * 1e-3), "per_b": rows, "roofline": roofline,
-            "gpu_launches_per_call": {str(b): (3 if b <= 48 else 7) for b in SWEEP}}  # decode / prefill kernels
+            "gpu_launches_per_call": {str(b): (3 if b <= 64 else 7) for b in SWEEP}}  # decode / prefill kernels
 
 
 # ---------------------------------------------------------------- prefill (all N)

@@ -137,8 +137,9 @@ int rvc_moe_forward(const rvc_moe_weights *w, const void *x_router, const void *
  * returned for its tokens (rvc_ep_reduce); the exchanges between these calls are the caller's
  * (NCCL all-to-allv of rvc_ep_row_bytes-byte rows, and of n_embd f32 partials back). */
 
-/* Bytes of one Q8_0 row record of this backend: per 32-element block 32 int8 quants, then all
- * blocks' f32 scales, then all blocks' int32 quant sums (n_embd / 32 * 40 bytes). */
+/* Bytes of one Q8_0 row record of this backend: quants 0-15 of every 32-element block (16 int8
+ * each), then quants 16-31 of every block, then all blocks' f32 scales, then all blocks' int32
+ * quant sums (n_embd / 32 * 40 bytes). */
 size_t rvc_q8_record_bytes(int n_embd);
 
 /* Bytes of one sent row: a record, then `used` int32 local expert ids (-1: the slot's expert is on
@@ -195,7 +196,7 @@ int rvc_moe_forward_noalloc(const rvc_moe_weights *w, const void *x_router, cons
 
 /* Measurement hook (no counterpart in the reference): enqueue on `stream`, again, the two
  * grouped expert GEMMs (gate/up with GELU and h quantisation, then down) of the last
- * rvc_moe_forward call of more than 48 tokens enqueued with this workspace and these weights,
+ * rvc_moe_forward call of more than 64 tokens enqueued with this workspace and these weights,
  * on the plan, records and scale planes that call left in the workspace. The GEMMs rewrite the
  * same h records and y, so the layer's outputs stay as they were. Lets a caller time the
  * layer's dominant kernels alone with events on `stream`. Returns cudaErrorInvalidValue if no

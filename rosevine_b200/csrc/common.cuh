@@ -149,15 +149,24 @@ __device__ __forceinline__ int q4q8_sumi(const uint4 nib, const int4 qa, const i
 // ----------------------------------------------------------- Q8_0 row records
 // A quantised activation row (x of a token, h of a pair) as one contiguous record, so that a
 // row can be staged into shared memory with a single bulk copy:
-//   [nblk x 32 int8 quants][nblk x f32 scale (the f16 scale widened)][nblk x int32 sum of quants]
-// nblk*40 bytes, a multiple of 16 when nblk is even.
+//   [nblk x 16 int8: quants 0-15 of each block][nblk x 16 int8: quants 16-31 of each block]
+//   [nblk x f32 scale (the f16 scale widened)][nblk x int32 sum of quants]
+// nblk*40 bytes, a multiple of 16 when nblk is even. The quants' two planes put a block's halves
+// 16 bytes after the previous block's: 8 threads reading blocks b0 + 11 l (l = 0..7) of one record
+// (the batched gate/up rows of the decode kernel) hit 8 distinct 16-byte bank groups, where
+// 32-byte blocks would put them in 4.
 __host__ __device__ constexpr int q8rec_bytes(int nblk) { return nblk * 40; }
+
+// Byte offset of quant j (0..31) of block b in a record of nblk blocks.
+__host__ __device__ __forceinline__ int q8rec_q_off(int nblk, int b, int j) {
+    return (j < 16 ? b * 16 : (nblk + b) * 16) + (j & 15);
+}
 
 struct Q8Rec {
     const uint8_t *p;  // start of the record
     int nblk;
-    __device__ __forceinline__ int4 qa(int b) const { return *reinterpret_cast<const int4 *>(p + b * 32); }
-    __device__ __forceinline__ int4 qb(int b) const { return *reinterpret_cast<const int4 *>(p + b * 32 + 16); }
+    __device__ __forceinline__ int4 qa(int b) const { return *reinterpret_cast<const int4 *>(p + b * 16); }
+    __device__ __forceinline__ int4 qb(int b) const { return *reinterpret_cast<const int4 *>(p + (nblk + b) * 16); }
     __device__ __forceinline__ float d(int b) const { return reinterpret_cast<const float *>(p + nblk * 32)[b]; }
     __device__ __forceinline__ int s(int b) const { return reinterpret_cast<const int *>(p + nblk * 36)[b]; }
 };
@@ -165,7 +174,7 @@ struct Q8Rec {
 // Store block b of a record from the warp that quantised it (quant_q8_lane below).
 __device__ __forceinline__ void q8rec_store(uint8_t *rec, int nblk, int b, int lane, int8_t q, uint16_t dbits,
                                             int qsum) {
-    rec[b * 32 + lane] = (uint8_t)q;
+    rec[q8rec_q_off(nblk, b, lane)] = (uint8_t)q;
     if (lane == 0) {
         reinterpret_cast<float *>(rec + nblk * 32)[b] = __half2float(__ushort_as_half(dbits));
         reinterpret_cast<int *>(rec + nblk * 36)[b] = qsum;

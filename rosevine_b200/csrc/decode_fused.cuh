@@ -58,6 +58,11 @@ constexpr int FD_REDUNDANT_TOK = FD_GROUPS;  // up to this many tokens every CTA
 constexpr int FD_ROWS = 32;                  // packed gate/up rows per ring slot
 constexpr int FD_TB = 4;                     // tokens per router item
 constexpr int FD_SCRATCH = 16384;            // ring bytes lent to phases 1-2 (scratch below)
+// Active experts whose down tiles k_fd_gate pulls toward L2 for k_fd_down's first stages (about
+// 18 MB at the target's shapes). Prefetching every active expert's tiles at larger batches (127 MB
+// at 32 tokens) held up the gate kernel's first weight copies by ~20 us and did not stay in L2
+// beside the gate/up stream; the down kernel's own ring covers the later stages.
+constexpr int FD_L2_EXPERTS = 16;
 
 // Shared-memory plans of the three kernels, computed on the host (fd_layout), passed by value.
 struct FdLayout {
@@ -665,12 +670,14 @@ __device__ __forceinline__ int2 fd_dn_pairs(const FdCtx &C, int k, const int32_t
     return make_int2(p_off[p_act[alo]], p_off[p_act[ahi - 1]] + p_cnt[p_act[ahi - 1]]);
 }
 
-// Activation records into buffer `dst` on `bar`: with h, thread 0 copies n consecutive h
-// records from plan position p0; otherwise thread i < n copies the x record of plan position
-// p0 + i (token order[p0 + i] / used), thread 0 arriving with all n records' bytes.
-__device__ __noinline__ void fd_issue_records(uint8_t *dst, uint64_t *bar, bool h, int p0, int n, const int32_t *p_order,
-                                              int used, const uint8_t *xrec, int xrb, const uint8_t *hrec, int hrb) {
-    const int i = threadIdx.x;
+// Activation records into buffer `dst` on `bar`, by the calling threads numbered i = 0, 1, ...
+// (others pass i < 0 or beyond n): with h, thread 0 copies n consecutive h records from plan
+// position p0; otherwise thread i < n copies the x record of plan position p0 + i (token
+// order[p0 + i] / used), thread 0 arriving with all n records' bytes.
+__device__ __noinline__ void fd_issue_records(int i, uint8_t *dst, uint64_t *bar, bool h, int p0, int n,
+                                              const int32_t *p_order, int used, const uint8_t *xrec, int xrb,
+                                              const uint8_t *hrec, int hrb) {
+    if (i < 0) return;
     if (h) {
         if (i == 0) {
             mbar_arrive_expect_tx(bar, (uint32_t)n * hrb);
@@ -994,11 +1001,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     if (tid < 2 * first)
         fd_issue_gate<NB8>(C, tid >> 1, tid & 1, ring, L.slot_bytes, L.nslot, full, p_act, a.pk.gu_nib, a.pk.gu_scl,
                            a.ff);
-    // warm L2 with the down tiles k_fd_down's CTA c will read (its rows of every active expert)
+    // warm L2 with the down tiles k_fd_down's CTA c reads first (its rows of the first
+    // FD_L2_EXPERTS active experts)
     {
         int r0, rows;
         fd_rows_of(c, G, a.n_embd, L.rg, r0, rows);
-        if (rows > 0 && tid >= 32 && tid - 32 < n_act) {
+        if (rows > 0 && tid >= 32 && tid - 32 < min(n_act, FD_L2_EXPERTS)) {
             const size_t row0 = (size_t)p_act[tid - 32] * a.n_embd + r0;
             bulk_prefetch_l2(a.pk.dn_nib + row0 * nbh * 16, (uint32_t)rows * nbh * 16);
             bulk_prefetch_l2(a.pk.dn_scl + row0 * nbh, (uint32_t)rows * nbh * 2);
@@ -1010,9 +1018,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     int j_done = 0;         // stages consumed
     // chunk tags (when the records are not resident): expert slot x * 4096 + chunk m
     auto gu_chunks = [&](int x) { return (p_cnt[p_act[x]] + AX - 1) / AX; };
-    auto issue_gu = [&](int buf, int id) {  // every thread (threads i < records copy one each)
+    auto issue_gu = [&](int buf, int id, int base) {  // every thread (threads base + i copy record i)
         const int x = id >> 12, m = id & 4095, e = p_act[x];
-        fd_issue_records(act0 + (size_t)buf * L.act_bytes, &actb[buf], false, p_off[e] + m * AX,
+        fd_issue_records(tid - base, act0 + (size_t)buf * L.act_bytes, &actb[buf], false, p_off[e] + m * AX,
                          min(AX, p_cnt[e] - m * AX), p_order, used, a.xrec, xrb, nullptr, 0);
         act_pend |= 1u << buf;
     };
@@ -1033,9 +1041,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
             act_pend |= 1u;
         } else {
             const int id0 = (C.g0 / nbh) << 12;
-            issue_gu(0, id0);
+            issue_gu(0, id0, 0);
             const int id1 = after_gu(0, id0);
-            if (id1 >= 0) issue_gu(1, id1);
+            if (id1 >= 0) issue_gu(1, id1, 0);
         }
     }
     auto wait_act = [&](int b) {
@@ -1051,6 +1059,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
     // stages are in, each warp takes (unit, half, token pair) tasks, then (unit, token) tasks
     // form h = gelu(gate) * up and its Q8_0 block in the pair's plan-ordered record.
     const int W = resident ? max(1, L.nslot / 2) : 1;
+    // Copies are issued by threads of the last warp after the waits, so that their issue overlaps
+    // the other warps' work instead of holding up the barrier after it. Batches defer a released
+    // slot's refill to the next unit's start: with nslot >= 4 (two units in the ring) the stages
+    // of unit u + 1 are then issued at the start of unit u, before anyone waits for them.
+    const bool defer = WIDE && L.nslot >= 4;
+    int to_issue = 0;  // released stages whose refill is deferred
     int cur_buf = 1, cur_id = -1;
     if (resident && n_units > 0) {
         if (!wait_act(0)) goto fail;
@@ -1068,6 +1082,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
         }
         if (u0 == 0) RVC_MARK(4, 4);
         RVC_TRACE(5, u0, 0);
+        for (; to_issue > 0; --to_issue, ++j_issued)  // (defer only)
+            if (tid >= FD_THREADS - 2)
+                fd_issue_gate<NB8>(C, j_issued, tid - (FD_THREADS - 2), ring, L.slot_bytes, L.nslot, full, p_act,
+                                   a.pk.gu_nib, a.pk.gu_scl, a.ff);
         const int x_first = (C.g0 + u0) / nbh;
         const int M = resident ? 1 : gu_chunks(x_first);
 #pragma unroll 1
@@ -1076,12 +1094,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                 const int id = (x_first << 12) | m;
                 if (id != cur_id) {  // switch buffers; the one left becomes free for the tag after next
                     const int nbuf = cur_id < 0 ? 0 : cur_buf ^ 1;
-                    __syncthreads();
+                    // (the barrier in wait_act also ends every read of cur_buf's records)
+                    if (!wait_act(nbuf)) goto fail;
                     if (cur_id >= 0) {
                         const int n = after_gu(u0, id);
-                        if (n >= 0) issue_gu(cur_buf, n);
+                        if (n >= 0) issue_gu(cur_buf, n, FD_THREADS - AX);
                     }
-                    if (!wait_act(nbuf)) goto fail;
                     cur_buf = nbuf, cur_id = id;
                 }
             }
@@ -1173,7 +1191,11 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
         RVC_TRACE(5, u0, 3);
 #pragma unroll 1
         for (; j_done < 2 * (u0 + nw); ++j_done)
-            if (j_issued < NS) {
+            if (j_issued + to_issue < NS) {
+                if (defer) {
+                    ++to_issue;
+                    continue;
+                }
                 if (tid < 2)
                     fd_issue_gate<NB8>(C, j_issued, tid, ring, L.slot_bytes, L.nslot, full, p_act, a.pk.gu_nib,
                                        a.pk.gu_scl, a.ff);
@@ -1235,16 +1257,23 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
                       a.pk.dn_scl, a.n_embd, nbh);
     int j_issued = first, j_done = 0;
     unsigned act_pend = 0, act_use = 0;
+    // Copies after the first are issued by the highest threads (the tiles by the last eps, the
+    // records by the one below them), after the waits that free their buffers, so that issuing
+    // overlaps the dot products (a stage's items go to the lowest threads first) instead of
+    // holding up a barrier. A released slot is refilled at the next stage's start: with two or
+    // more slots, stage k + 1 has been issued before anyone waits for it.
+    const int rec_thr = FD_THREADS - 1 - C.eps, tile_thr = FD_THREADS - C.eps;
+    int to_issue = 0;
     // h-record tags: down stage k * 4096 + chunk m, each its own load
     auto dn_chunks = [&](int k) {
         const int2 q = fd_dn_pairs(C, k, p_act, p_off, p_cnt);
         return (q.y - q.x + AH - 1) / AH;
     };
-    auto issue_dn = [&](int buf, int id) {  // (thread 0 copies)
+    auto issue_dn = [&](int buf, int id, int thr) {  // (thread thr copies)
         const int k = id >> 12, m = id & 4095;
         const int2 q = fd_dn_pairs(C, k, p_act, p_off, p_cnt);
         const int s0 = q.x + m * AH;
-        fd_issue_records(act0 + (size_t)buf * L.d_act_bytes, &actb[buf], true, s0, min(AH, q.y - s0), nullptr, used,
+        fd_issue_records(tid - thr, act0 + (size_t)buf * L.d_act_bytes, &actb[buf], true, s0, min(AH, q.y - s0), nullptr, used,
                          nullptr, 0, a.hrec, hrb);
         act_pend |= 1u << buf;
     };
@@ -1255,15 +1284,21 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
     };
     int cur_buf = 1, cur_id = -1;
     if (NS > 0) {
-        issue_dn(0, 0);
+        issue_dn(0, 0, rec_thr);
         const int id1 = next_dn(0);
-        if (id1 >= 0) issue_dn(1, id1);
+        if (id1 >= 0) issue_dn(1, id1, rec_thr);
     }
 #pragma unroll 1
     for (int k = 0; k < NS; ++k) {
         const int alo = k * C.eps, ahi = min(C.n_act, alo + C.eps);
         const int2 qr = fd_dn_pairs(C, k, p_act, p_off, p_cnt);
+        RVC_TRACE(6, k, 0);
         if (__syncthreads_or(!fd_mbar_wait(&full[k % L.d_nslot], (uint32_t)(k / L.d_nslot) & 1u, a.status))) goto fail;
+        RVC_TRACE(6, k, 1);
+        for (; to_issue > 0; --to_issue, ++j_issued)
+            if (tid >= tile_thr)
+                fd_issue_down(C, j_issued, tid - tile_thr, ring, L.d_slot_bytes, L.d_nslot, full, p_act, a.pk.dn_nib,
+                              a.pk.dn_scl, a.n_embd, nbh);
         {
             const uint8_t *slot = ring + (size_t)(k % L.d_nslot) * L.d_slot_bytes;
             const int M = (qr.y - qr.x + AH - 1) / AH;
@@ -1271,18 +1306,18 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
             for (int m = 0; m < M; ++m) {
                 const int id = (k << 12) | m;
                 const int nbuf = cur_buf ^ 1;  // every chunk is a new tag
-                __syncthreads();
-                if (cur_id >= 0) {
-                    const int n = next_dn(id);
-                    if (n >= 0) issue_dn(cur_buf, n);
-                }
-                {
+                {  // (the barrier also ends every read of cur_buf's records)
                     const bool ok = fd_mbar_wait(&actb[nbuf], (act_use >> nbuf) & 1u, a.status);
                     act_use ^= 1u << nbuf;
                     act_pend &= ~(1u << nbuf);
                     if (__syncthreads_or(!ok)) goto fail;
                 }
+                if (cur_id >= 0) {
+                    const int n = next_dn(id);
+                    if (n >= 0) issue_dn(cur_buf, n, rec_thr);
+                }
                 cur_buf = nbuf, cur_id = id;
+                RVC_TRACE(6, k, 2);
                 const uint8_t *recs = act0 + (size_t)cur_buf * L.d_act_bytes;
                 const int s0 = qr.x + m * AH, np = min(AH, qr.y - s0);
 #pragma unroll 1
@@ -1301,14 +1336,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
                 }
             }
         }
-        __syncthreads();  // release the slot
+        __syncthreads();  // release the slot (refilled at the next stage's start)
+        RVC_TRACE(6, k, 3);
         j_done = k + 1;
-        if (j_issued < NS) {
-            if (tid < C.eps)
-                fd_issue_down(C, j_issued, tid, ring, L.d_slot_bytes, L.d_nslot, full, p_act, a.pk.dn_nib, a.pk.dn_scl,
-                              a.n_embd, nbh);
-            ++j_issued;
-        }
+        if (j_issued + to_issue < NS) ++to_issue;
     }
     // slot-order combine (exec.rs:626-638): o = (y*ds)*w for j = 0, then o = o + (y*ds)*w
 #pragma unroll 1

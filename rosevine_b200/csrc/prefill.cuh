@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(256) k_ep_scatter(const uint8_t *__restrict__ 
     for (long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += (long long)gridDim.x * 8) {
         const int r = (int)(i / nb), b = (int)(i - (long long)r * nb);
         const uint8_t *src = rows + (size_t)r * rb;
-        const uint16_t qh = __half_as_ushort(__int2half_rn((int)(int8_t)src[b * 32 + lane]));
+        const uint16_t qh = __half_as_ushort(__int2half_rn((int)(int8_t)src[q8rec_q_off(nb, b, lane)]));
         const float d = reinterpret_cast<const float *>(src + nb * 32)[b];
         for (int j = 0; j < used; ++j) {
             const int p = r * used + j;

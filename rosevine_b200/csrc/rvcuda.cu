@@ -77,9 +77,9 @@ PackedView packed_view(const rvc_moe_weights *w) {
 }
 
 // Batches above PF_MIN_TOK tokens take the prefill kernels (grouped GEMMs), smaller ones the
-// decode kernels (measured on B200, L2 flushed before each call, layer us decode / prefill
-// kernels: 24 tokens 434 / 744, 32 tokens 596 / 853, 48 tokens 821 / 927, 64 tokens 967 / 934).
-constexpr int PF_MIN_TOK = 48;
+// decode kernels (measured on B200, CUDA graphs, L2 flushed before each call, layer us decode /
+// prefill kernels: 32 tokens 389 / 388, 48 tokens 502 / 500, 64 tokens 602 / 865).
+constexpr int PF_MIN_TOK = 64;
 
 // Workspace carve-up for calls of up to max_tok tokens.
 struct Workspace {

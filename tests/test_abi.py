@@ -51,14 +51,12 @@ def test_host_size_queries(lib):
 
 def test_noalloc_scratch_holds_the_decode_layout_at_the_target_shapes(lib):
     # rvc_moe_forward_noalloc runs the decode kernels (up to 64 tokens) on a fixed
-    # RVC_NOALLOC_SCRATCH_BYTES array. A workspace for 48 tokens, the largest call that
-    # rvc_moe_forward also gives the decode kernels, has the decode layout alone; it grows
-    # linearly with the tokens, and extended to 64 tokens it still fits the array.
+    # RVC_NOALLOC_SCRATCH_BYTES array. A workspace for 64 tokens, the largest call that
+    # rvc_moe_forward also gives the decode kernels, has the decode layout alone and fits it.
     import rosevine_b200.rvcuda as rc
     dec32 = rc.workspace_bytes(32, 2816, 704, 128, 8)
-    dec48 = rc.workspace_bytes(48, 2816, 704, 128, 8)
-    per_tok = (dec48 - dec32) / 16
-    assert 0 < per_tok and dec48 + 16 * per_tok < rc.NOALLOC_SCRATCH_BYTES, (dec48, per_tok)
+    dec64 = rc.workspace_bytes(64, 2816, 704, 128, 8)
+    assert 0 < dec32 < dec64 < rc.NOALLOC_SCRATCH_BYTES, (dec32, dec64)
 
 
 def test_error_strings(lib):

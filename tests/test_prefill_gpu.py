@@ -1,4 +1,4 @@
-"""GPU parity of the prefill path (batches above 48 tokens: the grouped expert GEMMs).
+"""GPU parity of the prefill path (batches above 64 tokens: the grouped expert GEMMs).
 
 The grouped GEMM (k_pf_gemm_tc) forms each 32-column block's integer dot on the tensor cores
 (tcgen05.mma into tensor memory, the integer operands held exactly as f16, f32 accumulation exact
