@@ -63,6 +63,7 @@ constexpr int FD_SCRATCH = 16384;            // ring bytes lent to phases 1-2 (s
 // at 32 tokens) held up the gate kernel's first weight copies by ~20 us and did not stay in L2
 // beside the gate/up stream; the down kernel's own ring covers the later stages.
 constexpr int FD_L2_EXPERTS = 16;
+constexpr int FD_HB = FD_MAX_SLOTS / 2;  // token chunks whose dots k_fd_gate<..., true> holds for one h phase
 
 // Shared-memory plans of the three kernels, computed on the host (fd_layout), passed by value.
 struct FdLayout {
@@ -1082,10 +1083,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
         }
         if (u0 == 0) RVC_MARK(4, 4);
         RVC_TRACE(5, u0, 0);
-        for (; to_issue > 0; --to_issue, ++j_issued)  // (defer only)
-            if (tid >= FD_THREADS - 2)
-                fd_issue_gate<NB8>(C, j_issued, tid - (FD_THREADS - 2), ring, L.slot_bytes, L.nslot, full, p_act,
-                                   a.pk.gu_nib, a.pk.gu_scl, a.ff);
         const int x_first = (C.g0 + u0) / nbh;
         const int M = resident ? 1 : gu_chunks(x_first);
 #pragma unroll 1
@@ -1103,6 +1100,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                     cur_buf = nbuf, cur_id = id;
                 }
             }
+            // (defer only) refill the slots the previous unit released; placed after the record
+            // switch's barrier so that no barrier waits for the issuing threads
+            for (; to_issue > 0; --to_issue, ++j_issued)
+                if (tid >= FD_THREADS - 2)
+                    fd_issue_gate<NB8>(C, j_issued, tid - (FD_THREADS - 2), ring, L.slot_bytes, L.nslot, full, p_act,
+                                       a.pk.gu_nib, a.pk.gu_scl, a.ff);
             RVC_TRACE(5, u0, 1);
             const uint8_t *recs = act0 + (size_t)cur_buf * L.act_bytes;
             if constexpr (WIDE) {  // one unit per wave: warps 0-7 the gate half, 8-15 the up half
@@ -1113,8 +1116,8 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                     const bool two = i + 1 < nt;
                     const float2 acc =
                         fd_gu_wide<NB8>(slot, recs + (size_t)i * xrb, recs + (size_t)(two ? i + 1 : i) * xrb, two);
-                    if ((lane & 7) == 0) {
-                        float *dst = sgu + ((size_t)i * 2 + half) * 32 + (warp & 7) * 4 + (lane >> 3);
+                    if ((lane & 7) == 0) {  // token slot (m % FD_HB) * AX + i of the h phase's batch
+                        float *dst = sgu + ((size_t)((m % FD_HB) * AX + i) * 2 + half) * 32 + (warp & 7) * 4 + (lane >> 3);
                         dst[0] = acc.x;
                         if (two) dst[64] = acc.y;
                     }
@@ -1157,31 +1160,43 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_gate(FdArgs a) {
                 fd_gu_split<NB8>(slot, r0p, r1p, two, active, &s_hand[0][0][0], dst);
             }
             }
+            // h = gelu(gate) * up and its Q8_0 block per (unit, token): after each chunk, or for
+            // batches after every FD_HB chunks of the unit and its last one (their dots wait in sgu's
+            // FD_HB * AX token slots; the next chunk's record switch is a barrier, and it writes
+            // other slots)
+            int hm0 = m, nh = 0;
+            if constexpr (WIDE) {
+                if (m % FD_HB != FD_HB - 1 && m != M - 1) continue;
+                hm0 = m - m % FD_HB;
+                nh = min(p_cnt[p_act[x_first]], (m + 1) * AX) - hm0 * AX;
+            } else {
+#pragma unroll 1
+                for (int w = 0; w < nw; ++w) {
+                    const int e = p_act[(C.g0 + u0 + w) / nbh];
+                    nh += resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
+                }
+            }
             __syncthreads();
             RVC_TRACE(5, u0, 2);
-            int nh = 0;
-#pragma unroll 1
-            for (int w = 0; w < nw; ++w) {
-                const int e = p_act[(C.g0 + u0 + w) / nbh];
-                nh += resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
-            }
             const int hrb = q8rec_bytes(nbh);
 #pragma unroll 1
             for (int task = warp; task < nh; task += FD_WARPS) {
-                int w = 0, i = task, e = 0;
+                int w = 0, i = task, e = p_act[x_first];  // batches: token i of chunks hm0.. (slot i)
+                if constexpr (!WIDE) {
 #pragma unroll 1
-                for (;; ++w) {
-                    e = p_act[(C.g0 + u0 + w) / nbh];
-                    const int nt = resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
-                    if (i < nt) break;
-                    i -= nt;
+                    for (;; ++w) {
+                        e = p_act[(C.g0 + u0 + w) / nbh];
+                        const int nt = resident ? p_cnt[e] : min(AX, p_cnt[e] - m * AX);
+                        if (i < nt) break;
+                        i -= nt;
+                    }
                 }
                 const float *g = sgu + ((size_t)(w * AX + i) * 2) * 32;
                 const float hv = __fmul_rn(gelu_tanh(g[lane]), g[32 + lane]);
                 uint16_t dbits;
                 int qsum;
                 const int8_t qv = quant_q8_lane(hv, &dbits, &qsum);
-                q8rec_store(a.hrec + (size_t)(p_off[e] + m * AX + i) * hrb, nbh, (C.g0 + u0 + w) % nbh, lane, qv,
+                q8rec_store(a.hrec + (size_t)(p_off[e] + hm0 * AX + i) * hrb, nbh, (C.g0 + u0 + w) % nbh, lane, qv,
                             dbits, qsum);
             }
             __syncthreads();
@@ -1295,10 +1310,6 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
         RVC_TRACE(6, k, 0);
         if (__syncthreads_or(!fd_mbar_wait(&full[k % L.d_nslot], (uint32_t)(k / L.d_nslot) & 1u, a.status))) goto fail;
         RVC_TRACE(6, k, 1);
-        for (; to_issue > 0; --to_issue, ++j_issued)
-            if (tid >= tile_thr)
-                fd_issue_down(C, j_issued, tid - tile_thr, ring, L.d_slot_bytes, L.d_nslot, full, p_act, a.pk.dn_nib,
-                              a.pk.dn_scl, a.n_embd, nbh);
         {
             const uint8_t *slot = ring + (size_t)(k % L.d_nslot) * L.d_slot_bytes;
             const int M = (qr.y - qr.x + AH - 1) / AH;
@@ -1316,6 +1327,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) k_fd_down(FdArgs a) {
                     const int n = next_dn(id);
                     if (n >= 0) issue_dn(cur_buf, n, rec_thr);
                 }
+                // refill the slot the previous stage released (after the barrier above, so that
+                // no barrier waits for the issuing threads)
+                for (; to_issue > 0; --to_issue, ++j_issued)
+                    if (tid >= tile_thr)
+                        fd_issue_down(C, j_issued, tid - tile_thr, ring, L.d_slot_bytes, L.d_nslot, full, p_act,
+                                      a.pk.dn_nib, a.pk.dn_scl, a.n_embd, nbh);
                 cur_buf = nbuf, cur_id = id;
                 RVC_TRACE(6, k, 2);
                 const uint8_t *recs = act0 + (size_t)cur_buf * L.d_act_bytes;
