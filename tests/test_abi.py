@@ -104,6 +104,20 @@ def test_workspace_too_small_is_rejected(lib):
                                None) == rc.ERR_WORKSPACE
 
 
+def test_noalloc_scratch_refusals_on_the_host(lib):
+    """rvc_moe_forward_noalloc refuses, before any device work, a call of at most 64 tokens whose
+    decode layout exceeds its fixed array (n_embd 8192, ff 4096: the down partials alone take
+    16 MB) and a call of more than 64 tokens at the target's shapes."""
+    p = ctypes.c_void_p(4096)  # aligned, never dereferenced
+    assert rc.workspace_bytes(64, 8192, 4096, 128, 8) > rc.NOALLOC_SCRATCH_BYTES
+    wide = rc.MoeWeights(8192, 4096, 128, 8, rc.BF16, 4096, 4096, None)
+    assert lib.rvc_moe_forward_noalloc(ctypes.byref(wide), p, p, rc.BF16, None, 0, 64, p, None, None,
+                                       None) == rc.ERR_WORKSPACE
+    target = rc.MoeWeights(2816, 704, 128, 8, rc.BF16, 4096, 4096, None)
+    assert lib.rvc_moe_forward_noalloc(ctypes.byref(target), p, p, rc.BF16, None, 0, 65, p, None, None,
+                                       None) == rc.ERR_WORKSPACE
+
+
 def test_checked_views_refuse_out_of_range():
     v = rc.View(1 << 20, 100)
     assert v.need(100) == 1 << 20
