@@ -28,10 +28,11 @@
 //   3. tokens that could not be certified get the exact sequential chains and an exact
 //      selection (rare: a few percent of tokens); every CTA builds the stable (expert, pair)
 //      plan of MoePlan::new in shared memory.
-//   4. gate/up: the (expert, 32-column) units of all active experts are split evenly over the
-//      CTAs. Weight rows stream through a ring of shared-memory slots filled by 1-D TMA bulk
-//      copies; token records sit beside them; h = gelu(gate)*up is quantised to Q8_0 records.
-//      The CTAs also pull this call's down-projection tiles toward L2.
+//   4. gate/up: the (expert, 32-column) units of all active experts are split over the CTAs
+//      (evenly for one or two tokens, by cost for batches: fd_unit_range). Weight rows stream
+//      through a ring of shared-memory slots filled by 1-D TMA bulk copies; token records sit
+//      beside them; h = gelu(gate)*up is quantised to Q8_0 records. The CTAs also pull the down
+//      tiles of the first FD_L2_EXPERTS active experts toward L2.
 //  k_fd_down
 //   5. down + combine: each CTA owns a range of output rows for every pair, computes
 //      y = W_down[rows] . h for all pairs from tiles streamed through its ring and combines the
